@@ -1,0 +1,182 @@
+/*
+ * b200_edsl.h — C ABI of libb200edsl.so, the B200 (sm_100a) implementation of
+ * ml-edsl's dense-layer hot path: linalg.matmul and relu(X @ W + b).
+ *
+ * All entry points are plain C: pointers, sizes and strides in elements, no
+ * C++ or torch types. They never throw. Functions returning int return 0
+ * (B200_OK) on success or one of the B200_ERR_* codes; the message of the
+ * last failure on the calling thread is b200_last_error().
+ *
+ * Three families:
+ *   1. memref-descriptor entry points (b200_memref_*): the exact flattened
+ *      signature ml-edsl's JIT'd functions have, so the reference's ctypes
+ *      call path (reference: mlir_edsl/backend.py:70-102 builds the
+ *      descriptors, :184-191 appends the output descriptor last and calls
+ *      ctypes.CFUNCTYPE(None, *types)(ptr)) can call them unchanged. Host
+ *      buffers; synchronous; void return — read b200_last_status().
+ *   2. host-pointer entry points (*_host): host buffers in and out,
+ *      host<->device copies pipelined with compute inside the call, rows
+ *      sharded over `ndev` GPUs. Replaces the reference's GPU executor path
+ *      (reference: cpp/src/MLIRCompiler.cpp:352-461 executeGPUFunction).
+ *   3. device-pointer entry points: device buffers, asynchronous on the given
+ *      cudaStream_t (passed as void*, NULL = legacy default stream).
+ *
+ * Element order is row-major. ld* arguments are row pitches in elements.
+ * Activation codes: B200_ACT_NONE, B200_ACT_RELU (arith.maximumf(x, 0):
+ * NaN propagates, -0 becomes +0), B200_ACT_LEAKY_RELU (maximumf(x,0) +
+ * alpha*minimumf(x,0)) — reference: cpp/src/builders/LinalgBuilder.cpp:207-225.
+ */
+#ifndef B200_EDSL_H
+#define B200_EDSL_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200_OK 0
+#define B200_ERR_INVALID_ARG 1
+#define B200_ERR_CUDA 2
+#define B200_ERR_DRIVER 3
+#define B200_ERR_NO_DEVICE 4
+#define B200_ERR_DEVICE_TIMEOUT 5
+#define B200_ERR_OUT_OF_MEMORY 6
+#define B200_ERR_TOO_LARGE 7
+
+#define B200_ACT_NONE 0
+#define B200_ACT_RELU 1
+#define B200_ACT_LEAKY_RELU 2
+
+/* ---------------------------------------------------------------- runtime */
+
+/* Library version string. */
+const char* b200_version(void);
+
+/* Message of the last failing call on this thread ("" if none). Replaces the
+ * reference's std::runtime_error / checkCU messages
+ * (reference: cpp/src/MLIRExecutor.cpp:160-167). */
+const char* b200_last_error(void);
+
+/* Status code of the last call on this thread; the only error channel of the
+ * void b200_memref_* entry points. */
+int b200_last_status(void);
+
+/* Number of CUDA devices visible (0 without a GPU or driver). */
+int b200_device_count(void);
+
+/* Number of kernels this library has launched in this process. */
+long long b200_launch_count(void);
+
+/* Default device count used by the b200_memref_* entry points (1 initially;
+ * the B200_DEVICES environment variable overrides the initial value). */
+int b200_set_default_devices(int ndev);
+int b200_get_default_devices(void);
+
+/* Frees every device buffer and stream the runtime caches. */
+int b200_release(void);
+
+/* ------------------------------------------------- device-pointer entry points */
+
+/* Y = act(X @ W + b) in f32 with 3xTF32 tensor-core arithmetic.
+ * X[M,K] (pitch ldx), W[K,N] (pitch ldw), b[N] or NULL, Y[M,N] (pitch ldy).
+ * Scratch for the tf32 hi/lo operand split comes from a buffer the runtime
+ * caches per (device, stream).
+ * Replaces: linalg.fill+matmul (reference: cpp/src/builders/LinalgBuilder.cpp:106-139),
+ * bias generic (:301-339), activation generic (:180-239). */
+int b200_dense_f32(const float* X, int64_t ldx, const float* W, int64_t ldw, const float* b,
+                   float* Y, int64_t ldy, int64_t M, int64_t N, int64_t K, int act, float alpha,
+                   void* stream);
+
+/* Same as b200_dense_f32 with caller-provided scratch of at least
+ * b200_dense_f32_workspace_bytes(M, N, K) bytes (256-byte aligned). */
+int64_t b200_dense_f32_workspace_bytes(int64_t M, int64_t N, int64_t K);
+int b200_dense_f32_ws(const float* X, int64_t ldx, const float* W, int64_t ldw, const float* b,
+                      float* Y, int64_t ldy, int64_t M, int64_t N, int64_t K, int act,
+                      float alpha, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* C = A @ B (+ bias) in i32, wrapping modulo 2^32 (arith.muli/addi).
+ * Replaces: linalg.matmul on i32 (reference: cpp/src/builders/LinalgBuilder.cpp:106-139). */
+int b200_matmul_i32(const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb,
+                    const int32_t* bias, int32_t* C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                    void* stream);
+
+/* Y = act(X + b) (b may be NULL). Replaces the unfused bias_add / relu /
+ * leaky_relu generics (reference: cpp/src/builders/LinalgBuilder.cpp:180-239,301-339). */
+int b200_bias_act_f32(const float* X, int64_t ldx, const float* b, float* Y, int64_t ldy,
+                      int64_t M, int64_t N, int act, float alpha, void* stream);
+
+/* Y[i] = act(X[i]) over `count` contiguous elements (any rank). */
+int b200_act_f32(const float* X, float* Y, int64_t count, int act, float alpha, void* stream);
+
+/* Y = X + b in i32 (wrapping). */
+int b200_bias_add_i32(const int32_t* X, int64_t ldx, const int32_t* b, int32_t* Y, int64_t ldy,
+                      int64_t M, int64_t N, void* stream);
+
+/* Synchronizes `stream` and returns B200_ERR_DEVICE_TIMEOUT if a kernel of
+ * this library gave up a bounded wait since the last check, else B200_OK or
+ * B200_ERR_CUDA. */
+int b200_stream_sync(void* stream);
+
+/* --------------------------------------------------- host-pointer entry points */
+
+/* Host buffers; synchronous. Rows of X/Y are sharded over `ndev` devices
+ * (0 = default device count); W and b are replicated. Within a device the
+ * rows are processed in slabs so host->device copies, compute and
+ * device->host copies overlap. */
+int b200_dense_f32_host(const float* X, int64_t ldx, const float* W, int64_t ldw, const float* b,
+                        float* Y, int64_t ldy, int64_t M, int64_t N, int64_t K, int act,
+                        float alpha, int ndev);
+
+int b200_matmul_i32_host(const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb,
+                         const int32_t* bias, int32_t* C, int64_t ldc, int64_t M, int64_t N,
+                         int64_t K, int ndev);
+
+int b200_bias_act_f32_host(const float* X, int64_t ldx, const float* b, float* Y, int64_t ldy,
+                           int64_t M, int64_t N, int act, float alpha);
+
+int b200_bias_add_i32_host(const int32_t* X, int64_t ldx, const int32_t* b, int32_t* Y,
+                           int64_t ldy, int64_t M, int64_t N);
+
+int b200_act_f32_host(const float* X, float* Y, int64_t count, int act, float alpha);
+
+/* ------------------------------------------------- memref-descriptor entry points
+ * A rank-2 memref is passed as 7 arguments
+ *   (void* allocated, void* aligned, int64 offset, int64 size0, int64 size1,
+ *    int64 stride0, int64 stride1)
+ * and a rank-1 memref as 5: (allocated, aligned, offset, size0, stride0).
+ * The output memref comes last and must be fully allocated by the caller
+ * (reference: mlir_edsl/backend.py:37-63 _make_output_descriptor). The
+ * innermost stride must be 1. Rows are sharded over b200_get_default_devices().
+ */
+#define B200_MEMREF2(n) \
+  void *n##_alloc, void *n##_aligned, int64_t n##_off, int64_t n##_s0, int64_t n##_s1, \
+      int64_t n##_st0, int64_t n##_st1
+#define B200_MEMREF1(n) \
+  void *n##_alloc, void *n##_aligned, int64_t n##_off, int64_t n##_s0, int64_t n##_st0
+
+/* C = A @ B, f32 (21 arguments). */
+void b200_memref_matmul_f32(B200_MEMREF2(A), B200_MEMREF2(B), B200_MEMREF2(C));
+/* C = relu(A @ B), f32. */
+void b200_memref_matmul_relu_f32(B200_MEMREF2(A), B200_MEMREF2(B), B200_MEMREF2(C));
+/* Y = X @ W + b, f32 (26 arguments). */
+void b200_memref_dense_f32(B200_MEMREF2(X), B200_MEMREF2(W), B200_MEMREF1(b), B200_MEMREF2(Y));
+/* Y = relu(X @ W + b), f32 (26 arguments). */
+void b200_memref_dense_relu_f32(B200_MEMREF2(X), B200_MEMREF2(W), B200_MEMREF1(b),
+                                B200_MEMREF2(Y));
+/* C = A @ B, i32 wrapping. */
+void b200_memref_matmul_i32(B200_MEMREF2(A), B200_MEMREF2(B), B200_MEMREF2(C));
+/* Y = X @ W + b, i32 wrapping. */
+void b200_memref_dense_i32(B200_MEMREF2(X), B200_MEMREF2(W), B200_MEMREF1(b), B200_MEMREF2(Y));
+/* Y = X + b, f32 (reference library_call "bias_add"). */
+void b200_memref_bias_add_f32(B200_MEMREF2(X), B200_MEMREF1(b), B200_MEMREF2(Y));
+/* Y = relu(X + b), f32 (the fused bias_add+relu generic). */
+void b200_memref_bias_relu_f32(B200_MEMREF2(X), B200_MEMREF1(b), B200_MEMREF2(Y));
+/* Y = relu(X), f32 rank 2 (reference library_call "relu"). */
+void b200_memref_relu_f32(B200_MEMREF2(X), B200_MEMREF2(Y));
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200_EDSL_H */

@@ -1,0 +1,442 @@
+// f32 GEMM with fused bias + activation epilogue on the sm_100a tensor cores.
+//
+//   Y[M,N] = act( sum_k X[m,k] * W[k,n]  (+ b[n]) )
+//
+// This is the B200 implementation of the reference's
+//   linalg.fill(0) -> linalg.matmul -> linalg.generic{bias_add} -> linalg.generic{relu}
+// chain (reference: cpp/src/builders/LinalgBuilder.cpp:106-139 matmul with
+// zero init, :301-339 bias broadcast generic, :180-239 relu/leaky_relu
+// generic; fused into one pass by linalg-fuse-elementwise-ops,
+// cpp/src/MLIRLowering.cpp:355).
+//
+// Precision: "3xTF32". Each f32 operand x is split into two tf32-exact parts
+// x = hi + lo (hi = x with the low 13 mantissa bits cleared, lo = the
+// remainder truncated the same way). The tensor core then accumulates
+// hi*hi + hi*lo + lo*hi in f32 (the lo*lo term is below f32 resolution).
+// The split runs in two HBM-bound pre-pass kernels that also
+//   * transpose W to K-major (both UMMA operands are K-major), and
+//   * pad the row pitch to a multiple of 4 floats (TMA needs 16-byte strides),
+// which is how ragged shapes such as K=1001 reach the TMA path.
+//
+// Accumulation: the tensor core adds into its f32 accumulator with
+// round-toward-zero, so a single TMEM accumulator over all of K drifts
+// linearly in K (measured 3.3e-3 at K=4096 for |x| <= 1, against ~1e-5 for
+// round-to-nearest). The kernel therefore accumulates each 128-wide slice of
+// K in TMEM ("chunk") and promotes it into f32 registers with ordinary
+// round-to-nearest adds; two TMEM chunk buffers let the MMAs of chunk c+1 run
+// while the epilogue warps drain chunk c.
+//
+// Main kernel (one 128 x 256 output tile per CTA, 320 threads):
+//   warp 0      TMA producer: 4 tiles (A_hi, A_lo, B_hi, B_lo) per k-block
+//               into a 2-stage shared-memory ring (96 KB per stage).
+//   warp 1      allocates 512 TMEM columns (2 chunk buffers); lane 0 issues 3
+//               tcgen05.mma per 8-wide k-step and frees ring stages and chunk
+//               buffers with tcgen05.commit.
+//   warps 2-9   epilogue: each thread owns one row x 128 columns of the tile
+//               in registers, adds every chunk (tcgen05.ld), then applies
+//               bias and activation (arith.maximumf semantics: NaN
+//               propagates, -0 -> +0) and stores.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <algorithm>
+#include <cstdint>
+#include "ptx.cuh"
+#include "kernels.h"
+
+namespace b200 {
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBK = 32;  // 32 floats = 128 B rows = one SWIZZLE_128B atom row
+constexpr int kStages = 2;
+constexpr int kATileBytes = kBM * kBK * 4;                      // 16 KB
+constexpr int kBTileBytes = kBN * kBK * 4;                      // 32 KB
+constexpr int kStageBytes = 2 * kATileBytes + 2 * kBTileBytes;  // 96 KB
+constexpr int kChunkKB = 4;   // k-blocks (K = 128) per TMEM partial-sum chunk
+constexpr int kEpiWarps = 8;  // 2 warps per TMEM lane quarter, one per column half
+constexpr int kTmemCols = 2 * kBN;  // two chunk accumulators of 128 x 256 f32
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kGroupM = 16;  // tile raster: 16 M-tiles share each N sweep
+
+// Shared memory: [ring stages][barriers/flags][bias tile], base aligned to 1 KB.
+constexpr int kBarOffset = kStages * kStageBytes;
+constexpr int kBiasOffset = kBarOffset + 256;  // 2*S + 4 barriers, slot, flag
+constexpr int kSmemBytes = kBiasOffset + kBN * 4 + 1024;  // + alignment slack
+
+__device__ __forceinline__ void tf32_split(float x, float& h, float& l) {
+  const uint32_t u = __float_as_uint(x);
+  if ((u & 0x7F800000u) == 0x7F800000u) {  // Inf / NaN travel in the hi part
+    h = x;
+    l = 0.0f;
+    return;
+  }
+  h = __uint_as_float(u & 0xFFFFE000u);
+  const float r = x - h;  // exact: r holds the 13 cleared mantissa bits
+  l = __uint_as_float(__float_as_uint(r) & 0xFFFFE000u);
+}
+
+// ---------------------------------------------------------------------------
+// Pre-pass 1: X[M,K] (row pitch ldx) -> hi[M,Kp], lo[M,Kp]; pad columns zero.
+__global__ void split_rows_kernel(const float* __restrict__ X, int64_t ldx, int64_t M, int64_t K,
+                                  int64_t Kp, float* __restrict__ hi, float* __restrict__ lo,
+                                  int vec_in) {
+  const int64_t q_per_row = Kp >> 2;
+  const int64_t total = M * q_per_row;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / q_per_row;
+    const int64_t k = (i - m * q_per_row) << 2;
+    float v[4];
+    if (vec_in && k + 4 <= K) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(X + m * ldx + k));
+      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = (k + j < K) ? __ldg(X + m * ldx + k + j) : 0.0f;
+    }
+    float4 h, l;
+    tf32_split(v[0], h.x, l.x);
+    tf32_split(v[1], h.y, l.y);
+    tf32_split(v[2], h.z, l.z);
+    tf32_split(v[3], h.w, l.w);
+    *reinterpret_cast<float4*>(hi + m * Kp + k) = h;
+    *reinterpret_cast<float4*>(lo + m * Kp + k) = l;
+  }
+}
+
+// Pre-pass 2: W[K,N] (row pitch ldw) -> hiT[N,Kp], loT[N,Kp] (K-major).
+__global__ void split_transpose_kernel(const float* __restrict__ W, int64_t ldw, int64_t K,
+                                       int64_t N, int64_t Kp, float* __restrict__ hiT,
+                                       float* __restrict__ loT) {
+  __shared__ float th[32][33];
+  __shared__ float tl[32][33];
+  const int64_t n0 = (int64_t)blockIdx.x * 32;
+  const int64_t k0 = (int64_t)blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int64_t k = k0 + ty + 8 * j, n = n0 + tx;
+    const float x = (k < K && n < N) ? __ldg(W + k * ldw + n) : 0.0f;
+    float h, l;
+    tf32_split(x, h, l);
+    th[ty + 8 * j][tx] = h;
+    tl[ty + 8 * j][tx] = l;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int64_t n = n0 + ty + 8 * j, k = k0 + tx;
+    if (n < N && k < Kp) {
+      hiT[n * Kp + k] = th[tx][ty + 8 * j];
+      loT[n * Kp + k] = tl[tx][ty + 8 * j];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float apply_act(float x, int act, float alpha) {
+  if (act == kActRelu) {
+    // arith.maximumf(x, 0): NaN propagates, max(-0, +0) = +0
+    return (x > 0.0f || x != x) ? x : 0.0f;
+  }
+  if (act == kActLeakyRelu) {
+    // max(x,0) + alpha*min(x,0), both with maximumf/minimumf semantics
+    const float pos = (x > 0.0f || x != x) ? x : 0.0f;
+    const float neg = (x < 0.0f || x != x) ? x : 0.0f;
+    return pos + neg * alpha;
+  }
+  return x;
+}
+
+struct Epilogue {
+  float* Y;
+  int64_t ldy;
+  const float* bias;  // may be null
+  int64_t M, N;
+  int act;
+  float alpha;
+  int vec_out;  // Y base 16-byte aligned and ldy % 4 == 0
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAhi,
+                       const __grid_constant__ CUtensorMap tmAlo,
+                       const __grid_constant__ CUtensorMap tmBhi,
+                       const __grid_constant__ CUtensorMap tmBlo, int num_kb, int tiles_m,
+                       int tiles_n, Epilogue ep, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBarOffset);  // TMA -> MMA
+  uint64_t* empty = full + kStages;                                   // MMA -> TMA
+  uint64_t* tfull = empty + kStages;   // MMA -> epilogue: chunk accumulator ready
+  uint64_t* tempty = tfull + 2;        // epilogue -> MMA: chunk accumulator drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* sbias = reinterpret_cast<float*>(smem + kBiasOffset);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // Grouped raster so that one wave of CTAs shares A rows and B columns in L2.
+  const int tiles_per_group = kGroupM * tiles_n;
+  const int group = blockIdx.x / tiles_per_group;
+  const int first_m = group * kGroupM;
+  const int group_rows = min(tiles_m - first_m, kGroupM);
+  const int in_group = blockIdx.x - group * tiles_per_group;
+  const int tile_m = first_m + in_group % group_rows;
+  const int tile_n = in_group / group_rows;
+  const int m0 = tile_m * kBM;
+  const int n0 = tile_n * kBN;
+  const int num_chunks = (num_kb + kChunkKB - 1) / kChunkKB;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kEpiWarps);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmAhi);
+    tma_prefetch_desc(&tmAlo);
+    tma_prefetch_desc(&tmBhi);
+    tma_prefetch_desc(&tmBlo);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  if (warp >= 2) {
+    for (int i = threadIdx.x - 64; i < kBN; i += 32 * kEpiWarps) {
+      const int64_t n = n0 + i;
+      sbias[i] = (ep.bias != nullptr && n < ep.N) ? ep.bias[n] : 0.0f;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int s = kb % kStages;
+        const int round = kb / kStages;
+        if (round > 0 &&
+            !mbar_wait(&empty[s], (round - 1) & 1, status, kDevTimeoutEmpty, abort_flag))
+          break;
+        uint8_t* st = smem + s * kStageBytes;
+        mbar_arrive_expect_tx(&full[s], kStageBytes);
+        const int kx = kb * kBK;
+        tma_load_2d(st, &tmAhi, &full[s], kx, m0);
+        tma_load_2d(st + kATileBytes, &tmAlo, &full[s], kx, m0);
+        tma_load_2d(st + 2 * kATileBytes, &tmBhi, &full[s], kx, n0);
+        tma_load_2d(st + 2 * kATileBytes + kBTileBytes, &tmBlo, &full[s], kx, n0);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32_f32(kBM, kBN);
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int s = kb % kStages;
+        const int round = kb / kStages;
+        const int chunk = kb / kChunkKB;
+        const int buf = chunk & 1;
+        const bool chunk_start = (kb % kChunkKB) == 0;
+        const bool chunk_end = (kb % kChunkKB) == kChunkKB - 1 || kb == num_kb - 1;
+        if (chunk_start && chunk >= 2) {
+          if (!mbar_wait(&tempty[buf], ((chunk >> 1) - 1) & 1, status, kDevTimeoutAccum,
+                         abort_flag))
+            break;
+          tc_fence_after();
+        }
+        if (!mbar_wait(&full[s], round & 1, status, kDevTimeoutFull, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * kBN;
+        const uint32_t st = smem_u32(smem + s * kStageBytes);
+#pragma unroll
+        for (int k = 0; k < kBK / 8; ++k) {  // tf32 UMMA consumes K = 8 (32 B)
+          const uint64_t a_hi = umma_desc_k_sw128(st + k * 32);
+          const uint64_t a_lo = umma_desc_k_sw128(st + kATileBytes + k * 32);
+          const uint64_t b_hi = umma_desc_k_sw128(st + 2 * kATileBytes + k * 32);
+          const uint64_t b_lo = umma_desc_k_sw128(st + 2 * kATileBytes + kBTileBytes + k * 32);
+          umma_tf32(d_tmem, a_lo, b_hi, idesc, (chunk_start && k == 0) ? 0u : 1u);
+          umma_tf32(d_tmem, a_hi, b_lo, idesc, 1u);
+          umma_tf32(d_tmem, a_hi, b_hi, idesc, 1u);
+        }
+        umma_commit(&empty[s]);  // stage s may be refilled once these MMAs finish
+        if (chunk_end) umma_commit(&tfull[buf]);
+      }
+    }
+  } else {
+    // ------------------------------------------------ epilogue (8 warps)
+    // Warp w reads TMEM lane quarter w % 4 and column half (w - 2) / 4.
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    float acc[128];
+#pragma unroll
+    for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
+    bool ok = true;
+#pragma unroll 1
+    for (int c = 0; c < num_chunks; ++c) {
+      const int buf = c & 1;
+      if (!mbar_wait(&tfull[buf], (c >> 1) & 1, status, kDevTimeoutAccum, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + lane_off + buf * kBN + half * 128;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + g * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[g * 32 + j] += __uint_as_float(r[j]);  // RN add
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+    if (ok && !*abort_flag) {
+      const int64_t row = (int64_t)m0 + quarter * 32 + lane;
+      const int64_t col0 = (int64_t)n0 + half * 128;
+      if (row < ep.M) {
+        float* dst = ep.Y + row * ep.ldy + col0;
+        const float* bh = sbias + half * 128;
+#pragma unroll
+        for (int j = 0; j < 128; j += 4) {
+          const float v0 = apply_act(acc[j] + bh[j], ep.act, ep.alpha);
+          const float v1 = apply_act(acc[j + 1] + bh[j + 1], ep.act, ep.alpha);
+          const float v2 = apply_act(acc[j + 2] + bh[j + 2], ep.act, ep.alpha);
+          const float v3 = apply_act(acc[j + 3] + bh[j + 3], ep.act, ep.alpha);
+          if (ep.vec_out && col0 + j + 4 <= ep.N) {
+            *reinterpret_cast<float4*>(dst + j) = make_float4(v0, v1, v2, v3);
+          } else {
+            if (col0 + j < ep.N) dst[j] = v0;
+            if (col0 + j + 1 < ep.N) dst[j + 1] = v1;
+            if (col0 + j + 2 < ep.N) dst[j + 2] = v2;
+            if (col0 + j + 3 < ep.N) dst[j + 3] = v3;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D f32 tensor map: `rows` rows of `cols` valid floats, row pitch `pitch`
+// floats (multiple of 4), box = box_rows x 32 floats, 128-byte swizzle.
+// Coordinates beyond `cols` / `rows` read as zero.
+static int make_tmap(CUtensorMap* map, const float* base, int64_t cols, int64_t rows,
+                     int64_t pitch, int box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return kErrDriver;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)pitch * 4};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? kOk : kErrDriver;
+}
+
+int64_t dense_f32_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  const int64_t Kp = (K + 3) & ~int64_t(3);
+  // hi + lo of X (M x Kp) and of W^T (N x Kp), each region 256-byte aligned
+  auto al = [](int64_t b) { return (b + 255) & ~int64_t(255); };
+  return 2 * al(M * Kp * 4) + 2 * al(N * Kp * 4);
+}
+
+int split_w_f32(const float* W, int64_t ldw, int64_t K, int64_t N, float* whiT, float* wloT,
+                cudaStream_t stream) {
+  const int64_t Kp = (K + 3) & ~int64_t(3);
+  dim3 grid((unsigned)((N + 31) / 32), (unsigned)((Kp + 31) / 32));
+  split_transpose_kernel<<<grid, dim3(32, 8), 0, stream>>>(W, ldw, K, N, Kp, whiT, wloT);
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int split_x_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xhi, float* xlo,
+                cudaStream_t stream) {
+  const int64_t Kp = (K + 3) & ~int64_t(3);
+  const int vec_in = ((ldx & 3) == 0) && ((reinterpret_cast<uintptr_t>(X) & 15) == 0);
+  const int64_t total = M * (Kp / 4);
+  int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
+  if (blocks < 1) blocks = 1;
+  split_rows_kernel<<<blocks, 256, 0, stream>>>(X, ldx, M, K, Kp, xhi, xlo, vec_in);
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
+                         const float* wloT, int64_t M, int64_t N, int64_t K, const float* bias,
+                         float* Y, int64_t ldy, int act, float alpha, int* status,
+                         cudaStream_t stream) {
+  static bool attr_set = false;  // per process; the attribute is per function
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemBytes) != cudaSuccess)
+      return kErrCuda;
+    attr_set = true;
+  }
+  const int64_t Kp = (K + 3) & ~int64_t(3);
+  CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
+  int rc = make_tmap(&ta_hi, xhi, K, M, Kp, kBM);
+  if (rc == kOk) rc = make_tmap(&ta_lo, xlo, K, M, Kp, kBM);
+  if (rc == kOk) rc = make_tmap(&tb_hi, whiT, K, N, Kp, kBN);
+  if (rc == kOk) rc = make_tmap(&tb_lo, wloT, K, N, Kp, kBN);
+  if (rc != kOk) return rc;
+  Epilogue ep;
+  ep.Y = Y;
+  ep.ldy = ldy;
+  ep.bias = bias;
+  ep.M = M;
+  ep.N = N;
+  ep.act = act;
+  ep.alpha = alpha;
+  ep.vec_out = ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(Y) & 15) == 0);
+  const int tiles_m = (int)((M + kBM - 1) / kBM);
+  const int tiles_n = (int)((N + kBN - 1) / kBN);
+  const int num_kb = (int)((K + kBK - 1) / kBK);
+  gemm_tf32x3_kernel<<<tiles_m * tiles_n, kThreads, kSmemBytes, stream>>>(
+      ta_hi, ta_lo, tb_hi, tb_lo, num_kb, tiles_m, tiles_n, ep, status);
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+}  // namespace b200

@@ -1,0 +1,50 @@
+// Internal interface between the CUDA kernel files and the host runtime.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace b200 {
+
+// Status codes shared with the public C-ABI (include/b200_edsl.h).
+enum Status : int {
+  kOk = 0,
+  kErrInvalidArg = 1,
+  kErrCuda = 2,
+  kErrDriver = 3,
+  kErrNoDevice = 4,
+  kErrDeviceTimeout = 5,
+  kErrOutOfMemory = 6,
+  kErrTooLarge = 7,
+};
+
+enum Act : int { kActNone = 0, kActRelu = 1, kActLeakyRelu = 2 };
+
+// Number of kernels this library has launched (process-wide).
+void count_launch();
+
+// ---- 3xTF32 GEMM (gemm_tf32x3.cu)
+int64_t dense_f32_workspace_bytes(int64_t M, int64_t N, int64_t K);
+int split_x_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xhi, float* xlo,
+                cudaStream_t stream);
+int split_w_f32(const float* W, int64_t ldw, int64_t K, int64_t N, float* whiT, float* wloT,
+                cudaStream_t stream);
+int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
+                         const float* wloT, int64_t M, int64_t N, int64_t K, const float* bias,
+                         float* Y, int64_t ldy, int act, float alpha, int* status,
+                         cudaStream_t stream);
+
+// ---- i32 GEMM (gemm_i32.cu): C = A*B mod 2^32
+int gemm_i32(const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb, int32_t* C,
+             int64_t ldc, int64_t M, int64_t N, int64_t K, const int32_t* bias,
+             cudaStream_t stream);
+
+// ---- elementwise (elementwise.cu)
+int bias_act_f32(const float* X, int64_t ldx, const float* b, float* Y, int64_t ldy, int64_t M,
+                 int64_t N, int act, float alpha, cudaStream_t stream);
+int act_f32(const float* X, float* Y, int64_t count, int act, float alpha, cudaStream_t stream);
+int bias_add_i32(const int32_t* X, int64_t ldx, const int32_t* b, int32_t* Y, int64_t ldy,
+                 int64_t M, int64_t N, cudaStream_t stream);
+int fill_bias_act_f32(const float* b, float* Y, int64_t ldy, int64_t M, int64_t N, int act,
+                      float alpha, cudaStream_t stream);
+
+}  // namespace b200

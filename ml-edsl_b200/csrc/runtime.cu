@@ -1,0 +1,716 @@
+// Host runtime behind include/b200_edsl.h.
+//
+// Owns, per device: three streams (compute, host->device, device->host), a
+// device status word that kernels set when a bounded wait gives up, grow-only
+// device buffers for host-pointer calls, and per-stream scratch for the
+// device-pointer calls. Replaces the reference's GPU executor, which
+// allocated, copied, launched with a full context synchronize after every
+// kernel, copied back and freed on each call
+// (reference: cpp/src/MLIRExecutor.cpp:187-238, cpp/src/MLIRCompiler.cpp:352-461).
+#include <cuda_runtime.h>
+#include <algorithm>
+#include <atomic>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+#include "../../include/b200_edsl.h"
+#include "kernels.h"
+
+namespace b200 {
+
+static std::atomic<long long> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+namespace {
+
+thread_local std::string t_err;
+thread_local int t_status = 0;
+
+int fail(int code, const std::string& msg) {
+  t_err = msg;
+  t_status = code;
+  return code;
+}
+int fail_cuda(cudaError_t e, const char* what) {
+  cudaGetLastError();  // clear the non-sticky error
+  std::string m = std::string(what) + ": " + cudaGetErrorString(e);
+  return fail(e == cudaErrorMemoryAllocation ? kErrOutOfMemory : kErrCuda, m);
+}
+int succeed() {
+  t_status = kOk;
+  return kOk;
+}
+
+#define B200_CUDA(call, what)                    \
+  do {                                           \
+    cudaError_t e_ = (call);                     \
+    if (e_ != cudaSuccess) return fail_cuda(e_, what); \
+  } while (0)
+
+struct DevBuf {
+  void* p = nullptr;
+  size_t n = 0;
+  // Ensures capacity >= need. The caller guarantees no in-flight work uses it.
+  cudaError_t reserve(size_t need) {
+    if (need <= n) return cudaSuccess;
+    if (p) cudaFree(p);
+    p = nullptr;
+    n = 0;
+    cudaError_t e = cudaMalloc(&p, need);
+    if (e == cudaSuccess) n = need;
+    return e;
+  }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    n = 0;
+  }
+};
+
+constexpr int kRing = 2;  // slab buffers in flight per device
+
+struct DeviceCtx {
+  int dev = -1;
+  std::mutex mu;  // one host-pointer call per device at a time
+  bool ready = false;
+  cudaStream_t s_comp = nullptr, s_h2d = nullptr, s_d2h = nullptr;
+  int* status = nullptr;  // device word written by timed-out kernels
+  // host-pointer call buffers
+  DevBuf w, whi, wlo, bias;
+  DevBuf x[kRing], xhi[kRing], xlo[kRing], y[kRing];
+  cudaEvent_t ev_h2d[kRing], ev_comp[kRing], ev_d2h[kRing];
+  // device-pointer call scratch, keyed by stream
+  std::map<cudaStream_t, DevBuf> scratch;
+};
+
+std::mutex g_mu;
+DeviceCtx g_dev[64];
+int g_default_devices = -1;
+
+int device_count() {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+// Returns the initialised context of `dev` (caller holds no lock).
+int get_ctx(int dev, DeviceCtx** out) {
+  if (dev < 0 || dev >= 64) return fail(kErrInvalidArg, "device index out of range");
+  DeviceCtx& c = g_dev[dev];
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!c.ready) {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    B200_CUDA(cudaSetDevice(dev), "cudaSetDevice");
+    B200_CUDA(cudaStreamCreateWithFlags(&c.s_comp, cudaStreamNonBlocking), "cudaStreamCreate");
+    B200_CUDA(cudaStreamCreateWithFlags(&c.s_h2d, cudaStreamNonBlocking), "cudaStreamCreate");
+    B200_CUDA(cudaStreamCreateWithFlags(&c.s_d2h, cudaStreamNonBlocking), "cudaStreamCreate");
+    B200_CUDA(cudaMalloc(&c.status, sizeof(int)), "cudaMalloc(status)");
+    B200_CUDA(cudaMemset(c.status, 0, sizeof(int)), "cudaMemset(status)");
+    for (int i = 0; i < kRing; ++i) {
+      B200_CUDA(cudaEventCreateWithFlags(&c.ev_h2d[i], cudaEventDisableTiming), "event");
+      B200_CUDA(cudaEventCreateWithFlags(&c.ev_comp[i], cudaEventDisableTiming), "event");
+      B200_CUDA(cudaEventCreateWithFlags(&c.ev_d2h[i], cudaEventDisableTiming), "event");
+    }
+    c.dev = dev;
+    c.ready = true;
+    cudaSetDevice(prev);
+  }
+  *out = &c;
+  return kOk;
+}
+
+int current_ctx(DeviceCtx** out) {
+  int dev = 0;
+  B200_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  return get_ctx(dev, out);
+}
+
+// Reads and clears the device status word after the stream has drained.
+int check_device_status(DeviceCtx* c) {
+  int h = 0;
+  B200_CUDA(cudaMemcpy(&h, c->status, sizeof(int), cudaMemcpyDeviceToHost), "status read");
+  if (h != 0) {
+    cudaMemset(c->status, 0, sizeof(int));
+    char buf[160];
+    snprintf(buf, sizeof buf,
+             "device %d: a kernel gave up a bounded wait (code %d); results are invalid",
+             c->dev, h);
+    return fail(kErrDeviceTimeout, buf);
+  }
+  return kOk;
+}
+
+int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+bool bad_dims(int64_t M, int64_t N, int64_t K) { return M < 0 || N < 0 || K < 0; }
+
+// Scratch layout inside one workspace block.
+struct SplitBufs {
+  float *xhi, *xlo, *whi, *wlo;
+};
+SplitBufs carve(void* ws, int64_t M, int64_t N, int64_t K) {
+  const int64_t Kp = round_up(K, 4);
+  auto al = [](int64_t b) { return round_up(b, 256); };
+  char* p = static_cast<char*>(ws);
+  SplitBufs s;
+  s.xhi = reinterpret_cast<float*>(p);
+  p += al(M * Kp * 4);
+  s.xlo = reinterpret_cast<float*>(p);
+  p += al(M * Kp * 4);
+  s.whi = reinterpret_cast<float*>(p);
+  p += al(N * Kp * 4);
+  s.wlo = reinterpret_cast<float*>(p);
+  return s;
+}
+
+int dense_device(DeviceCtx* c, const float* X, int64_t ldx, const float* W, int64_t ldw,
+                 const float* b, float* Y, int64_t ldy, int64_t M, int64_t N, int64_t K, int act,
+                 float alpha, void* ws, cudaStream_t st) {
+  if (M == 0 || N == 0) return kOk;
+  if (K == 0) return fill_bias_act_f32(b, Y, ldy, M, N, act, alpha, st);
+  SplitBufs s = carve(ws, M, N, K);
+  int rc = split_w_f32(W, ldw, K, N, s.whi, s.wlo, st);
+  if (rc == kOk) rc = split_x_f32(X, ldx, M, K, s.xhi, s.xlo, st);
+  if (rc == kOk)
+    rc = gemm_tf32x3_presplit(s.xhi, s.xlo, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha,
+                              c->status, st);
+  if (rc != kOk) return fail(rc, std::string("dense_f32 launch failed: ") +
+                                     cudaGetErrorString(cudaGetLastError()));
+  return kOk;
+}
+
+int validate_dense(const void* X, int64_t ldx, const void* W, int64_t ldw, const void* Y,
+                   int64_t ldy, int64_t M, int64_t N, int64_t K, int act) {
+  if (bad_dims(M, N, K)) return fail(kErrInvalidArg, "negative dimension");
+  if (act < kActNone || act > kActLeakyRelu) return fail(kErrInvalidArg, "unknown activation");
+  if (M > 0 && N > 0) {
+    if (!Y) return fail(kErrInvalidArg, "null output");
+    if (ldy < N) return fail(kErrInvalidArg, "ldy < N");
+    if (K > 0) {
+      if (!X || !W) return fail(kErrInvalidArg, "null input");
+      if (ldx < K) return fail(kErrInvalidArg, "ldx < K");
+      if (ldw < N) return fail(kErrInvalidArg, "ldw < N");
+    }
+  }
+  if (M > (int64_t)1 << 31 || N > (int64_t)1 << 31 || K > (int64_t)1 << 31)
+    return fail(kErrTooLarge, "dimension exceeds 2^31");
+  return kOk;
+}
+
+// One device's share of a host-pointer dense call: rows [0, M) of the given
+// host views. H2D of slab i+1, compute of slab i and D2H of slab i-1 overlap.
+int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, int64_t ldw,
+                         const float* b, float* Y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                         int act, float alpha) {
+  DeviceCtx* c = nullptr;
+  int rc = get_ctx(dev, &c);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(c->mu);
+  B200_CUDA(cudaSetDevice(dev), "cudaSetDevice");
+  if (M == 0 || N == 0) return kOk;
+  const int64_t Kp = round_up(std::max<int64_t>(K, 1), 4);
+
+  // Slab size: one slab for small calls, else ~8 slabs of >= 1024 rows.
+  int64_t slab = M;
+  if (M * K * 4 >= ((int64_t)32 << 20) && M >= 2048)
+    slab = std::max<int64_t>(1024, round_up((M + 7) / 8, 128));
+  const int64_t nslab = (M + slab - 1) / slab;
+
+  // Weights (replicated): upload + split once per call on the compute stream.
+  B200_CUDA(c->bias.reserve(std::max<int64_t>(N, 1) * 4), "alloc bias");
+  if (K > 0) {
+    B200_CUDA(c->w.reserve(K * N * 4), "alloc W");
+    B200_CUDA(c->whi.reserve(N * Kp * 4), "alloc W split");
+    B200_CUDA(c->wlo.reserve(N * Kp * 4), "alloc W split");
+  }
+  for (int i = 0; i < kRing && i < nslab; ++i) {
+    B200_CUDA(c->y[i].reserve(slab * N * 4), "alloc Y slab");
+    if (K > 0) {
+      B200_CUDA(c->x[i].reserve(slab * K * 4), "alloc X slab");
+      B200_CUDA(c->xhi[i].reserve(slab * Kp * 4), "alloc X split");
+      B200_CUDA(c->xlo[i].reserve(slab * Kp * 4), "alloc X split");
+    }
+  }
+  float* dW = static_cast<float*>(c->w.p);
+  float* dWhi = static_cast<float*>(c->whi.p);
+  float* dWlo = static_cast<float*>(c->wlo.p);
+  float* db = b ? static_cast<float*>(c->bias.p) : nullptr;
+  if (b) B200_CUDA(cudaMemcpyAsync(db, b, N * 4, cudaMemcpyHostToDevice, c->s_comp), "H2D b");
+  if (K > 0) {
+    B200_CUDA(cudaMemcpy2DAsync(dW, N * 4, W, ldw * 4, N * 4, K, cudaMemcpyHostToDevice,
+                                c->s_comp),
+              "H2D W");
+    rc = split_w_f32(dW, N, K, N, dWhi, dWlo, c->s_comp);
+    if (rc) return fail(rc, "split W launch failed");
+  }
+
+  for (int64_t i = 0; i < nslab; ++i) {
+    const int slot = (int)(i % kRing);
+    const int64_t r0 = i * slab;
+    const int64_t rows = std::min(slab, M - r0);
+    float* dX = static_cast<float*>(c->x[slot].p);
+    float* dY = static_cast<float*>(c->y[slot].p);
+    if (i >= kRing) B200_CUDA(cudaStreamWaitEvent(c->s_h2d, c->ev_d2h[slot], 0), "wait");
+    if (K > 0)
+      B200_CUDA(cudaMemcpy2DAsync(dX, K * 4, X + r0 * ldx, ldx * 4, K * 4, rows,
+                                  cudaMemcpyHostToDevice, c->s_h2d),
+                "H2D X");
+    B200_CUDA(cudaEventRecord(c->ev_h2d[slot], c->s_h2d), "record");
+    B200_CUDA(cudaStreamWaitEvent(c->s_comp, c->ev_h2d[slot], 0), "wait");
+    if (K == 0) {
+      rc = fill_bias_act_f32(db, dY, N, rows, N, act, alpha, c->s_comp);
+    } else {
+      float* xhi = static_cast<float*>(c->xhi[slot].p);
+      float* xlo = static_cast<float*>(c->xlo[slot].p);
+      rc = split_x_f32(dX, K, rows, K, xhi, xlo, c->s_comp);
+      if (rc == kOk)
+        rc = gemm_tf32x3_presplit(xhi, xlo, dWhi, dWlo, rows, N, K, db, dY, N, act, alpha,
+                                  c->status, c->s_comp);
+    }
+    if (rc) return fail(rc, "dense kernel launch failed");
+    B200_CUDA(cudaEventRecord(c->ev_comp[slot], c->s_comp), "record");
+    B200_CUDA(cudaStreamWaitEvent(c->s_d2h, c->ev_comp[slot], 0), "wait");
+    B200_CUDA(cudaMemcpy2DAsync(Y + r0 * ldy, ldy * 4, dY, N * 4, N * 4, rows,
+                                cudaMemcpyDeviceToHost, c->s_d2h),
+              "D2H Y");
+    B200_CUDA(cudaEventRecord(c->ev_d2h[slot], c->s_d2h), "record");
+  }
+  B200_CUDA(cudaStreamSynchronize(c->s_d2h), "sync");
+  B200_CUDA(cudaStreamSynchronize(c->s_comp), "sync");
+  return check_device_status(c);
+}
+
+int resolve_ndev(int ndev) {
+  if (ndev <= 0) ndev = b200_get_default_devices();
+  return ndev;
+}
+
+// Splits rows [0, M) into `ndev` contiguous shards and runs fn(dev, r0, rows)
+// on one host thread per device.
+template <class Fn>
+int run_sharded(int ndev, int64_t M, Fn fn) {
+  const int avail = device_count();
+  if (avail == 0) return fail(kErrNoDevice, "no CUDA device available");
+  if (ndev > avail) {
+    char buf[96];
+    snprintf(buf, sizeof buf, "requested %d devices, %d available", ndev, avail);
+    return fail(kErrInvalidArg, buf);
+  }
+  if (ndev == 1) return fn(0, 0, M);
+  std::vector<int> rcs(ndev, kOk);
+  std::vector<std::string> errs(ndev);
+  std::vector<std::thread> th;
+  const int64_t base = M / ndev, rem = M % ndev;
+  int64_t r0 = 0;
+  for (int d = 0; d < ndev; ++d) {
+    const int64_t rows = base + (d < rem ? 1 : 0);
+    th.emplace_back([&, d, r0, rows] {
+      rcs[d] = fn(d, r0, rows);
+      if (rcs[d]) errs[d] = t_err;
+    });
+    r0 += rows;
+  }
+  for (auto& t : th) t.join();
+  for (int d = 0; d < ndev; ++d)
+    if (rcs[d]) return fail(rcs[d], "device " + std::to_string(d) + ": " + errs[d]);
+  return kOk;
+}
+
+int simple_host_i32_matmul(int dev, const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb,
+                           const int32_t* bias, int32_t* C, int64_t ldc, int64_t M, int64_t N,
+                           int64_t K) {
+  DeviceCtx* c = nullptr;
+  int rc = get_ctx(dev, &c);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(c->mu);
+  B200_CUDA(cudaSetDevice(dev), "cudaSetDevice");
+  if (M == 0 || N == 0) return kOk;
+  B200_CUDA(c->x[0].reserve(std::max<int64_t>(M * K, 1) * 4), "alloc A");
+  B200_CUDA(c->w.reserve(std::max<int64_t>(K * N, 1) * 4), "alloc B");
+  B200_CUDA(c->y[0].reserve(M * N * 4), "alloc C");
+  B200_CUDA(c->bias.reserve(std::max<int64_t>(N, 1) * 4), "alloc bias");
+  int32_t* dA = static_cast<int32_t*>(c->x[0].p);
+  int32_t* dB = static_cast<int32_t*>(c->w.p);
+  int32_t* dC = static_cast<int32_t*>(c->y[0].p);
+  int32_t* db = bias ? static_cast<int32_t*>(c->bias.p) : nullptr;
+  cudaStream_t s = c->s_comp;
+  if (K > 0) {
+    B200_CUDA(cudaMemcpy2DAsync(dA, K * 4, A, lda * 4, K * 4, M, cudaMemcpyHostToDevice, s),
+              "H2D A");
+    B200_CUDA(cudaMemcpy2DAsync(dB, N * 4, B, ldb * 4, N * 4, K, cudaMemcpyHostToDevice, s),
+              "H2D B");
+  }
+  if (bias) B200_CUDA(cudaMemcpyAsync(db, bias, N * 4, cudaMemcpyHostToDevice, s), "H2D bias");
+  rc = gemm_i32(dA, K, dB, N, dC, N, M, N, K, db, s);
+  if (rc) return fail(rc, "i32 matmul launch failed");
+  B200_CUDA(cudaMemcpy2DAsync(C, ldc * 4, dC, N * 4, N * 4, M, cudaMemcpyDeviceToHost, s),
+            "D2H C");
+  B200_CUDA(cudaStreamSynchronize(s), "sync");
+  return kOk;
+}
+
+// Host wrapper for the elementwise kernels: one device, whole-buffer copies.
+template <class Launch>
+int elementwise_host(size_t in_bytes_x, const void* X, size_t in_bytes_b, const void* b,
+                     size_t out_bytes, void* Y, Launch launch) {
+  DeviceCtx* c = nullptr;
+  int rc = get_ctx(0, &c);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(c->mu);
+  B200_CUDA(cudaSetDevice(0), "cudaSetDevice");
+  if (out_bytes == 0) return kOk;
+  B200_CUDA(c->x[0].reserve(std::max<size_t>(in_bytes_x, 4)), "alloc X");
+  B200_CUDA(c->bias.reserve(std::max<size_t>(in_bytes_b, 4)), "alloc b");
+  B200_CUDA(c->y[0].reserve(out_bytes), "alloc Y");
+  cudaStream_t s = c->s_comp;
+  B200_CUDA(cudaMemcpyAsync(c->x[0].p, X, in_bytes_x, cudaMemcpyHostToDevice, s), "H2D X");
+  if (b) B200_CUDA(cudaMemcpyAsync(c->bias.p, b, in_bytes_b, cudaMemcpyHostToDevice, s), "H2D b");
+  rc = launch(c->x[0].p, b ? c->bias.p : nullptr, c->y[0].p, s);
+  if (rc) return fail(rc, "elementwise launch failed");
+  B200_CUDA(cudaMemcpyAsync(Y, c->y[0].p, out_bytes, cudaMemcpyDeviceToHost, s), "D2H Y");
+  B200_CUDA(cudaStreamSynchronize(s), "sync");
+  return kOk;
+}
+
+}  // namespace
+}  // namespace b200
+
+using namespace b200;
+
+template <class T>
+static T* at(void* aligned, int64_t off) {
+  return static_cast<T*>(aligned) + off;
+}
+
+// =========================================================================
+extern "C" {
+
+const char* b200_version(void) { return "b200-edsl 0.1 (sm_100a, tcgen05 3xTF32)"; }
+const char* b200_last_error(void) { return t_err.c_str(); }
+int b200_last_status(void) { return t_status; }
+int b200_device_count(void) { return device_count(); }
+long long b200_launch_count(void) { return g_launches.load(); }
+
+int b200_set_default_devices(int ndev) {
+  if (ndev < 1) return fail(kErrInvalidArg, "ndev must be >= 1");
+  g_default_devices = ndev;
+  return succeed();
+}
+
+int b200_get_default_devices(void) {
+  if (g_default_devices < 1) {
+    const char* e = getenv("B200_DEVICES");
+    g_default_devices = (e && atoi(e) > 0) ? atoi(e) : 1;
+  }
+  return g_default_devices;
+}
+
+int b200_release(void) {
+  for (int d = 0; d < 64; ++d) {
+    DeviceCtx& c = g_dev[d];
+    std::lock_guard<std::mutex> lk(c.mu);
+    if (!c.ready) continue;
+    cudaSetDevice(d);
+    cudaDeviceSynchronize();
+    c.w.release(); c.whi.release(); c.wlo.release(); c.bias.release();
+    for (int i = 0; i < kRing; ++i) {
+      c.x[i].release(); c.xhi[i].release(); c.xlo[i].release(); c.y[i].release();
+    }
+    for (auto& kv : c.scratch) kv.second.release();
+    c.scratch.clear();
+  }
+  return succeed();
+}
+
+// ---------------------------------------------------------------- device API
+int64_t b200_dense_f32_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  if (bad_dims(M, N, K)) return -1;
+  return dense_f32_workspace_bytes(M, N, std::max<int64_t>(K, 1));
+}
+
+int b200_dense_f32_ws(const float* X, int64_t ldx, const float* W, int64_t ldw, const float* b,
+                      float* Y, int64_t ldy, int64_t M, int64_t N, int64_t K, int act,
+                      float alpha, void* workspace, int64_t workspace_bytes, void* stream) {
+  int rc = validate_dense(X, ldx, W, ldw, Y, ldy, M, N, K, act);
+  if (rc) return rc;
+  const int64_t need = dense_f32_workspace_bytes(M, N, std::max<int64_t>(K, 1));
+  if (K > 0 && M > 0 && N > 0) {
+    if (!workspace || workspace_bytes < need)
+      return fail(kErrInvalidArg, "workspace missing or smaller than "
+                                  "b200_dense_f32_workspace_bytes()");
+    if (reinterpret_cast<uintptr_t>(workspace) & 255)
+      return fail(kErrInvalidArg, "workspace must be 256-byte aligned");
+  }
+  DeviceCtx* c = nullptr;
+  if ((rc = current_ctx(&c))) return rc;
+  rc = dense_device(c, X, ldx, W, ldw, b, Y, ldy, M, N, K, act, alpha, workspace,
+                    static_cast<cudaStream_t>(stream));
+  return rc ? rc : succeed();
+}
+
+int b200_dense_f32(const float* X, int64_t ldx, const float* W, int64_t ldw, const float* b,
+                   float* Y, int64_t ldy, int64_t M, int64_t N, int64_t K, int act, float alpha,
+                   void* stream) {
+  int rc = validate_dense(X, ldx, W, ldw, Y, ldy, M, N, K, act);
+  if (rc) return rc;
+  DeviceCtx* c = nullptr;
+  if ((rc = current_ctx(&c))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* ws = nullptr;
+  if (M > 0 && N > 0 && K > 0) {
+    const size_t need = (size_t)dense_f32_workspace_bytes(M, N, K);
+    std::lock_guard<std::mutex> lk(g_mu);
+    DevBuf& buf = c->scratch[st];
+    if (buf.n < need) {
+      // The old buffer may still be read by queued work on this stream.
+      B200_CUDA(cudaStreamSynchronize(st), "sync before scratch growth");
+      B200_CUDA(buf.reserve(need), "alloc scratch");
+    }
+    ws = buf.p;
+  }
+  rc = dense_device(c, X, ldx, W, ldw, b, Y, ldy, M, N, K, act, alpha, ws, st);
+  return rc ? rc : succeed();
+}
+
+int b200_matmul_i32(const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb,
+                    const int32_t* bias, int32_t* C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                    void* stream) {
+  int rc = validate_dense(A, lda, B, ldb, C, ldc, M, N, K, kActNone);
+  if (rc) return rc;
+  if (M == 0 || N == 0) return succeed();
+  rc = gemm_i32(A, lda, B, ldb, C, ldc, M, N, K, bias, static_cast<cudaStream_t>(stream));
+  return rc ? fail(rc, "i32 matmul launch failed") : succeed();
+}
+
+int b200_bias_act_f32(const float* X, int64_t ldx, const float* b, float* Y, int64_t ldy,
+                      int64_t M, int64_t N, int act, float alpha, void* stream) {
+  if (M < 0 || N < 0 || act < 0 || act > 2) return fail(kErrInvalidArg, "bad arguments");
+  if (M > 0 && N > 0 && (!X || !Y || ldx < N || ldy < N))
+    return fail(kErrInvalidArg, "null buffer or pitch < N");
+  int rc = bias_act_f32(X, ldx, b, Y, ldy, M, N, act, alpha, static_cast<cudaStream_t>(stream));
+  return rc ? fail(rc, "bias/activation launch failed") : succeed();
+}
+
+int b200_act_f32(const float* X, float* Y, int64_t count, int act, float alpha, void* stream) {
+  if (count < 0 || act < 0 || act > 2) return fail(kErrInvalidArg, "bad arguments");
+  if (count > 0 && (!X || !Y)) return fail(kErrInvalidArg, "null buffer");
+  int rc = act_f32(X, Y, count, act, alpha, static_cast<cudaStream_t>(stream));
+  return rc ? fail(rc, "activation launch failed") : succeed();
+}
+
+int b200_bias_add_i32(const int32_t* X, int64_t ldx, const int32_t* b, int32_t* Y, int64_t ldy,
+                      int64_t M, int64_t N, void* stream) {
+  if (M < 0 || N < 0) return fail(kErrInvalidArg, "negative dimension");
+  if (M > 0 && N > 0 && (!X || !b || !Y || ldx < N || ldy < N))
+    return fail(kErrInvalidArg, "null buffer or pitch < N");
+  int rc = bias_add_i32(X, ldx, b, Y, ldy, M, N, static_cast<cudaStream_t>(stream));
+  return rc ? fail(rc, "bias add launch failed") : succeed();
+}
+
+int b200_stream_sync(void* stream) {
+  DeviceCtx* c = nullptr;
+  int rc = current_ctx(&c);
+  if (rc) return rc;
+  B200_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "stream sync");
+  rc = check_device_status(c);
+  return rc ? rc : succeed();
+}
+
+// ---------------------------------------------------------------- host API
+int b200_dense_f32_host(const float* X, int64_t ldx, const float* W, int64_t ldw, const float* b,
+                        float* Y, int64_t ldy, int64_t M, int64_t N, int64_t K, int act,
+                        float alpha, int ndev) {
+  int rc = validate_dense(X, ldx, W, ldw, Y, ldy, M, N, K, act);
+  if (rc) return rc;
+  ndev = resolve_ndev(ndev);
+  if (M < ndev) ndev = M > 0 ? (int)M : 1;
+  rc = run_sharded(ndev, M, [&](int dev, int64_t r0, int64_t rows) {
+    return dense_host_on_device(dev, X + r0 * ldx, ldx, W, ldw, b, Y + r0 * ldy, ldy, rows, N, K,
+                                act, alpha);
+  });
+  return rc ? rc : succeed();
+}
+
+int b200_matmul_i32_host(const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb,
+                         const int32_t* bias, int32_t* C, int64_t ldc, int64_t M, int64_t N,
+                         int64_t K, int ndev) {
+  int rc = validate_dense(A, lda, B, ldb, C, ldc, M, N, K, kActNone);
+  if (rc) return rc;
+  ndev = resolve_ndev(ndev);
+  if (M < ndev) ndev = M > 0 ? (int)M : 1;
+  rc = run_sharded(ndev, M, [&](int dev, int64_t r0, int64_t rows) {
+    return simple_host_i32_matmul(dev, A + r0 * lda, lda, B, ldb, bias, C + r0 * ldc, ldc, rows,
+                                  N, K);
+  });
+  return rc ? rc : succeed();
+}
+
+int b200_bias_act_f32_host(const float* X, int64_t ldx, const float* b, float* Y, int64_t ldy,
+                           int64_t M, int64_t N, int act, float alpha) {
+  if (M < 0 || N < 0 || act < 0 || act > 2) return fail(kErrInvalidArg, "bad arguments");
+  if (M == 0 || N == 0) return succeed();
+  if (!X || !Y || ldx < N || ldy < N) return fail(kErrInvalidArg, "null buffer or pitch < N");
+  if (device_count() == 0) return fail(kErrNoDevice, "no CUDA device available");
+  // Device copies are dense (pitch N); host pitches are honoured by 2-D copies.
+  std::vector<float> xs, ys;
+  const float* xin = X;
+  if (ldx != N) {
+    xs.resize(M * N);
+    for (int64_t i = 0; i < M; ++i) memcpy(&xs[i * N], X + i * ldx, N * 4);
+    xin = xs.data();
+  }
+  float* yout = Y;
+  if (ldy != N) {
+    ys.resize(M * N);
+    yout = ys.data();
+  }
+  int rc = elementwise_host(M * N * 4, xin, b ? N * 4 : 0, b, M * N * 4, yout,
+                            [&](void* dx, void* dbias, void* dy, cudaStream_t s) {
+                              return bias_act_f32(static_cast<float*>(dx), N,
+                                                  static_cast<float*>(dbias),
+                                                  static_cast<float*>(dy), N, M, N, act, alpha, s);
+                            });
+  if (rc) return rc;
+  if (ldy != N)
+    for (int64_t i = 0; i < M; ++i) memcpy(Y + i * ldy, &ys[i * N], N * 4);
+  return succeed();
+}
+
+int b200_bias_add_i32_host(const int32_t* X, int64_t ldx, const int32_t* b, int32_t* Y,
+                           int64_t ldy, int64_t M, int64_t N) {
+  if (M < 0 || N < 0) return fail(kErrInvalidArg, "negative dimension");
+  if (M == 0 || N == 0) return succeed();
+  if (!X || !b || !Y || ldx != N || ldy != N)
+    return fail(kErrInvalidArg, "null buffer or non-contiguous rows");
+  if (device_count() == 0) return fail(kErrNoDevice, "no CUDA device available");
+  int rc = elementwise_host(M * N * 4, X, N * 4, b, M * N * 4, Y,
+                            [&](void* dx, void* dbias, void* dy, cudaStream_t s) {
+                              return bias_add_i32(static_cast<int32_t*>(dx), N,
+                                                  static_cast<int32_t*>(dbias),
+                                                  static_cast<int32_t*>(dy), N, M, N, s);
+                            });
+  return rc ? rc : succeed();
+}
+
+int b200_act_f32_host(const float* X, float* Y, int64_t count, int act, float alpha) {
+  if (count < 0 || act < 0 || act > 2) return fail(kErrInvalidArg, "bad arguments");
+  if (count == 0) return succeed();
+  if (!X || !Y) return fail(kErrInvalidArg, "null buffer");
+  if (device_count() == 0) return fail(kErrNoDevice, "no CUDA device available");
+  int rc = elementwise_host(count * 4, X, 0, nullptr, count * 4, Y,
+                            [&](void* dx, void*, void* dy, cudaStream_t s) {
+                              return act_f32(static_cast<float*>(dx), static_cast<float*>(dy),
+                                             count, act, alpha, s);
+                            });
+  return rc ? rc : succeed();
+}
+
+// ---------------------------------------------------------------- memref ABI
+#define M2(n) n##_aligned, n##_off, n##_s0, n##_s1, n##_st0, n##_st1
+#define M1(n) n##_aligned, n##_off, n##_s0, n##_st0
+
+static bool memref2_ok(const char* name, void* aligned, int64_t s1, int64_t st0, int64_t st1) {
+  if (!aligned) return fail(kErrInvalidArg, std::string(name) + ": null memref"), false;
+  if (st1 != 1) return fail(kErrInvalidArg, std::string(name) + ": innermost stride != 1"), false;
+  if (st0 < s1) return fail(kErrInvalidArg, std::string(name) + ": row stride < row length"), false;
+  return true;
+}
+static bool memref1_ok(const char* name, void* aligned, int64_t st0) {
+  if (!aligned) return fail(kErrInvalidArg, std::string(name) + ": null memref"), false;
+  if (st0 != 1) return fail(kErrInvalidArg, std::string(name) + ": stride != 1"), false;
+  return true;
+}
+
+static void memref_dense_f32(void* x_al, int64_t x_off, int64_t x_s0, int64_t x_s1,
+                             int64_t x_st0, int64_t x_st1, void* w_al, int64_t w_off,
+                             int64_t w_s0, int64_t w_s1, int64_t w_st0, int64_t w_st1,
+                             void* b_al, int64_t b_off, int64_t b_s0, int64_t b_st0, bool has_b,
+                             void* y_al, int64_t y_off, int64_t y_s0, int64_t y_s1, int64_t y_st0,
+                             int64_t y_st1, int act) {
+  if (!memref2_ok("lhs", x_al, x_s1, x_st0, x_st1) || !memref2_ok("rhs", w_al, w_s1, w_st0, w_st1) ||
+      !memref2_ok("out", y_al, y_s1, y_st0, y_st1))
+    return;
+  if (has_b && !memref1_ok("bias", b_al, b_st0)) return;
+  if (x_s1 != w_s0 || y_s0 != x_s0 || y_s1 != w_s1 || (has_b && b_s0 != w_s1)) {
+    fail(kErrInvalidArg, "memref shapes do not form [M,K]x[K,N]->[M,N]");
+    return;
+  }
+  b200_dense_f32_host(at<float>(x_al, x_off), x_st0, at<float>(w_al, w_off), w_st0,
+                      has_b ? at<float>(b_al, b_off) : nullptr, at<float>(y_al, y_off), y_st0,
+                      x_s0, w_s1, x_s1, act, 0.0f, 0);
+}
+
+void b200_memref_matmul_f32(B200_MEMREF2(A), B200_MEMREF2(B), B200_MEMREF2(C)) {
+  memref_dense_f32(M2(A), M2(B), nullptr, 0, 0, 1, false, M2(C), kActNone);
+}
+void b200_memref_matmul_relu_f32(B200_MEMREF2(A), B200_MEMREF2(B), B200_MEMREF2(C)) {
+  memref_dense_f32(M2(A), M2(B), nullptr, 0, 0, 1, false, M2(C), kActRelu);
+}
+void b200_memref_dense_f32(B200_MEMREF2(X), B200_MEMREF2(W), B200_MEMREF1(b), B200_MEMREF2(Y)) {
+  memref_dense_f32(M2(X), M2(W), M1(b), true, M2(Y), kActNone);
+}
+void b200_memref_dense_relu_f32(B200_MEMREF2(X), B200_MEMREF2(W), B200_MEMREF1(b),
+                                B200_MEMREF2(Y)) {
+  memref_dense_f32(M2(X), M2(W), M1(b), true, M2(Y), kActRelu);
+}
+
+static void memref_i32(void* x_al, int64_t x_off, int64_t x_s0, int64_t x_s1, int64_t x_st0,
+                       int64_t x_st1, void* w_al, int64_t w_off, int64_t w_s0, int64_t w_s1,
+                       int64_t w_st0, int64_t w_st1, void* b_al, int64_t b_off, int64_t b_s0,
+                       int64_t b_st0, bool has_b, void* y_al, int64_t y_off, int64_t y_s0,
+                       int64_t y_s1, int64_t y_st0, int64_t y_st1) {
+  if (!memref2_ok("lhs", x_al, x_s1, x_st0, x_st1) || !memref2_ok("rhs", w_al, w_s1, w_st0, w_st1) ||
+      !memref2_ok("out", y_al, y_s1, y_st0, y_st1))
+    return;
+  if (has_b && !memref1_ok("bias", b_al, b_st0)) return;
+  if (x_s1 != w_s0 || y_s0 != x_s0 || y_s1 != w_s1 || (has_b && b_s0 != w_s1)) {
+    fail(kErrInvalidArg, "memref shapes do not form [M,K]x[K,N]->[M,N]");
+    return;
+  }
+  b200_matmul_i32_host(at<int32_t>(x_al, x_off), x_st0, at<int32_t>(w_al, w_off), w_st0,
+                       has_b ? at<int32_t>(b_al, b_off) : nullptr, at<int32_t>(y_al, y_off),
+                       y_st0, x_s0, w_s1, x_s1, 0);
+}
+
+void b200_memref_matmul_i32(B200_MEMREF2(A), B200_MEMREF2(B), B200_MEMREF2(C)) {
+  memref_i32(M2(A), M2(B), nullptr, 0, 0, 1, false, M2(C));
+}
+void b200_memref_dense_i32(B200_MEMREF2(X), B200_MEMREF2(W), B200_MEMREF1(b), B200_MEMREF2(Y)) {
+  memref_i32(M2(X), M2(W), M1(b), true, M2(Y));
+}
+
+static void memref_bias_act(void* x_al, int64_t x_off, int64_t x_s0, int64_t x_s1, int64_t x_st0,
+                            int64_t x_st1, void* b_al, int64_t b_off, int64_t b_s0, int64_t b_st0,
+                            bool has_b, void* y_al, int64_t y_off, int64_t y_s0, int64_t y_s1,
+                            int64_t y_st0, int64_t y_st1, int act) {
+  if (!memref2_ok("input", x_al, x_s1, x_st0, x_st1) || !memref2_ok("out", y_al, y_s1, y_st0, y_st1))
+    return;
+  if (has_b && !memref1_ok("bias", b_al, b_st0)) return;
+  if (y_s0 != x_s0 || y_s1 != x_s1 || (has_b && b_s0 != x_s1)) {
+    fail(kErrInvalidArg, "memref shapes do not match");
+    return;
+  }
+  b200_bias_act_f32_host(at<float>(x_al, x_off), x_st0, has_b ? at<float>(b_al, b_off) : nullptr,
+                         at<float>(y_al, y_off), y_st0, x_s0, x_s1, act, 0.0f);
+}
+
+void b200_memref_bias_add_f32(B200_MEMREF2(X), B200_MEMREF1(b), B200_MEMREF2(Y)) {
+  memref_bias_act(M2(X), M1(b), true, M2(Y), kActNone);
+}
+void b200_memref_bias_relu_f32(B200_MEMREF2(X), B200_MEMREF1(b), B200_MEMREF2(Y)) {
+  memref_bias_act(M2(X), M1(b), true, M2(Y), kActRelu);
+}
+void b200_memref_relu_f32(B200_MEMREF2(X), B200_MEMREF2(Y)) {
+  memref_bias_act(M2(X), nullptr, 0, 0, 1, false, M2(Y), kActRelu);
+}
+
+}  // extern "C"

@@ -1,0 +1,9 @@
+"""CPU oracle for the dense-layer hot path (test infrastructure only).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use this
+package, as the checker; the product path never imports it.
+"""
+from .oracle import (  # noqa: F401
+    build, dense_f32, matmul_i32, bias_act_f32, fma_mode, gen_config_inputs, f32_bound,
+    ACT_NONE, ACT_RELU, ACT_LEAKY_RELU, MODE_AUTO, MODE_FMA, MODE_MULADD,
+)

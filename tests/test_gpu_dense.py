@@ -1,0 +1,197 @@
+"""GPU parity of the 3xTF32 tcgen05 dense kernel against the CPU oracle.
+
+Tolerance (the f32 bar of the path): max|Y_b200 - Y_oracle| <=
+1e-4 * sqrt(K) * max|X| * max|W|, checked through the C-ABI.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle
+from gpu_util import dense_device, max_err, ptr, stream_ptr
+from mlir_edsl import _native
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(M, N, K, seed, lo=-1.0, hi=1.0):
+    rng = np.random.default_rng(seed)
+    X = rng.uniform(lo, hi, (M, K)).astype(np.float32)
+    W = rng.uniform(lo, hi, (K, N)).astype(np.float32)
+    b = rng.uniform(lo, hi, (N,)).astype(np.float32)
+    return X, W, b
+
+
+SHAPES = [
+    (128, 256, 32),     # exactly one tile, one k-block
+    (1, 1, 1),
+    (2, 2, 2),
+    (7, 9, 13),
+    (129, 257, 63),     # one past every tile edge
+    (256, 512, 96),     # multiple tiles, 3 k-blocks (ring wrap-around)
+    (300, 500, 1001),   # K not a multiple of 4: padded split path
+    (1000, 999, 1001),  # the ragged benchmark shape
+]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+@pytest.mark.parametrize("act", [0, 1])
+def test_dense_matches_oracle(cuda, M, N, K, act):
+    import torch
+    X, W, b = _inputs(M, N, K, seed=M * 7 + N * 3 + K)
+    got = dense_device(torch, X, W, b, act=act)
+    ref = oracle.dense_f32(X, W, b, act=act)
+    bound = oracle.f32_bound(K, X, W)
+    assert np.isfinite(got).all()
+    assert max_err(got, ref) <= bound, (max_err(got, ref), bound)
+
+
+def test_matmul_no_bias(cuda):
+    import torch
+    X, W, _ = _inputs(384, 640, 200, seed=5)
+    got = dense_device(torch, X, W, None, act=0)
+    ref = oracle.dense_f32(X, W)
+    assert max_err(got, ref) <= oracle.f32_bound(200, X, W)
+
+
+def test_leaky_relu_epilogue(cuda):
+    import torch
+    X, W, b = _inputs(200, 300, 64, seed=9)
+    got = dense_device(torch, X, W, b, act=2, alpha=0.1)
+    ref = oracle.dense_f32(X, W, b, act=2, alpha=0.1)
+    assert max_err(got, ref) <= oracle.f32_bound(64, X, W)
+
+
+def test_precision_is_fp32_level(cuda):
+    """3xTF32 must be far tighter than 1xTF32: error vs float64 ~ f32 rounding."""
+    import torch
+    X, W, b = _inputs(512, 512, 4096, seed=11)
+    got = dense_device(torch, X, W, b, act=0)
+    exact = X.astype(np.float64) @ W.astype(np.float64) + b
+    err = float(np.max(np.abs(got - exact)))
+    # 1xTF32 gives ~1e-2 here; f32 FMA accumulation gives ~1e-5
+    assert err < 2e-4, err
+
+
+def test_relu_nan_and_signed_zero(cuda):
+    """arith.maximumf semantics: NaN propagates, -0 becomes +0."""
+    import torch
+    X = np.zeros((4, 8), np.float32)
+    W = np.zeros((8, 8), np.float32)
+    b = np.array([np.nan, -0.0, 0.0, -1.0, 1.0, np.inf, -np.inf, 2.5], np.float32)
+    got = dense_device(torch, X, W, b, act=1)
+    assert np.isnan(got[:, 0]).all()
+    assert (got[:, 1] == 0).all() and not np.signbit(got[:, 1]).any()
+    np.testing.assert_array_equal(got[:, 2:], np.tile([0, 0, 1, np.inf, 0, 2.5], (4, 1)))
+
+
+def test_nan_input_propagates(cuda):
+    import torch
+    X, W, b = _inputs(64, 64, 16, seed=3)
+    X[5, 3] = np.nan
+    got = dense_device(torch, X, W, b, act=1)
+    assert np.isnan(got[5]).all()
+    mask = np.ones(64, bool)
+    mask[5] = False
+    assert np.isfinite(got[mask]).all()
+
+
+@pytest.mark.parametrize("name", ["matmul_256", "dense_1024", "dense_ragged"])
+def test_benchmark_configs(cuda, name):
+    import torch
+    g = oracle.gen_config_inputs(name)
+    if "X" in g:
+        X, W, b, act = g["X"], g["W"], g["b"], 1
+    else:
+        X, W, b, act = g["A"], g["B"], None, 0
+    got = dense_device(torch, X, W, b, act=act)
+    ref = oracle.dense_f32(X, W, b, act=act)
+    assert max_err(got, ref) <= oracle.f32_bound(X.shape[1], X, W)
+
+
+def test_strided_views(cuda):
+    """Row pitches larger than the row length on every operand."""
+    import torch
+    dev = torch.device("cuda:0")
+    M, N, K = 150, 170, 90
+    X, W, b = _inputs(M, N, K, seed=21)
+    bigX = torch.zeros((M, K + 13), device=dev)
+    bigW = torch.zeros((K, N + 5), device=dev)
+    bigY = torch.full((M, N + 7), -7.0, device=dev)
+    bigX[:, :K] = torch.from_numpy(X).to(dev)
+    bigW[:, :N] = torch.from_numpy(W).to(dev)
+    tb = torch.from_numpy(b).to(dev)
+    L = _native.lib()
+    _native.check(L.b200_dense_f32(ptr(bigX), K + 13, ptr(bigW), N + 5, ptr(tb), ptr(bigY), N + 7,
+                                   M, N, K, 1, 0.0, stream_ptr(torch)))
+    _native.check(L.b200_stream_sync(stream_ptr(torch)))
+    out = bigY.cpu().numpy()
+    ref = oracle.dense_f32(X, W, b, act=1)
+    assert max_err(out[:, :N], ref) <= oracle.f32_bound(K, X, W)
+    assert (out[:, N:] == -7.0).all()  # padding columns untouched
+
+
+def test_k_zero_gives_bias(cuda):
+    import torch
+    dev = torch.device("cuda:0")
+    b = torch.tensor([-1.0, 2.0, -0.0], device=dev)
+    Y = torch.full((4, 3), 9.0, device=dev)
+    L = _native.lib()
+    _native.check(L.b200_dense_f32(None, 0, None, 3, ptr(b), ptr(Y), 3, 4, 3, 0, 1, 0.0,
+                                   stream_ptr(torch)))
+    _native.check(L.b200_stream_sync(stream_ptr(torch)))
+    np.testing.assert_array_equal(Y.cpu().numpy(), np.tile([0.0, 2.0, 0.0], (4, 1)))
+
+
+def test_host_api_pipelined_slabs(cuda):
+    """Host buffers through b200_dense_f32_host with enough rows to run the
+    slab pipeline (H2D / compute / D2H overlap)."""
+    M, N, K = 4608, 256, 2048
+    X, W, b = _inputs(M, N, K, seed=31)
+    Y = np.full((M, N), np.nan, np.float32)
+    L = _native.lib()
+    c = ctypes.c_void_p
+    _native.check(L.b200_dense_f32_host(c(X.ctypes.data), K, c(W.ctypes.data), N,
+                                        c(b.ctypes.data), c(Y.ctypes.data), N, M, N, K, 1, 0.0, 1))
+    ref = oracle.dense_f32(X, W, b, act=1)
+    assert max_err(Y, ref) <= oracle.f32_bound(K, X, W)
+
+
+def test_workspace_entry_point(cuda):
+    import torch
+    dev = torch.device("cuda:0")
+    M, N, K = 200, 300, 130
+    X, W, b = _inputs(M, N, K, seed=41)
+    L = _native.lib()
+    nbytes = L.b200_dense_f32_workspace_bytes(M, N, K)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    tX, tW, tb = (torch.from_numpy(a).to(dev) for a in (X, W, b))
+    tY = torch.empty((M, N), device=dev)
+    _native.check(L.b200_dense_f32_ws(ptr(tX), K, ptr(tW), N, ptr(tb), ptr(tY), N, M, N, K, 1, 0.0,
+                                      ptr(ws), nbytes, stream_ptr(torch)))
+    _native.check(L.b200_stream_sync(stream_ptr(torch)))
+    ref = oracle.dense_f32(X, W, b, act=1)
+    assert max_err(tY.cpu().numpy(), ref) <= oracle.f32_bound(K, X, W)
+    # too-small workspace is rejected with a clear error
+    with pytest.raises(_native.B200Error, match="workspace"):
+        _native.check(L.b200_dense_f32_ws(ptr(tX), K, ptr(tW), N, ptr(tb), ptr(tY), N, M, N, K, 1,
+                                          0.0, ptr(ws), nbytes - 1, stream_ptr(torch)))
+
+
+@pytest.mark.parametrize("name", ["matmul_4096", "matmul_8192"])
+def test_large_matmul_sampled_rows(cuda, name):
+    """Full-size cfg3 matmul on the GPU; the oracle checks 128 sampled rows
+    (each output row depends only on its X row, so sampling is exact)."""
+    import torch
+    g = oracle.gen_config_inputs(name)
+    A, B = g["A"], g["B"]
+    got = dense_device(torch, A, B, None, act=0)
+    rows = np.random.default_rng(0).choice(A.shape[0], 128, replace=False)
+    ref = oracle.dense_f32(A[rows], B)
+    err = max_err(got[rows], ref)
+    bound = oracle.f32_bound(A.shape[1], A, B)
+    assert err <= bound, (err, bound)
+    # fp32-level accuracy, not tf32-level
+    exact = A[rows].astype(np.float64) @ B.astype(np.float64)
+    assert float(np.max(np.abs(got[rows] - exact))) < bound / 10

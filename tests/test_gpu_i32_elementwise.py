@@ -1,0 +1,103 @@
+"""GPU parity of the i32 CUDA-core GEMM (bit-exact) and elementwise kernels."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle
+from gpu_util import ptr, stream_ptr
+from mlir_edsl import _native
+
+pytestmark = pytest.mark.gpu
+
+
+def _i32_device(torch, A, B, bias=None):
+    dev = torch.device("cuda:0")
+    tA, tB = torch.from_numpy(A).to(dev), torch.from_numpy(B).to(dev)
+    tb = torch.from_numpy(bias).to(dev) if bias is not None else None
+    M, K = A.shape
+    N = B.shape[1]
+    tC = torch.full((M, N), 12345, dtype=torch.int32, device=dev)
+    L = _native.lib()
+    _native.check(L.b200_matmul_i32(ptr(tA), K, ptr(tB), N, ptr(tb), ptr(tC), N, M, N, K,
+                                    stream_ptr(torch)))
+    _native.check(L.b200_stream_sync(stream_ptr(torch)))
+    return tC.cpu().numpy()
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (2, 2, 2), (7, 9, 13), (129, 130, 17),
+                                   (300, 257, 1000)])
+def test_i32_matches_oracle(cuda, M, N, K):
+    import torch
+    rng = np.random.default_rng(M + N + K)
+    A = rng.integers(-8, 9, (M, K), dtype=np.int32)
+    B = rng.integers(-8, 9, (K, N), dtype=np.int32)
+    np.testing.assert_array_equal(_i32_device(torch, A, B), oracle.matmul_i32(A, B))
+
+
+def test_i32_wraps_mod_2_32(cuda):
+    import torch
+    rng = np.random.default_rng(1)
+    A = rng.integers(-2**31, 2**31, (64, 96), dtype=np.int64).astype(np.int32)
+    B = rng.integers(-2**31, 2**31, (96, 80), dtype=np.int64).astype(np.int32)
+    bias = rng.integers(-2**31, 2**31, (80,), dtype=np.int64).astype(np.int32)
+    np.testing.assert_array_equal(_i32_device(torch, A, B, bias), oracle.matmul_i32(A, B, bias))
+
+
+def test_i32_2048_config(cuda):
+    import torch
+    g = oracle.gen_config_inputs("matmul_i32_2048")
+    np.testing.assert_array_equal(_i32_device(torch, g["A"], g["B"]),
+                                  oracle.matmul_i32(g["A"], g["B"]))
+
+
+def test_i32_identity_known_answer(cuda):
+    import torch
+    I = np.eye(2, dtype=np.int32)
+    B = np.array([[5, 6], [7, 8]], np.int32)
+    np.testing.assert_array_equal(_i32_device(torch, I, B), B)
+
+
+@pytest.mark.parametrize("act,alpha", [(0, 0.0), (1, 0.0), (2, 0.01), (2, 0.1)])
+@pytest.mark.parametrize("M,N", [(8, 16), (33, 17), (512, 1024)])
+def test_bias_act_f32(cuda, act, alpha, M, N):
+    import torch
+    dev = torch.device("cuda:0")
+    rng = np.random.default_rng(M * N)
+    X = rng.standard_normal((M, N)).astype(np.float32)
+    X[0, 0] = np.nan
+    X[-1, -1] = -0.0
+    b = rng.standard_normal(N).astype(np.float32)
+    tX, tb = torch.from_numpy(X).to(dev), torch.from_numpy(b).to(dev)
+    tY = torch.empty_like(tX)
+    L = _native.lib()
+    _native.check(L.b200_bias_act_f32(ptr(tX), N, ptr(tb), ptr(tY), N, M, N, act, alpha,
+                                      stream_ptr(torch)))
+    _native.check(L.b200_stream_sync(stream_ptr(torch)))
+    ref = oracle.bias_act_f32(X, b, act, alpha)
+    np.testing.assert_array_equal(tY.cpu().numpy(), ref)  # elementwise: bit-exact
+
+
+def test_act_f32_any_rank(cuda):
+    import torch
+    dev = torch.device("cuda:0")
+    X = np.linspace(-3, 3, 1001, dtype=np.float32)
+    tX = torch.from_numpy(X).to(dev)
+    tY = torch.empty_like(tX)
+    L = _native.lib()
+    _native.check(L.b200_act_f32(ptr(tX), ptr(tY), X.size, 1, 0.0, stream_ptr(torch)))
+    _native.check(L.b200_stream_sync(stream_ptr(torch)))
+    np.testing.assert_array_equal(tY.cpu().numpy(), np.where(X > 0, X, 0).astype(np.float32))
+
+
+def test_bias_add_i32_host(cuda):
+    rng = np.random.default_rng(3)
+    X = rng.integers(-2**31, 2**31, (20, 30), dtype=np.int64).astype(np.int32)
+    b = rng.integers(-2**31, 2**31, (30,), dtype=np.int64).astype(np.int32)
+    Y = np.empty_like(X)
+    c = ctypes.c_void_p
+    L = _native.lib()
+    _native.check(L.b200_bias_add_i32_host(c(X.ctypes.data), 30, c(b.ctypes.data),
+                                           c(Y.ctypes.data), 30, 20, 30))
+    np.testing.assert_array_equal(Y, (X.astype(np.int64) + b).astype(np.uint32).astype(np.int32)
+                                  if False else (X.view(np.uint32) + b.view(np.uint32)).view(np.int32))
