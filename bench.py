@@ -1,0 +1,437 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 dense-layer path (the driver's bench contract).
+
+Workload (the metric's multi-GPU config): the f32
+dense layer Y = relu(X @ W + b) with X[65536, 4096], W[4096, 4096], b[4096];
+rows of X/Y are split evenly across the N ranks (strong scaling), W and b
+are replicated, no collective on the data path. One step = one pass of the
+hot path over the rank's rows: tf32 hi/lo split of W and of the X rows, then
+the fused tcgen05 GEMM + bias + ReLU kernel.
+
+  value     TFLOP/s over all ranks (2*M*N*K per step), device-resident
+            inputs, CUDA events on the launching stream, max over ranks.
+  e2e       the same metric through the reference-facing plugin ABI
+            (b200_memref_dense_relu_f32, the flattened-memref signature of
+            ml-edsl's JIT'd functions) with pinned host buffers: every step
+            copies X-rows, W and b to the device and Y back inside the call.
+  roofline  the GEMM kernel alone (launched on pre-split operands) against
+            the 3xTF32-effective tensor peak = measured bf16 burst / 6.
+  cpu_baseline  (rank 0, N=1) the CPU oracle, a restatement of the reference's
+            CPU pipeline, on a bounded row sample of the same workload.
+  headline_8192 (N=1) the 8192^3 dense layer, device-resident.
+
+`--impl reference` times the reference's CPU pipeline restatement (oracle/)
+on all host cores on bounded row samples of the same workload; under
+torchrun only rank 0 runs it.
+
+Run: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "ml-edsl_b200"))
+sys.path.insert(0, ROOT)
+
+M_TOTAL, N_DIM, K_DIM = 65536, 4096, 4096
+METRIC = "TFLOP/s, f32 matmul+bias+ReLU at 8192^3 & M=65536 (1/2/4/8 B200), % roofline"
+UNIT = "TFLOP/s"
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-headline", action="store_true")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="rows per GPU override (small cases for profiling); 0 = 65536/N")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks / throttle reasons during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,"
+              "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.tmp = None
+
+    def start(self):
+        try:
+            self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.tmp.flush()
+        with open(self.tmp.name) as f:
+            rows = [r.split(",") for r in f.read().strip().splitlines() if r.strip()]
+        os.unlink(self.tmp.name)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        sm, mx, reasons, loaded = [], None, set(), 0
+        for r in rows:
+            r = [x.strip() for x in r]
+            if len(r) < 10:
+                continue
+            try:
+                clk, cmax, util = float(r[1]), float(r[2]), float(r[4])
+            except ValueError:
+                continue
+            mx = cmax
+            if util < 50:
+                continue
+            loaded += 1
+            sm.append(clk)
+            for name, val in zip(names, r[6:10]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples_under_load": loaded}
+
+
+# ----------------------------------------------------------------- CPU oracle timing
+_ORACLE_INPUTS = {}
+
+
+def _oracle_inputs(rows):
+    import numpy as np
+    have = _ORACLE_INPUTS.get("X")
+    if have is None or have.shape[0] < rows:
+        rng = np.random.default_rng(3)
+        _ORACLE_INPUTS["W"] = rng.uniform(-0.5, 0.5, (K_DIM, N_DIM)).astype(np.float32)
+        _ORACLE_INPUTS["b"] = rng.uniform(-0.5, 0.5, (N_DIM,)).astype(np.float32)
+        _ORACLE_INPUTS["X"] = rng.uniform(-0.5, 0.5, (max(rows, 64), K_DIM)).astype(np.float32)
+    return _ORACLE_INPUTS["X"][:rows], _ORACLE_INPUTS["W"], _ORACLE_INPUTS["b"]
+
+
+def time_oracle_rows(rows, threads, act=1):
+    """Times the CPU restatement of the reference pipeline on `rows` rows of
+    the workload; returns (seconds, flops)."""
+    import oracle
+    X, W, b = _oracle_inputs(rows)
+    t0 = time.perf_counter()
+    oracle.dense_f32(X, W, b, act=act, threads=threads)
+    dt = time.perf_counter() - t0
+    return dt, 2.0 * rows * N_DIM * K_DIM
+
+
+def calibrate_rows(target_s, threads):
+    """Row count whose oracle run takes about target_s seconds (multiple of 64)."""
+    probe = 64
+    dt, _ = time_oracle_rows(probe, threads)
+    rows = int(probe * target_s / max(dt, 1e-3))
+    return max(64, min(M_TOTAL, rows // 64 * 64))
+
+
+def run_reference(args):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return 0
+    import oracle
+    oracle.build()
+    cores = host_cores()
+    per_step = max(1.0, min(8.0, 150.0 / max(1, args.steps + args.warmup)))
+    rows = calibrate_rows(per_step, cores)
+    for _ in range(args.warmup):
+        time_oracle_rows(rows, cores)
+    times = []
+    for _ in range(args.steps):
+        dt, flops = time_oracle_rows(rows, cores)
+        times.append(dt)
+    total = sum(times)
+    value = 2.0 * rows * N_DIM * K_DIM * args.steps / total / 1e12
+    sample = (f"X[{rows},{K_DIM}] rows of the {M_TOTAL}-row workload @ W[{K_DIM},{N_DIM}] + b, "
+              f"relu; restatement of the reference CPU pipeline (64x64 tiles, k-ascending "
+              f"f32 fma), {cores} threads")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": total / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (np.random.default_rng(3), uniform[-0.5,0.5])",
+        "config": {"workload": "dense_relu X[65536,4096] @ W[4096,4096] + b (row sample)",
+                   "M_total": M_TOTAL, "N": N_DIM, "K": K_DIM, "rows_per_step": rows,
+                   "parallelism": "host threads"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------- B200 arm
+def run_b200(args):
+    import numpy as np
+    import torch
+    from mlir_edsl import _native
+
+    rank, local_rank, world = dist_env()
+    if world != args.gpus and world > 1:
+        print(f"WORLD_SIZE={world} but --gpus {args.gpus}", file=sys.stderr)
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    L = _native.lib()
+    rows = args.rows if args.rows > 0 else M_TOTAL // world
+    M, N, K = rows, N_DIM, K_DIM
+    g = torch.Generator(device=dev)
+    g.manual_seed(3 + 1000 * rank)
+    X = torch.rand((M, K), generator=g, device=dev) - 0.5
+    W = torch.rand((K, N), generator=g, device=dev) - 0.5
+    b = torch.rand((N,), generator=g, device=dev) - 0.5
+    Y = torch.empty((M, N), device=dev)
+    stream = torch.cuda.current_stream()
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+
+    def step():
+        _native.check(L.b200_dense_f32(P(X), K, P(W), N, P(b), P(Y), N, M, N, K, 1, 0.0, sp))
+
+    # ---- value: full step (split W, split X, GEMM), device-resident
+    for _ in range(args.warmup):
+        step()
+    _native.check(L.b200_stream_sync(sp))
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    launches0 = _native.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    barrier()
+    launches = _native.launch_count() - launches0
+    clocks = sampler.stop()
+    _native.check(L.b200_stream_sync(sp))
+    ms_local = e0.elapsed_time(e1)
+    ms_total = max_over_ranks(ms_local)
+    flops_step = 2.0 * M * N * K
+    value = world * flops_step * args.steps / (ms_total / 1e3) / 1e12
+
+    # ---- roofline: the GEMM kernel alone on pre-split operands
+    Kp = (K + 3) // 4 * 4
+    xhi = torch.empty((M, Kp), device=dev)
+    xlo = torch.empty_like(xhi)
+    whi = torch.empty((N, Kp), device=dev)
+    wlo = torch.empty_like(whi)
+    _native.check(L.b200_tf32_split_rows(P(X), K, M, K, P(xhi), P(xlo), sp))
+    _native.check(L.b200_tf32_split_transpose(P(W), N, K, N, P(whi), P(wlo), sp))
+
+    def gemm():
+        _native.check(L.b200_gemm_tf32x3_presplit(P(xhi), P(xlo), P(whi), P(wlo), P(b), P(Y), N,
+                                                  M, N, K, 1, 0.0, sp))
+
+    for _ in range(2):
+        gemm()
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        gemm()
+    e1.record(stream)
+    barrier()
+    _native.check(L.b200_stream_sync(sp))
+    gemm_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    bf16, peak_src = peaks()
+    peak = bf16 / 6.0
+    achieved = flops_step / (gemm_ms / 1e3) / 1e12
+    traffic = None
+    tfile = os.path.join(ROOT, "profiles", "gemm_tf32x3_dense65536_traffic.txt")
+    if os.path.exists(tfile):
+        for ln in open(tfile):
+            if ln.startswith("bytes_per_launch_rows_") and f"rows_{M}:" in ln:
+                traffic = float(ln.split(":")[1])
+    del xhi, xlo, whi, wlo
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "traffic": traffic,
+                "kernel": "gemm_tf32x3_kernel",
+                "peak_source": f"{peak_src} cuBLAS bf16 burst {bf16:.1f} TFLOP/s / 2 (tf32 "
+                               f"rate) / 3 (three MMAs per product) = 3xTF32-effective",
+                "kernel_ms": gemm_ms, "step_ms": ms_total / args.steps,
+                "kernel_share_of_step": gemm_ms / (ms_total / args.steps)}
+
+    # ---- e2e: plugin ABI with pinned host buffers, copies inside every step
+    e2e = None
+    if not args.no_e2e:
+        Xh = torch.empty((M, K), pin_memory=True)
+        Wh = torch.empty((K, N), pin_memory=True)
+        bh = torch.empty((N,), pin_memory=True)
+        Yh = torch.empty((M, N), pin_memory=True)
+        Xh.copy_(X)
+        Wh.copy_(W)
+        bh.copy_(b)
+        fn = L.b200_memref_dense_relu_f32
+        i64 = ctypes.c_int64
+        vp = ctypes.c_void_p
+        fn.argtypes = [vp, vp, i64, i64, i64, i64, i64] * 2 + [vp, vp, i64, i64, i64] + \
+                      [vp, vp, i64, i64, i64, i64, i64]
+        fn.restype = None
+        d2 = lambda t, r, c: [vp(t.data_ptr()), vp(t.data_ptr()), 0, r, c, c, 1]
+        call_args = d2(Xh, M, K) + d2(Wh, K, N) + [vp(bh.data_ptr()), vp(bh.data_ptr()), 0, N, 1] \
+            + d2(Yh, M, N)
+
+        def e2e_step():
+            fn(*call_args)
+            _native.check_last()
+
+        for _ in range(max(1, min(args.warmup, 2))):
+            e2e_step()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_step()
+        t_e2e = max_over_ranks(time.perf_counter() - t0)
+        # correctness of the e2e result against the device-resident path
+        step()
+        torch.cuda.synchronize()
+        assert torch.equal(Yh, Y.cpu()), "e2e result differs from device path"
+        e2e = {"value": world * flops_step * args.steps / t_e2e / 1e12, "unit": UNIT,
+               "h2d_bytes_per_step": (M * K + K * N + N) * 4, "d2h_bytes_per_step": M * N * 4,
+               "ms_per_step": t_e2e / args.steps * 1e3,
+               "api": "b200_memref_dense_relu_f32 (reference flattened-memref ABI), pinned host "
+                      "buffers, host wall clock, max over ranks"}
+        del Xh, Wh, bh, Yh
+
+    # ---- headline 8192^3 dense (N=1 only)
+    headline = None
+    if world == 1 and not args.no_headline:
+        del X, Y
+        torch.cuda.empty_cache()
+        n = 8192
+        g.manual_seed(2)
+        A = torch.rand((n, n), generator=g, device=dev) * 2 - 1
+        B = torch.rand((n, n), generator=g, device=dev) * 2 - 1
+        bb = torch.rand((n,), generator=g, device=dev) * 2 - 1
+        C = torch.empty((n, n), device=dev)
+
+        def hstep():
+            _native.check(L.b200_dense_f32(P(A), n, P(B), n, P(bb), P(C), n, n, n, n, 1, 0.0, sp))
+
+        for _ in range(args.warmup):
+            hstep()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            hstep()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        hms = e0.elapsed_time(e1) / args.steps
+        hval = 2.0 * n ** 3 / (hms / 1e3) / 1e12
+        headline = {"workload": "dense_relu 8192^3 (seed 2)", "value": hval, "unit": UNIT,
+                    "ms_per_step": hms, "frac_of_3xtf32_peak": hval / peak}
+        del A, B, bb, C
+
+    # ---- CPU baseline (rank 0, N=1)
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        import oracle
+        oracle.build()
+        cores = host_cores()
+        rows_s = calibrate_rows(10.0, cores)
+        dt, fl = time_oracle_rows(rows_s, cores)
+        cpu = {"value": fl / dt / 1e12, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"X[{rows_s},{K_DIM}] rows of the workload @ W + b, relu, one run "
+                         f"({dt:.1f} s); oracle/ref_linalg.c restatement of the reference CPU "
+                         f"pipeline"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_total / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (torch.Generator seed 3+1000*rank, uniform[-0.5,0.5])",
+            "config": {"workload": "dense_relu X[65536,4096] @ W[4096,4096] + b, rows split "
+                                   "across GPUs", "M_total": M_TOTAL, "N": N, "K": K,
+                       "rows_per_gpu": M, "parallelism": f"dp{world} (row shards, W/b "
+                                                         "replicated, no collective)",
+                       "l2": "inputs larger than L2 (X rows >= 128 MiB + W 64 MiB per GPU)",
+                       "precision": "3xTF32 tensor cores, f32 accumulation promoted every 128 "
+                                    "of K"},
+            "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
+            "gpu_launches": launches, "headline_8192": headline,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

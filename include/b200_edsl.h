@@ -118,10 +118,34 @@ int b200_bias_add_i32(const int32_t* X, int64_t ldx, const int32_t* b, int32_t* 
  * B200_ERR_CUDA. */
 int b200_stream_sync(void* stream);
 
+/* tf32 operand split used by the dense kernel, exposed so that a weight
+ * matrix can be split once and reused across calls:
+ *   b200_tf32_split_rows:      X[M,K] -> hi[M,Kp], lo[M,Kp]
+ *   b200_tf32_split_transpose: W[K,N] -> hiT[N,Kp], loT[N,Kp] (K-major)
+ * with Kp = K rounded up to a multiple of 4, x = hi + lo, hi and lo exact
+ * tf32 values (Inf/NaN travel in hi). Outputs must be 16-byte aligned. */
+int b200_tf32_split_rows(const float* X, int64_t ldx, int64_t M, int64_t K, float* hi, float* lo,
+                         void* stream);
+int b200_tf32_split_transpose(const float* W, int64_t ldw, int64_t K, int64_t N, float* hiT,
+                              float* loT, void* stream);
+
+/* Y = act(Xhi/Xlo @ WhiT/WloT^T + b) on pre-split operands (the tcgen05
+ * kernel alone). Same arithmetic as b200_dense_f32. */
+int b200_gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
+                              const float* wloT, const float* b, float* Y, int64_t ldy, int64_t M,
+                              int64_t N, int64_t K, int act, float alpha, void* stream);
+
+/* Device buffers on the current device (synchronous copies). */
+int b200_malloc(void** ptr, int64_t bytes);
+int b200_free(void* ptr);
+int b200_memcpy_h2d(void* dst, const void* src, int64_t bytes);
+int b200_memcpy_d2h(void* dst, const void* src, int64_t bytes);
+
 /* --------------------------------------------------- host-pointer entry points */
 
 /* Host buffers; synchronous. Rows of X/Y are sharded over `ndev` devices
- * (0 = default device count); W and b are replicated. Within a device the
+ * (0 = default device count; 1 = the calling thread's current device,
+ * otherwise devices 0..ndev-1); W and b are replicated. Within a device the
  * rows are processed in slabs so host->device copies, compute and
  * device->host copies overlap. */
 int b200_dense_f32_host(const float* X, int64_t ldx, const float* W, int64_t ldw, const float* b,

@@ -129,6 +129,7 @@ int get_ctx(int dev, DeviceCtx** out) {
 }
 
 int current_ctx(DeviceCtx** out) {
+  if (device_count() == 0) return fail(kErrNoDevice, "no CUDA device available");
   int dev = 0;
   B200_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   return get_ctx(dev, out);
@@ -305,7 +306,11 @@ int run_sharded(int ndev, int64_t M, Fn fn) {
     snprintf(buf, sizeof buf, "requested %d devices, %d available", ndev, avail);
     return fail(kErrInvalidArg, buf);
   }
-  if (ndev == 1) return fn(0, 0, M);
+  if (ndev == 1) {
+    int cur = 0;
+    B200_CUDA(cudaGetDevice(&cur), "cudaGetDevice");
+    return fn(cur, 0, M);
+  }
   std::vector<int> rcs(ndev, kOk);
   std::vector<std::string> errs(ndev);
   std::vector<std::thread> th;
@@ -363,10 +368,9 @@ template <class Launch>
 int elementwise_host(size_t in_bytes_x, const void* X, size_t in_bytes_b, const void* b,
                      size_t out_bytes, void* Y, Launch launch) {
   DeviceCtx* c = nullptr;
-  int rc = get_ctx(0, &c);
+  int rc = current_ctx(&c);
   if (rc) return rc;
   std::lock_guard<std::mutex> lk(c->mu);
-  B200_CUDA(cudaSetDevice(0), "cudaSetDevice");
   if (out_bytes == 0) return kOk;
   B200_CUDA(c->x[0].reserve(std::max<size_t>(in_bytes_x, 4)), "alloc X");
   B200_CUDA(c->bias.reserve(std::max<size_t>(in_bytes_b, 4)), "alloc b");
@@ -523,6 +527,70 @@ int b200_stream_sync(void* stream) {
   B200_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "stream sync");
   rc = check_device_status(c);
   return rc ? rc : succeed();
+}
+
+// ---------------------------------------------------------------- split / presplit
+int b200_tf32_split_rows(const float* X, int64_t ldx, int64_t M, int64_t K, float* hi, float* lo,
+                         void* stream) {
+  if (M < 0 || K < 0 || (M > 0 && K > 0 && (!X || !hi || !lo || ldx < K)))
+    return fail(kErrInvalidArg, "bad split_rows arguments");
+  if (M == 0 || K == 0) return succeed();
+  int rc = split_x_f32(X, ldx, M, K, hi, lo, static_cast<cudaStream_t>(stream));
+  return rc ? fail(rc, "split_rows launch failed") : succeed();
+}
+
+int b200_tf32_split_transpose(const float* W, int64_t ldw, int64_t K, int64_t N, float* hiT,
+                              float* loT, void* stream) {
+  if (N < 0 || K < 0 || (N > 0 && K > 0 && (!W || !hiT || !loT || ldw < N)))
+    return fail(kErrInvalidArg, "bad split_transpose arguments");
+  if (N == 0 || K == 0) return succeed();
+  int rc = split_w_f32(W, ldw, K, N, hiT, loT, static_cast<cudaStream_t>(stream));
+  return rc ? fail(rc, "split_transpose launch failed") : succeed();
+}
+
+int b200_gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
+                              const float* wloT, const float* b, float* Y, int64_t ldy, int64_t M,
+                              int64_t N, int64_t K, int act, float alpha, void* stream) {
+  int rc = validate_dense(xhi, K, whiT, N, Y, ldy, M, N, K, act);
+  if (rc) return rc;
+  if (M > 0 && N > 0 && K > 0 && (!xlo || !wloT)) return fail(kErrInvalidArg, "null lo operand");
+  for (const void* p : {(const void*)xhi, (const void*)xlo, (const void*)whiT, (const void*)wloT})
+    if (reinterpret_cast<uintptr_t>(p) & 15)
+      return fail(kErrInvalidArg, "split operands must be 16-byte aligned");
+  DeviceCtx* c = nullptr;
+  if ((rc = current_ctx(&c))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (M == 0 || N == 0) return succeed();
+  if (K == 0) rc = fill_bias_act_f32(b, Y, ldy, M, N, act, alpha, st);
+  else rc = gemm_tf32x3_presplit(xhi, xlo, whiT, wloT, M, N, K, b, Y, ldy, act, alpha, c->status, st);
+  return rc ? fail(rc, "gemm launch failed") : succeed();
+}
+
+// ---------------------------------------------------------------- device buffers
+int b200_malloc(void** ptr, int64_t bytes) {
+  if (!ptr || bytes < 0) return fail(kErrInvalidArg, "bad malloc arguments");
+  *ptr = nullptr;
+  if (bytes == 0) return succeed();
+  if (device_count() == 0) return fail(kErrNoDevice, "no CUDA device available");
+  B200_CUDA(cudaMalloc(ptr, (size_t)bytes), "cudaMalloc");
+  return succeed();
+}
+
+int b200_free(void* ptr) {
+  if (ptr) B200_CUDA(cudaFree(ptr), "cudaFree");
+  return succeed();
+}
+
+int b200_memcpy_h2d(void* dst, const void* src, int64_t bytes) {
+  if (bytes < 0) return fail(kErrInvalidArg, "negative size");
+  if (bytes) B200_CUDA(cudaMemcpy(dst, src, (size_t)bytes, cudaMemcpyHostToDevice), "H2D");
+  return succeed();
+}
+
+int b200_memcpy_d2h(void* dst, const void* src, int64_t bytes) {
+  if (bytes < 0) return fail(kErrInvalidArg, "negative size");
+  if (bytes) B200_CUDA(cudaMemcpy(dst, src, (size_t)bytes, cudaMemcpyDeviceToHost), "D2H");
+  return succeed();
 }
 
 // ---------------------------------------------------------------- host API

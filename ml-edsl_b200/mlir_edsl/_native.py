@@ -28,6 +28,8 @@ EXPORTED_SYMBOLS = [
     "b200_launch_count", "b200_set_default_devices", "b200_get_default_devices", "b200_release",
     "b200_dense_f32", "b200_dense_f32_workspace_bytes", "b200_dense_f32_ws", "b200_matmul_i32",
     "b200_bias_act_f32", "b200_act_f32", "b200_bias_add_i32", "b200_stream_sync",
+    "b200_tf32_split_rows", "b200_tf32_split_transpose", "b200_gemm_tf32x3_presplit",
+    "b200_malloc", "b200_free", "b200_memcpy_h2d", "b200_memcpy_d2h",
     "b200_dense_f32_host", "b200_matmul_i32_host", "b200_bias_act_f32_host",
     "b200_bias_add_i32_host", "b200_act_f32_host",
     "b200_memref_matmul_f32", "b200_memref_matmul_relu_f32", "b200_memref_dense_f32",
@@ -67,6 +69,14 @@ def _declare(lib):
         "b200_act_f32": ([vp, vp, i64, i32, f32, vp], i32),
         "b200_bias_add_i32": ([vp, i64, vp, vp, i64, i64, i64, vp], i32),
         "b200_stream_sync": ([vp], i32),
+        "b200_tf32_split_rows": ([vp, i64, i64, i64, vp, vp, vp], i32),
+        "b200_tf32_split_transpose": ([vp, i64, i64, i64, vp, vp, vp], i32),
+        "b200_gemm_tf32x3_presplit": ([vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i32, f32, vp],
+                                      i32),
+        "b200_malloc": ([c.POINTER(vp), i64], i32),
+        "b200_free": ([vp], i32),
+        "b200_memcpy_h2d": ([vp, vp, i64], i32),
+        "b200_memcpy_d2h": ([vp, vp, i64], i32),
         "b200_dense_f32_host": ([vp, i64, vp, i64, vp, vp, i64, i64, i64, i64, i32, f32, i32],
                                 i32),
         "b200_matmul_i32_host": ([vp, i64, vp, i64, vp, vp, i64, i64, i64, i64, i32], i32),

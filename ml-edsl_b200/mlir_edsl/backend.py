@@ -1,0 +1,257 @@
+"""B200 backend: the drop-in counterpart of the reference's CppMLIRBackend.
+
+Same method names and call shape as the reference (mlir_edsl/backend.py:105-271):
+compile_function_from_ast(name, params, return_type, ast_node),
+execute_function(name, *args), execute_gpu_function(name, *args),
+has_function, list_functions, clear_module, set_optimization_level,
+set_target, get_module_ir; get_backend() returns the process-wide instance.
+
+Execution of a compiled plan:
+  * a single fused step whose operands are all parameters calls the
+    library's memref-descriptor entry point with the reference's flattened
+    ctypes ABI (descriptor layout: backend.py:37-102 of the reference;
+    output descriptor appended last, void return);
+  * multi-step plans (stacked dense layers) run on the device through the
+    device-pointer entry points, intermediates never leave HBM;
+  * errors surface as the reference's exception types: TypeError for dtype
+    mismatches, ValueError for shapes, RuntimeError (B200Error) for device
+    failures.
+"""
+import ctypes
+from typing import Dict, List, Tuple, Union
+
+import numpy as np
+
+from . import _native
+from .lowering import ACT_LEAKY_RELU, ACT_NONE, ACT_RELU, Plan, Ref, lower
+from .types import ScalarType, TensorType, Type
+
+SCALAR_TYPE_TO_NUMPY_DTYPE = {ScalarType.F32: np.float32, ScalarType.I32: np.int32,
+                              ScalarType.I1: np.bool_}
+
+try:
+    HAS_B200_BACKEND = _native.lib() is not None
+except Exception:  # library not built: every call raises through _native.lib()
+    HAS_B200_BACKEND = False
+HAS_CPP_BACKEND = HAS_B200_BACKEND  # name used by reference-side code
+
+_global_backend = None
+
+
+def _memref_descriptor(data: np.ndarray, array_type: TensorType):
+    """(c_types, c_vals, buffer) of a standard MLIR memref descriptor:
+    alloc, aligned, offset, sizes..., strides... (zero-copy)."""
+    expected = SCALAR_TYPE_TO_NUMPY_DTYPE[array_type.element_type.kind]
+    if data.dtype != expected:
+        raise TypeError(f"ndarray dtype {data.dtype} does not match expected {np.dtype(expected)} "
+                        f"for {array_type}")
+    if not data.flags["C_CONTIGUOUS"]:
+        data = np.ascontiguousarray(data)
+    ptr = data.ctypes.data_as(ctypes.c_void_p)
+    nd = data.ndim
+    c_types = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64] + [ctypes.c_int64] * (2 * nd)
+    c_vals = [ptr, ptr, 0] + list(data.shape) + [s // data.itemsize for s in data.strides]
+    return c_types, c_vals, data
+
+
+def _output_descriptor(shape, dtype):
+    buf = np.empty(shape, dtype=dtype)
+    ptr = buf.ctypes.data_as(ctypes.c_void_p)
+    nd = len(shape)
+    strides = [1] * nd
+    for i in range(nd - 2, -1, -1):
+        strides[i] = strides[i + 1] * shape[i + 1]
+    c_types = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64] + [ctypes.c_int64] * (2 * nd)
+    return c_types, [ptr, ptr, 0] + list(shape) + strides, buf
+
+
+def _memref_symbol(step) -> Union[str, None]:
+    """The memref entry point implementing a single step, if one exists."""
+    if step.op == "gemm_f32":
+        if step.act == ACT_LEAKY_RELU:
+            return None
+        base = "dense" if step.has_bias else "matmul"
+        return f"b200_memref_{base}{'_relu' if step.act == ACT_RELU else ''}_f32"
+    if step.op == "gemm_i32":
+        return "b200_memref_dense_i32" if step.has_bias else "b200_memref_matmul_i32"
+    if step.op == "bias_act_f32" and len(step.shape) == 2:
+        if step.has_bias and step.act == ACT_NONE:
+            return "b200_memref_bias_add_f32"
+        if step.has_bias and step.act == ACT_RELU:
+            return "b200_memref_bias_relu_f32"
+        if not step.has_bias and step.act == ACT_RELU:
+            return "b200_memref_relu_f32"
+    return None
+
+
+class B200Backend:
+    """Compiles traced functions to B200 kernel plans and executes them."""
+
+    def __init__(self):
+        self._signatures: Dict[str, Tuple[List[Type], Type]] = {}
+        self._plans: Dict[str, Plan] = {}
+        self._target = "b200"
+        self._opt_level = 3
+        self.last_launches = 0  # kernels launched by the last execute_function
+
+    # ------------------------------------------------------------ compile
+    def compile_function_from_ast(self, name: str, params: list, return_type: Type,
+                                  ast_node) -> None:
+        plan = lower(ast_node, [n for n, _ in params])
+        self._plans[name] = plan
+        self._signatures[name] = ([t for _, t in params], return_type)
+
+    # ------------------------------------------------------------ execute
+    def execute_function(self, name: str, *args):
+        param_types, return_type = self._signatures[name]
+        plan = self._plans[name]
+        if not isinstance(return_type, TensorType):
+            raise RuntimeError(f"execute_function: b200 target returns tensors, got {return_type}")
+        arrays = []
+        for pt, val in zip(param_types, args):
+            expected = SCALAR_TYPE_TO_NUMPY_DTYPE[pt.element_type.kind]
+            if val.dtype != expected:
+                raise TypeError(f"ndarray dtype {val.dtype} does not match expected "
+                                f"{np.dtype(expected)} for {pt}")
+            arrays.append(np.ascontiguousarray(val))
+        before = _native.launch_count()
+        try:
+            if plan.output.kind == "param":
+                return arrays[plan.output.index].copy()
+            if len(plan.steps) == 1 and all(r.kind == "param" for r in plan.steps[0].inputs):
+                sym = _memref_symbol(plan.steps[0])
+                if sym is not None:
+                    return self._run_memref(sym, plan, param_types, arrays)
+            return self._run_device(plan, param_types, arrays)
+        finally:
+            self.last_launches = _native.launch_count() - before
+
+    execute_gpu_function = execute_function
+
+    def _run_memref(self, sym, plan, param_types, arrays):
+        step = plan.steps[0]
+        c_types, c_vals, live = [], [], []
+        for ref in step.inputs:
+            ct, cv, buf = _memref_descriptor(arrays[ref.index], param_types[ref.index])
+            c_types += ct
+            c_vals += cv
+            live.append(buf)
+        dtype = np.float32 if step.dtype == "f32" else np.int32
+        ct, cv, out = _output_descriptor(step.shape, dtype)
+        c_types += ct
+        c_vals += cv
+        fn_ptr = ctypes.cast(getattr(_native.lib(), sym), ctypes.c_void_p).value
+        ctypes.CFUNCTYPE(None, *c_types)(fn_ptr)(*c_vals)
+        _native.check_last()
+        return out
+
+    def _run_device(self, plan: Plan, param_types, arrays):
+        L = _native.lib()
+        buffers = []
+
+        def dmalloc(nbytes):
+            p = ctypes.c_void_p()
+            _native.check(L.b200_malloc(ctypes.byref(p), max(int(nbytes), 4)))
+            buffers.append(p)
+            return p
+
+        try:
+            dparams = {}
+            needed = {r.index for s in plan.steps for r in s.inputs if r.kind == "param"}
+            for i in sorted(needed):
+                a = arrays[i]
+                p = dmalloc(a.nbytes)
+                _native.check(L.b200_memcpy_h2d(p, a.ctypes.data_as(ctypes.c_void_p), a.nbytes))
+                dparams[i] = p
+            douts = []
+
+            def dref(r: Ref):
+                return dparams[r.index] if r.kind == "param" else douts[r.index]
+
+            def shape_of(r: Ref):
+                return arrays[r.index].shape if r.kind == "param" else plan.steps[r.index].shape
+
+            for s in plan.steps:
+                nelem = int(np.prod(s.shape))
+                out = dmalloc(nelem * 4)
+                douts.append(out)
+                if s.op in ("gemm_f32", "gemm_i32"):
+                    a, b = s.inputs[0], s.inputs[1]
+                    M, K = shape_of(a)
+                    N = shape_of(b)[1]
+                    bias = dref(s.inputs[2]) if s.has_bias else None
+                    if s.op == "gemm_f32":
+                        _native.check(L.b200_dense_f32(dref(a), K, dref(b), N, bias, out, N, M, N,
+                                                       K, s.act, s.alpha, None))
+                    else:
+                        _native.check(L.b200_matmul_i32(dref(a), K, dref(b), N, bias, out, N, M,
+                                                        N, K, None))
+                elif s.op == "bias_act_f32":
+                    x = s.inputs[0]
+                    bias = dref(s.inputs[1]) if s.has_bias else None
+                    if len(s.shape) == 2:
+                        M, N = s.shape
+                        _native.check(L.b200_bias_act_f32(dref(x), N, bias, out, N, M, N, s.act,
+                                                          s.alpha, None))
+                    else:
+                        _native.check(L.b200_act_f32(dref(x), out, nelem, s.act, s.alpha, None))
+                elif s.op == "bias_add_i32":
+                    M, N = s.shape
+                    _native.check(L.b200_bias_add_i32(dref(s.inputs[0]), N, dref(s.inputs[1]),
+                                                      out, N, M, N, None))
+                else:
+                    raise RuntimeError(f"unknown step {s.op}")
+            final = plan.steps[plan.output.index]
+            res = np.empty(final.shape, np.float32 if final.dtype == "f32" else np.int32)
+            _native.check(L.b200_stream_sync(None))
+            _native.check(L.b200_memcpy_d2h(res.ctypes.data_as(ctypes.c_void_p),
+                                            douts[plan.output.index], res.nbytes))
+            return res
+        finally:
+            for p in buffers:
+                L.b200_free(p)
+
+    # ------------------------------------------------------------ management
+    def has_function(self, name: str) -> bool:
+        return name in self._plans
+
+    def list_functions(self) -> List[str]:
+        return list(self._plans)
+
+    def get_module_ir(self) -> str:
+        """Textual form of every compiled plan (the b200 analogue of module IR)."""
+        return "\n\n".join(f"func @{n}:\n{p.describe()}" for n, p in self._plans.items())
+
+    def get_plan(self, name: str) -> Plan:
+        return self._plans[name]
+
+    def clear_module(self):
+        self._plans.clear()
+        self._signatures.clear()
+
+    def set_optimization_level(self, level: int):
+        if level not in (0, 2, 3):
+            raise ValueError(f"Invalid optimization level {level}. Must be 0, 2, or 3.")
+        self._opt_level = level  # kernels are precompiled; accepted for API parity
+
+    def set_target(self, target: str) -> None:
+        if target not in ("b200", "gpu"):
+            raise ValueError(f"Invalid target '{target}'. This backend implements 'b200' "
+                             "('gpu' is accepted as an alias); the reference CPU pipeline "
+                             "is not part of it.")
+        self._target = "b200"
+
+    @staticmethod
+    def set_default_devices(ndev: int):
+        """Number of GPUs the memref entry points shard rows over."""
+        _native.check(_native.lib().b200_set_default_devices(int(ndev)))
+
+
+def get_backend():
+    """The process-wide backend (None if the native library is missing)."""
+    global _global_backend
+    if not HAS_B200_BACKEND:
+        return None
+    if _global_backend is None:
+        _global_backend = B200Backend()
+    return _global_backend
