@@ -39,6 +39,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 #include "ptx.cuh"
 #include "kernels.h"
@@ -407,12 +408,16 @@ int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
                          const float* wloT, int64_t M, int64_t N, int64_t K, const float* bias,
                          float* Y, int64_t ldy, int act, float alpha, int* status,
                          cudaStream_t stream) {
-  static bool attr_set = false;  // per process; the attribute is per function
-  if (!attr_set) {
+  // The dynamic shared-memory opt-in is made once per device (thread-safe).
+  static std::atomic<uint64_t> attr_done{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return kErrCuda;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(attr_done.load() & bit)) {
     if (cudaFuncSetAttribute(gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemBytes) != cudaSuccess)
       return kErrCuda;
-    attr_set = true;
+    attr_done.fetch_or(bit);
   }
   const int64_t Kp = (K + 3) & ~int64_t(3);
   CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
