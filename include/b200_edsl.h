@@ -95,6 +95,23 @@ int b200_dense_f32_ws(const float* X, int64_t ldx, const float* W, int64_t ldw, 
                       float* Y, int64_t ldy, int64_t M, int64_t N, int64_t K, int act,
                       float alpha, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Y = act(X @ W + b) like b200_dense_f32, for callers that must not
+ * allocate device memory while they run (for example a serving process whose
+ * framework allocator already holds nearly all of HBM, or a latency-bound loop
+ * that cannot absorb cudaMalloc/cudaFree synchronisation). This entry point
+ * has no counterpart in the reference.
+ * The call allocates nothing: its scratch is a fixed 64 MiB device array that
+ * every GPU loading this library holds until the process exits. Problems
+ * needing more than that (8 * (M + N) * roundup(K, 4) bytes plus alignment)
+ * fail with B200_ERR_TOO_LARGE. All calls on a device share the array, so
+ * calls that overlap on the GPU race; the call synchronises `stream` before
+ * it returns. The first call on a device resolves the array's device address
+ * (cudaGetSymbolAddress with that device current); make that first call
+ * before any stream capture. */
+int b200_dense_f32_noalloc(const float* X, int64_t ldx, const float* W, int64_t ldw,
+                           const float* b, float* Y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                           int act, float alpha, void* stream);
+
 /* C = A @ B (+ bias) in i32, wrapping modulo 2^32 (arith.muli/addi).
  * Replaces: linalg.matmul on i32 (reference: cpp/src/builders/LinalgBuilder.cpp:106-139). */
 int b200_matmul_i32(const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb,

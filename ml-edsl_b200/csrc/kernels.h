@@ -22,6 +22,11 @@ enum Act : int { kActNone = 0, kActRelu = 1, kActLeakyRelu = 2 };
 // Number of kernels this library has launched (process-wide).
 void count_launch();
 
+// Records an error for b200_last_error()/b200_last_status() on this thread
+// and returns `code`; report_ok() records success and returns kOk.
+int report_error(int code, const char* msg);
+int report_ok();
+
 // ---- 3xTF32 GEMM (gemm_tf32x3.cu)
 int64_t dense_f32_workspace_bytes(int64_t M, int64_t N, int64_t K);
 int split_x_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xhi, float* xlo,
