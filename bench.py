@@ -232,15 +232,13 @@ def run_b200(args):
             dist.barrier()
         torch.cuda.synchronize()
 
+    from mlir_edsl.sharding import max_over_ranks as _max, row_shards
+
     def max_over_ranks(x):
-        if dist is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return _max(x, dist, dev)
 
     L = _native.lib()
-    rows = args.rows if args.rows > 0 else M_TOTAL // world
+    rows = args.rows if args.rows > 0 else row_shards(M_TOTAL, world)[rank][1]
     M, N, K = rows, N_DIM, K_DIM
     g = torch.Generator(device=dev)
     g.manual_seed(3 + 1000 * rank)
@@ -276,7 +274,8 @@ def run_b200(args):
     ms_local = e0.elapsed_time(e1)
     ms_total = max_over_ranks(ms_local)
     flops_step = 2.0 * M * N * K
-    value = world * flops_step * args.steps / (ms_total / 1e3) / 1e12
+    flops_job = (2.0 * M_TOTAL * N * K) if args.rows == 0 else world * flops_step
+    value = flops_job * args.steps / (ms_total / 1e3) / 1e12
 
     # ---- roofline: the GEMM kernel alone on pre-split operands
     Kp = (K + 3) // 4 * 4
@@ -354,7 +353,7 @@ def run_b200(args):
         step()
         torch.cuda.synchronize()
         assert torch.equal(Yh, Y.cpu()), "e2e result differs from device path"
-        e2e = {"value": world * flops_step * args.steps / t_e2e / 1e12, "unit": UNIT,
+        e2e = {"value": flops_job * args.steps / t_e2e / 1e12, "unit": UNIT,
                "h2d_bytes_per_step": (M * K + K * N + N) * 4, "d2h_bytes_per_step": M * N * 4,
                "ms_per_step": t_e2e / args.steps * 1e3,
                "api": "b200_memref_dense_relu_f32 (reference flattened-memref ABI), pinned host "

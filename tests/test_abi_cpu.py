@@ -1,0 +1,116 @@
+"""The C-ABI library without a GPU: it loads, exports every function
+include/*.h declares, validates arguments, and fails loudly (no fallback)."""
+import ctypes
+import glob
+import os
+import re
+
+import numpy as np
+import pytest
+
+from conftest import HAS_GPU, ROOT
+from mlir_edsl import _native
+
+HEADERS = glob.glob(os.path.join(ROOT, "include", "*.h"))
+
+
+def declared_functions():
+    names = set()
+    for h in HEADERS:
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        src = re.sub(r"#define[^\n]*(\\\n[^\n]*)*", "", src)
+        for m in re.finditer(r"\b(b200_[a-z0-9_]+)\s*\(", src):
+            names.add(m.group(1))
+    return names
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert "b200_dense_f32" in names and "b200_memref_dense_relu_f32" in names
+    assert len(names) >= 30
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _native.lib()
+    missing = [n for n in sorted(declared_functions()) if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_header():
+    assert declared_functions() == set(_native.EXPORTED_SYMBOLS)
+
+
+def test_version_and_counters():
+    lib = _native.lib()
+    assert b"sm_100a" in lib.b200_version()
+    assert lib.b200_launch_count() >= 0
+
+
+def test_workspace_formula():
+    lib = _native.lib()
+    M, N, K = 100, 50, 1001
+    Kp = 1004
+    al = lambda b: (b + 255) // 256 * 256
+    assert lib.b200_dense_f32_workspace_bytes(M, N, K) == 2 * al(M * Kp * 4) + 2 * al(N * Kp * 4)
+    assert lib.b200_dense_f32_workspace_bytes(-1, 2, 3) == -1
+
+
+def test_invalid_arguments_rejected_before_device_use():
+    lib = _native.lib()
+    rc = lib.b200_dense_f32(None, 4, None, 4, None, None, 4, -1, 4, 4, 1, 0.0, None)
+    assert rc == 1 and b"negative" in lib.b200_last_error()
+    rc = lib.b200_dense_f32_host(None, 4, None, 4, None, None, 4, 4, 4, 4, 7, 0.0, 1)
+    assert rc == 1 and b"activation" in lib.b200_last_error()
+    assert lib.b200_set_default_devices(0) == 1
+    assert lib.b200_set_default_devices(1) == 0 and lib.b200_get_default_devices() == 1
+
+
+def test_memref_entry_rejects_strided_innermost():
+    lib = _native.lib()
+    fn = lib.b200_memref_relu_f32
+    X = np.ones((2, 4), np.float32)
+    Y = np.empty((2, 4), np.float32)
+    vp = ctypes.c_void_p
+    i64 = ctypes.c_int64
+    fn.argtypes = [vp, vp, i64, i64, i64, i64, i64] * 2
+    fn.restype = None
+    fn(vp(X.ctypes.data), vp(X.ctypes.data), 0, 2, 2, 4, 2,   # innermost stride 2
+       vp(Y.ctypes.data), vp(Y.ctypes.data), 0, 2, 4, 4, 1)
+    assert lib.b200_last_status() == 1
+    assert b"innermost stride" in lib.b200_last_error()
+
+
+@pytest.mark.skipif(HAS_GPU, reason="checks the no-device error path")
+def test_no_device_fails_loudly():
+    lib = _native.lib()
+    assert lib.b200_device_count() == 0
+    X = np.ones((4, 4), np.float32)
+    c = ctypes.c_void_p(X.ctypes.data)
+    rc = lib.b200_dense_f32_host(c, 4, c, 4, None, c, 4, 4, 4, 4, 1, 0.0, 1)
+    assert rc == 4 and b"no CUDA device" in lib.b200_last_error()
+    assert lib.b200_dense_f32_noalloc(c, 4, c, 4, None, c, 4, 4, 4, 4, 1, 0.0, None) == 4
+
+
+@pytest.mark.skipif(HAS_GPU, reason="checks the no-device error path")
+def test_frontend_has_no_cpu_fallback():
+    from mlir_edsl import Tensor, f32, ml_function, relu
+
+    @ml_function(target="b200")
+    def dense(X: Tensor[f32, 4, 4], W: Tensor[f32, 4, 4], b: Tensor[f32, 4]) -> Tensor[f32, 4, 4]:
+        return relu(X @ W + b)
+    with pytest.raises(_native.B200Error, match="NO_DEVICE"):
+        dense(np.ones((4, 4), np.float32), np.ones((4, 4), np.float32), np.ones(4, np.float32))
+
+    @ml_function(target="b200")
+    def net(X: Tensor[f32, 4, 4], W: Tensor[f32, 4, 4]) -> Tensor[f32, 4, 4]:
+        return relu(relu(X @ W) @ W)
+    with pytest.raises(_native.B200Error, match="NO_DEVICE"):
+        net(np.ones((4, 4), np.float32), np.ones((4, 4), np.float32))
+
+
+def test_missing_library_raises(monkeypatch, tmp_path):
+    monkeypatch.setattr(_native, "_lib", None)
+    monkeypatch.setattr(_native, "LIB_PATH", str(tmp_path / "nope.so"))
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        _native.lib()
