@@ -101,7 +101,7 @@ class ClockSampler:
             self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=self.tmp, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -129,7 +129,7 @@ class ClockSampler:
             except ValueError:
                 continue
             mx = cmax
-            if util < 50:
+            if util < 20:
                 continue
             loaded += 1
             sm.append(clk)
@@ -253,13 +253,14 @@ def run_b200(args):
     def step():
         _native.check(L.b200_dense_f32(P(X), K, P(W), N, P(b), P(Y), N, M, N, K, 1, 0.0, sp))
 
-    # ---- value: full step (split W, split X, GEMM), device-resident
+    # ---- value: full step (split W, split X, GEMM), device-resident.
+    # Clocks are sampled from the warm-up through the GEMM-only loop below.
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.5)
     for _ in range(args.warmup):
         step()
     _native.check(L.b200_stream_sync(sp))
-    sampler = ClockSampler(local_rank)
-    sampler.start()
-    time.sleep(0.3)
     barrier()
     launches0 = _native.launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -269,7 +270,6 @@ def run_b200(args):
     e1.record(stream)
     barrier()
     launches = _native.launch_count() - launches0
-    clocks = sampler.stop()
     _native.check(L.b200_stream_sync(sp))
     ms_local = e0.elapsed_time(e1)
     ms_total = max_over_ranks(ms_local)
@@ -300,6 +300,12 @@ def run_b200(args):
     barrier()
     _native.check(L.b200_stream_sync(sp))
     gemm_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    # keep the GPU busy long enough for several clock samples, then stop
+    t_soak = time.perf_counter()
+    while time.perf_counter() - t_soak < 1.0:
+        gemm()
+        torch.cuda.synchronize()
+    clocks = sampler.stop()
     bf16, peak_src = peaks()
     peak = bf16 / 6.0
     achieved = flops_step / (gemm_ms / 1e3) / 1e12

@@ -28,7 +28,9 @@
 //
 // Main kernel (one 128 x 256 output tile per CTA, 320 threads):
 //   warp 0      TMA producer: 4 tiles (A_hi, A_lo, B_hi, B_lo) per k-block
-//               into a 2-stage shared-memory ring (96 KB per stage).
+//               into a shared-memory ring: 4 stages of 48 KB (BK = 16,
+//               64-byte swizzle) by default; a 2 x 96 KB ring (BK = 32,
+//               128-byte swizzle) is kept for comparison (B200_GEMM_RING).
 //   warp 1      allocates 512 TMEM columns (2 chunk buffers); lane 0 issues 3
 //               tcgen05.mma per 8-wide k-step and frees ring stages and chunk
 //               buffers with tcgen05.commit.
@@ -40,6 +42,8 @@
 #include <cuda_runtime.h>
 #include <algorithm>
 #include <atomic>
+#include <cstdlib>
+#include <cstring>
 #include <cstdint>
 #include "ptx.cuh"
 #include "kernels.h"
@@ -48,21 +52,35 @@ namespace b200 {
 
 constexpr int kBM = 128;
 constexpr int kBN = 256;
-constexpr int kBK = 32;  // 32 floats = 128 B rows = one SWIZZLE_128B atom row
-constexpr int kStages = 2;
-constexpr int kATileBytes = kBM * kBK * 4;                      // 16 KB
-constexpr int kBTileBytes = kBN * kBK * 4;                      // 32 KB
-constexpr int kStageBytes = 2 * kATileBytes + 2 * kBTileBytes;  // 96 KB
-constexpr int kChunkKB = 4;   // k-blocks (K = 128) per TMEM partial-sum chunk
 constexpr int kEpiWarps = 8;  // 2 warps per TMEM lane quarter, one per column half
 constexpr int kTmemCols = 2 * kBN;  // two chunk accumulators of 128 x 256 f32
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kGroupM = 16;  // tile raster: 16 M-tiles share each N sweep
+constexpr int kChunkK = 128;  // K per TMEM partial-sum chunk
 
-// Shared memory: [ring stages][barriers/flags][bias tile], base aligned to 1 KB.
-constexpr int kBarOffset = kStages * kStageBytes;
-constexpr int kBiasOffset = kBarOffset + 256;  // 2*S + 4 barriers, slot, flag
-constexpr int kSmemBytes = kBiasOffset + kBN * 4 + 1024;  // + alignment slack
+// Shared-memory ring configuration. BK floats of K per stage; the rows of
+// each operand tile are BK*4 bytes, which selects the TMA / UMMA swizzle:
+// 128 B rows -> SWIZZLE_128B (UMMA layout 2), 64 B rows -> SWIZZLE_64B (4).
+// Layout: [Stages x (A_hi, A_lo, B_hi, B_lo)][barriers/flags][bias tile],
+// base aligned to 1 KB.
+template <int BK_, int STAGES_>
+struct RingCfg {
+  static constexpr int BK = BK_;
+  static constexpr int Stages = STAGES_;
+  static constexpr int ATileBytes = kBM * BK * 4;
+  static constexpr int BTileBytes = kBN * BK * 4;
+  static constexpr int StageBytes = 2 * ATileBytes + 2 * BTileBytes;
+  static constexpr int ChunkKB = kChunkK / BK;  // k-blocks per TMEM chunk
+  static constexpr uint32_t UmmaLayout = BK == 32 ? 2u : 4u;
+  static constexpr uint32_t SBO = 8 * BK * 4;  // 8-row core-matrix group stride
+  static constexpr int BarOffset = Stages * StageBytes;
+  static constexpr int BiasOffset = BarOffset + 256;
+  static constexpr int SmemBytes = BiasOffset + kBN * 4 + 1024;  // + alignment slack
+  static_assert(BK == 32 || BK == 16, "BK must be 32 (SW128) or 16 (SW64)");
+  static_assert(SmemBytes <= 232448, "shared memory over the sm_100 limit");
+};
+using CfgBK32S2 = RingCfg<32, 2>;  // 2 stages of 96 KB
+using CfgBK16S4 = RingCfg<16, 4>;  // 4 stages of 48 KB
 
 __device__ __forceinline__ void tf32_split(float x, float& h, float& l) {
   const uint32_t u = __float_as_uint(x);
@@ -159,6 +177,7 @@ struct Epilogue {
   int vec_out;  // Y base 16-byte aligned and ldy % 4 == 0
 };
 
+template <class Cfg>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAhi,
                        const __grid_constant__ CUtensorMap tmAlo,
@@ -168,13 +187,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBarOffset);  // TMA -> MMA
-  uint64_t* empty = full + kStages;                                   // MMA -> TMA
-  uint64_t* tfull = empty + kStages;   // MMA -> epilogue: chunk accumulator ready
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::BarOffset);  // TMA -> MMA
+  uint64_t* empty = full + Cfg::Stages;                                   // MMA -> TMA
+  uint64_t* tfull = empty + Cfg::Stages;   // MMA -> epilogue: chunk accumulator ready
   uint64_t* tempty = tfull + 2;        // epilogue -> MMA: chunk accumulator drained
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* sbias = reinterpret_cast<float*>(smem + kBiasOffset);
+  float* sbias = reinterpret_cast<float*>(smem + Cfg::BiasOffset);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -189,10 +208,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tile_n = in_group / group_rows;
   const int m0 = tile_m * kBM;
   const int n0 = tile_n * kBN;
-  const int num_chunks = (num_kb + kChunkKB - 1) / kChunkKB;
+  const int num_chunks = (num_kb + Cfg::ChunkKB - 1) / Cfg::ChunkKB;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < Cfg::Stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -225,18 +244,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
       for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % kStages;
-        const int round = kb / kStages;
+        const int s = kb % Cfg::Stages;
+        const int round = kb / Cfg::Stages;
         if (round > 0 &&
             !mbar_wait(&empty[s], (round - 1) & 1, status, kDevTimeoutEmpty, abort_flag))
           break;
-        uint8_t* st = smem + s * kStageBytes;
-        mbar_arrive_expect_tx(&full[s], kStageBytes);
-        const int kx = kb * kBK;
+        uint8_t* st = smem + s * Cfg::StageBytes;
+        mbar_arrive_expect_tx(&full[s], Cfg::StageBytes);
+        const int kx = kb * Cfg::BK;
         tma_load_2d(st, &tmAhi, &full[s], kx, m0);
-        tma_load_2d(st + kATileBytes, &tmAlo, &full[s], kx, m0);
-        tma_load_2d(st + 2 * kATileBytes, &tmBhi, &full[s], kx, n0);
-        tma_load_2d(st + 2 * kATileBytes + kBTileBytes, &tmBlo, &full[s], kx, n0);
+        tma_load_2d(st + Cfg::ATileBytes, &tmAlo, &full[s], kx, m0);
+        tma_load_2d(st + 2 * Cfg::ATileBytes, &tmBhi, &full[s], kx, n0);
+        tma_load_2d(st + 2 * Cfg::ATileBytes + Cfg::BTileBytes, &tmBlo, &full[s], kx, n0);
       }
     }
   } else if (warp == 1) {
@@ -244,12 +263,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_tf32_f32(kBM, kBN);
       for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % kStages;
-        const int round = kb / kStages;
-        const int chunk = kb / kChunkKB;
+        const int s = kb % Cfg::Stages;
+        const int round = kb / Cfg::Stages;
+        const int chunk = kb / Cfg::ChunkKB;
         const int buf = chunk & 1;
-        const bool chunk_start = (kb % kChunkKB) == 0;
-        const bool chunk_end = (kb % kChunkKB) == kChunkKB - 1 || kb == num_kb - 1;
+        const bool chunk_start = (kb % Cfg::ChunkKB) == 0;
+        const bool chunk_end = (kb % Cfg::ChunkKB) == Cfg::ChunkKB - 1 || kb == num_kb - 1;
         if (chunk_start && chunk >= 2) {
           if (!mbar_wait(&tempty[buf], ((chunk >> 1) - 1) & 1, status, kDevTimeoutAccum,
                          abort_flag))
@@ -259,13 +278,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&full[s], round & 1, status, kDevTimeoutFull, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * kBN;
-        const uint32_t st = smem_u32(smem + s * kStageBytes);
+        const uint32_t st = smem_u32(smem + s * Cfg::StageBytes);
 #pragma unroll
-        for (int k = 0; k < kBK / 8; ++k) {  // tf32 UMMA consumes K = 8 (32 B)
-          const uint64_t a_hi = umma_desc_k_sw128(st + k * 32);
-          const uint64_t a_lo = umma_desc_k_sw128(st + kATileBytes + k * 32);
-          const uint64_t b_hi = umma_desc_k_sw128(st + 2 * kATileBytes + k * 32);
-          const uint64_t b_lo = umma_desc_k_sw128(st + 2 * kATileBytes + kBTileBytes + k * 32);
+        for (int k = 0; k < Cfg::BK / 8; ++k) {  // tf32 UMMA consumes K = 8 (32 B)
+          const uint64_t a_hi = umma_desc_k<Cfg::UmmaLayout, Cfg::SBO>(st + k * 32);
+          const uint64_t a_lo = umma_desc_k<Cfg::UmmaLayout, Cfg::SBO>(st + Cfg::ATileBytes + k * 32);
+          const uint64_t b_hi = umma_desc_k<Cfg::UmmaLayout, Cfg::SBO>(st + 2 * Cfg::ATileBytes + k * 32);
+          const uint64_t b_lo = umma_desc_k<Cfg::UmmaLayout, Cfg::SBO>(st + 2 * Cfg::ATileBytes + Cfg::BTileBytes + k * 32);
           umma_tf32(d_tmem, a_lo, b_hi, idesc, (chunk_start && k == 0) ? 0u : 1u);
           umma_tf32(d_tmem, a_hi, b_lo, idesc, 1u);
           umma_tf32(d_tmem, a_hi, b_hi, idesc, 1u);
@@ -360,18 +379,19 @@ static EncodeTiledFn get_encode_fn() {
 }
 
 // 2-D f32 tensor map: `rows` rows of `cols` valid floats, row pitch `pitch`
-// floats (multiple of 4), box = box_rows x 32 floats, 128-byte swizzle.
-// Coordinates beyond `cols` / `rows` read as zero.
+// floats (multiple of 4), box = box_rows x bk floats, swizzle matching the
+// bk*4-byte row. Coordinates beyond `cols` / `rows` read as zero.
 static int make_tmap(CUtensorMap* map, const float* base, int64_t cols, int64_t rows,
-                     int64_t pitch, int box_rows) {
+                     int64_t pitch, int box_rows, int bk) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return kErrDriver;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)pitch * 4};
-  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  cuuint32_t box[2] = {(cuuint32_t)bk, (cuuint32_t)box_rows};
+  const CUtensorMapSwizzle swz = bk == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
-                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? kOk : kErrDriver;
 }
@@ -404,28 +424,52 @@ int split_x_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xhi, f
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
-int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
-                         const float* wloT, int64_t M, int64_t N, int64_t K, const float* bias,
-                         float* Y, int64_t ldy, int act, float alpha, int* status,
-                         cudaStream_t stream) {
+// Ring configuration used by gemm_tf32x3_presplit. B200_GEMM_RING=bk32s2
+// selects the 2 x 96 KB ring (kept for A/B measurements); default 4 x 48 KB.
+static int ring_variant() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("B200_GEMM_RING");
+    v = (e && strcmp(e, "bk32s2") == 0) ? 0 : 1;
+  }
+  return v;
+}
+
+template <class Cfg>
+static int launch_gemm(const float* xhi, const float* xlo, const float* whiT, const float* wloT,
+                       int64_t M, int64_t N, int64_t K, const Epilogue& ep, int* status,
+                       cudaStream_t stream) {
   // The dynamic shared-memory opt-in is made once per device (thread-safe).
   static std::atomic<uint64_t> attr_done{0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return kErrCuda;
   const uint64_t bit = 1ull << (dev & 63);
   if (!(attr_done.load() & bit)) {
-    if (cudaFuncSetAttribute(gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSmemBytes) != cudaSuccess)
+    if (cudaFuncSetAttribute(gemm_tf32x3_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cfg::SmemBytes) != cudaSuccess)
       return kErrCuda;
     attr_done.fetch_or(bit);
   }
   const int64_t Kp = (K + 3) & ~int64_t(3);
   CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
-  int rc = make_tmap(&ta_hi, xhi, K, M, Kp, kBM);
-  if (rc == kOk) rc = make_tmap(&ta_lo, xlo, K, M, Kp, kBM);
-  if (rc == kOk) rc = make_tmap(&tb_hi, whiT, K, N, Kp, kBN);
-  if (rc == kOk) rc = make_tmap(&tb_lo, wloT, K, N, Kp, kBN);
+  int rc = make_tmap(&ta_hi, xhi, K, M, Kp, kBM, Cfg::BK);
+  if (rc == kOk) rc = make_tmap(&ta_lo, xlo, K, M, Kp, kBM, Cfg::BK);
+  if (rc == kOk) rc = make_tmap(&tb_hi, whiT, K, N, Kp, kBN, Cfg::BK);
+  if (rc == kOk) rc = make_tmap(&tb_lo, wloT, K, N, Kp, kBN, Cfg::BK);
   if (rc != kOk) return rc;
+  const int tiles_m = (int)((M + kBM - 1) / kBM);
+  const int tiles_n = (int)((N + kBN - 1) / kBN);
+  const int num_kb = (int)((K + Cfg::BK - 1) / Cfg::BK);
+  gemm_tf32x3_kernel<Cfg><<<tiles_m * tiles_n, kThreads, Cfg::SmemBytes, stream>>>(
+      ta_hi, ta_lo, tb_hi, tb_lo, num_kb, tiles_m, tiles_n, ep, status);
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
+                         const float* wloT, int64_t M, int64_t N, int64_t K, const float* bias,
+                         float* Y, int64_t ldy, int act, float alpha, int* status,
+                         cudaStream_t stream) {
   Epilogue ep;
   ep.Y = Y;
   ep.ldy = ldy;
@@ -435,13 +479,9 @@ int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
   ep.act = act;
   ep.alpha = alpha;
   ep.vec_out = ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(Y) & 15) == 0);
-  const int tiles_m = (int)((M + kBM - 1) / kBM);
-  const int tiles_n = (int)((N + kBN - 1) / kBN);
-  const int num_kb = (int)((K + kBK - 1) / kBK);
-  gemm_tf32x3_kernel<<<tiles_m * tiles_n, kThreads, kSmemBytes, stream>>>(
-      ta_hi, ta_lo, tb_hi, tb_lo, num_kb, tiles_m, tiles_n, ep, status);
-  count_launch();
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  if (ring_variant() == 0)
+    return launch_gemm<CfgBK32S2>(xhi, xlo, whiT, wloT, M, N, K, ep, status, stream);
+  return launch_gemm<CfgBK16S4>(xhi, xlo, whiT, wloT, M, N, K, ep, status, stream);
 }
 
 }  // namespace b200

@@ -120,16 +120,19 @@ __device__ __forceinline__ void tc_fence_after() {
 
 // ---------------------------------------------------------------- UMMA
 // Shared-memory matrix descriptor for a K-major operand tile written by TMA
-// with 128-byte swizzling: rows of 128 B, 8-row core groups 1024 B apart.
-// Bit layout (sm_100 "version 1" descriptor): [0,14) start>>4, [16,30) LBO>>4,
-// [32,46) SBO>>4, [46,48) version=1, [49,52) base offset, [61,64) layout.
-__device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t smem_addr) {
+// with a 128- or 64-byte swizzle (rows of 128 B or 64 B; 8-row core groups
+// SBO bytes apart). Bit layout (sm_100 "version 1" descriptor): [0,14)
+// start>>4, [16,30) LBO>>4, [32,46) SBO>>4, [46,48) version=1, [49,52) base
+// offset, [61,64) layout (2 = SWIZZLE_128B, 4 = SWIZZLE_64B). Within a row,
+// successive K-steps are addressed by advancing the start address.
+template <uint32_t kLayout, uint32_t kSBO>
+__device__ __forceinline__ uint64_t umma_desc_k(uint32_t smem_addr) {
   uint64_t d = 0;
   d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
   d |= (uint64_t)1 << 16;                 // LBO (unused for swizzled K-major)
-  d |= (uint64_t)(1024 >> 4) << 32;       // SBO: 8 rows x 128 B
+  d |= (uint64_t)(kSBO >> 4) << 32;       // SBO: 8 rows
   d |= (uint64_t)1 << 46;                 // descriptor version for sm_100
-  d |= (uint64_t)2 << 61;                 // SWIZZLE_128B
+  d |= (uint64_t)kLayout << 61;
   return d;
 }
 
