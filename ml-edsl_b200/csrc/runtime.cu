@@ -72,7 +72,7 @@ struct DevBuf {
   }
 };
 
-constexpr int kRing = 2;  // slab buffers in flight per device
+constexpr int kRing = 3;  // slab buffers in flight per device
 
 struct DeviceCtx {
   int dev = -1;
@@ -208,7 +208,9 @@ int validate_dense(const void* X, int64_t ldx, const void* W, int64_t ldw, const
 }
 
 // One device's share of a host-pointer dense call: rows [0, M) of the given
-// host views. H2D of slab i+1, compute of slab i and D2H of slab i-1 overlap.
+// host views, processed in row slabs through a kRing-slot ring of device
+// buffers on three streams, so the copy-in of slab i+1, the compute of slab i
+// and the copy-out of slab i-1 overlap.
 int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, int64_t ldw,
                          const float* b, float* Y, int64_t ldy, int64_t M, int64_t N, int64_t K,
                          int act, float alpha) {
@@ -220,10 +222,17 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
   if (M == 0 || N == 0) return kOk;
   const int64_t Kp = round_up(std::max<int64_t>(K, 1), 4);
 
-  // Slab size: one slab for small calls, else ~8 slabs of >= 1024 rows.
+  // Slab size: one slab for small calls, else B200_HOST_SLABS (default 16)
+  // slabs of >= 512 rows, so the first copy-in and the last copy-out that
+  // cannot overlap anything are short.
   int64_t slab = M;
-  if (M * K * 4 >= ((int64_t)32 << 20) && M >= 2048)
-    slab = std::max<int64_t>(1024, round_up((M + 7) / 8, 128));
+  if (M * K * 4 >= ((int64_t)32 << 20) && M >= 1024) {
+    static const int64_t nslabs_cfg = [] {
+      const char* e = getenv("B200_HOST_SLABS");
+      return (int64_t)((e && atoi(e) > 0) ? atoi(e) : 16);
+    }();
+    slab = std::max<int64_t>(512, round_up((M + nslabs_cfg - 1) / nslabs_cfg, 128));
+  }
   const int64_t nslab = (M + slab - 1) / slab;
 
   // Weights (replicated): upload + split once per call on the compute stream.
@@ -260,13 +269,16 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
     const int64_t rows = std::min(slab, M - r0);
     float* dX = static_cast<float*>(c->x[slot].p);
     float* dY = static_cast<float*>(c->y[slot].p);
-    if (i >= kRing) B200_CUDA(cudaStreamWaitEvent(c->s_h2d, c->ev_d2h[slot], 0), "wait");
+    // Slot reuse: the copy-in may overwrite X once slab i-kRing's compute has
+    // read it; the compute may overwrite Y once slab i-kRing's copy-out is done.
+    if (i >= kRing) B200_CUDA(cudaStreamWaitEvent(c->s_h2d, c->ev_comp[slot], 0), "wait");
     if (K > 0)
       B200_CUDA(cudaMemcpy2DAsync(dX, K * 4, X + r0 * ldx, ldx * 4, K * 4, rows,
                                   cudaMemcpyHostToDevice, c->s_h2d),
                 "H2D X");
     B200_CUDA(cudaEventRecord(c->ev_h2d[slot], c->s_h2d), "record");
     B200_CUDA(cudaStreamWaitEvent(c->s_comp, c->ev_h2d[slot], 0), "wait");
+    if (i >= kRing) B200_CUDA(cudaStreamWaitEvent(c->s_comp, c->ev_d2h[slot], 0), "wait");
     if (K == 0) {
       rc = fill_bias_act_f32(db, dY, N, rows, N, act, alpha, c->s_comp);
     } else {
