@@ -55,6 +55,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-headline", action="store_true")
+    ap.add_argument("--configs", action="store_true",
+                    help="measure every BASELINE.json config on one GPU, one JSON line each")
     ap.add_argument("--rows", type=int, default=0,
                     help="rows per GPU override (small cases for profiling); 0 = 65536/N")
     return ap.parse_args()
@@ -431,8 +433,93 @@ def run_b200(args):
     return 0
 
 
+
+# ----------------------------------------------------------------- per-config table
+def run_configs(args):
+    """Device-resident timing of every BASELINE.json configuration on GPU 0
+    (parity for each is covered by tests/); one JSON line per config."""
+    import torch
+    from mlir_edsl import _native
+    L = _native.lib()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream()
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    P = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None
+    bf16, _ = peaks()
+    peak = bf16 / 6.0
+    g = torch.Generator(device=dev)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        _native.check(L.b200_stream_sync(sp))
+        return e0.elapsed_time(e1) / args.steps
+
+    def u(shape, seed, lo=-1.0, hi=1.0):
+        g.manual_seed(seed)
+        return torch.rand(shape, generator=g, device=dev) * (hi - lo) + lo
+
+    def dense(X, W, b, Y, act):
+        M, K = X.shape
+        N = W.shape[1]
+        _native.check(L.b200_dense_f32(P(X), K, P(W), N, P(b), P(Y), N, M, N, K, act, 0.0, sp))
+
+    def emit(name, ms, flops=None, nbytes=None):
+        line = {"config": name, "ms": ms}
+        if flops:
+            line.update({"TFLOP/s": flops / ms / 1e9, "frac_of_3xtf32_peak": flops / ms / 1e9 / peak})
+        if nbytes:
+            line["GB/s"] = nbytes / ms / 1e6
+        print(json.dumps(line), flush=True)
+
+    for name, (M, N, K), act, with_b, seed, lo in [
+            ("matmul_256", (256, 256, 256), 0, False, 0, -1.0),
+            ("dense_1024", (1024, 1024, 1024), 1, True, 1, -1.0),
+            ("matmul_4096", (4096, 4096, 4096), 0, False, 2, -1.0),
+            ("matmul_8192", (8192, 8192, 8192), 0, False, 2, -1.0),
+            ("dense_65536", (65536, 4096, 4096), 1, True, 3, -0.5),
+            ("dense_ragged", (1000, 999, 1001), 1, True, 4, -1.0)]:
+        X, W = u((M, K), seed, lo, -lo), u((K, N), seed + 100, lo, -lo)
+        b = u((N,), seed + 200, lo, -lo) if with_b else None
+        Y = torch.empty((M, N), device=dev)
+        emit(name, timed(lambda: dense(X, W, b, Y, act)), flops=2.0 * M * N * K)
+        del X, W, b, Y
+    # 2-layer MLP: relu(relu(X@W1+b1)@W2+b2), hidden activation stays in HBM
+    X, W1, b1 = u((512, 4096), 4), u((4096, 11008), 5), u((11008,), 6)
+    W2, b2 = u((11008, 4096), 7), u((4096,), 8)
+    H, Y = torch.empty((512, 11008), device=dev), torch.empty((512, 4096), device=dev)
+    emit("mlp_2layer", timed(lambda: (dense(X, W1, b1, H, 1), dense(H, W2, b2, Y, 1))),
+         flops=2.0 * 512 * 4096 * 11008 * 2)
+    del X, W1, b1, W2, b2, H, Y
+    # i32 2048^3 on the CUDA cores
+    g.manual_seed(2)
+    A = torch.randint(-8, 9, (2048, 2048), generator=g, device=dev, dtype=torch.int32)
+    B = torch.randint(-8, 9, (2048, 2048), generator=g, device=dev, dtype=torch.int32)
+    C = torch.empty_like(A)
+    ms = timed(lambda: _native.check(L.b200_matmul_i32(P(A), 2048, P(B), 2048, None, P(C), 2048,
+                                                      2048, 2048, 2048, sp)))
+    print(json.dumps({"config": "matmul_i32_2048", "ms": ms,
+                      "Tint-op/s": 2.0 * 2048 ** 3 / ms / 1e9}), flush=True)
+    # unfused elementwise bias+relu over the cfg4 output shape (HBM-bound)
+    Xe, be = u((65536, 4096), 9), u((4096,), 10)
+    Ye = torch.empty_like(Xe)
+    ms = timed(lambda: _native.check(L.b200_bias_act_f32(P(Xe), 4096, P(be), P(Ye), 4096, 65536,
+                                                         4096, 1, 0.0, sp)))
+    emit("bias_relu_65536x4096", ms, nbytes=2.0 * 65536 * 4096 * 4 + 4096 * 4)
+    return 0
+
 def main():
     args = parse_args()
+    if args.configs:
+        return run_configs(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_b200(args)
