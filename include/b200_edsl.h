@@ -80,13 +80,19 @@ int b200_release(void);
 
 /* Y = act(X @ W + b) in f32 with 3xTF32 tensor-core arithmetic.
  * X[M,K] (pitch ldx), W[K,N] (pitch ldw), b[N] or NULL, Y[M,N] (pitch ldy).
- * Scratch for the tf32 hi/lo operand split comes from a buffer the runtime
- * caches per (device, stream).
+ * Scratch for the tf32 hi/lo operand split (and, for problems with too few
+ * 128x256 output tiles to fill the GPU, the split-K partial sums) comes from a
+ * buffer the runtime caches per (device, stream).
  * Replaces: linalg.fill+matmul (reference: cpp/src/builders/LinalgBuilder.cpp:106-139),
  * bias generic (:301-339), activation generic (:180-239). */
 int b200_dense_f32(const float* X, int64_t ldx, const float* W, int64_t ldw, const float* b,
                    float* Y, int64_t ldy, int64_t M, int64_t N, int64_t K, int act, float alpha,
                    void* stream);
+
+/* Number of K splits b200_dense_f32 uses for an M x N x K problem (1 = no
+ * split; otherwise the GEMM writes partial sums and one extra HBM-bound kernel
+ * adds them in fixed order, so results are deterministic). */
+int b200_dense_f32_splits(int64_t M, int64_t N, int64_t K);
 
 /* Same as b200_dense_f32 with caller-provided scratch of at least
  * b200_dense_f32_workspace_bytes(M, N, K) bytes (256-byte aligned). */

@@ -175,6 +175,7 @@ struct Epilogue {
   int act;
   float alpha;
   int vec_out;  // Y base 16-byte aligned and ldy % 4 == 0
+  int64_t split_stride;  // split-K: split s writes its partial at Y + s * split_stride
 };
 
 template <class Cfg>
@@ -182,8 +183,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAhi,
                        const __grid_constant__ CUtensorMap tmAlo,
                        const __grid_constant__ CUtensorMap tmBhi,
-                       const __grid_constant__ CUtensorMap tmBlo, int num_kb, int tiles_m,
-                       int tiles_n, Epilogue ep, int* status) {
+                       const __grid_constant__ CUtensorMap tmBlo, int num_kb_total,
+                       int kb_per_split, int tiles_m, int tiles_n, Epilogue ep, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -208,6 +209,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tile_n = in_group / group_rows;
   const int m0 = tile_m * kBM;
   const int n0 = tile_n * kBN;
+  // Split-K: blockIdx.y selects a contiguous range of k-blocks.
+  const int kb0 = blockIdx.y * kb_per_split;
+  const int num_kb = min(num_kb_total - kb0, kb_per_split);
   const int num_chunks = (num_kb + Cfg::ChunkKB - 1) / Cfg::ChunkKB;
 
   if (threadIdx.x == 0) {
@@ -251,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         uint8_t* st = smem + s * Cfg::StageBytes;
         mbar_arrive_expect_tx(&full[s], Cfg::StageBytes);
-        const int kx = kb * Cfg::BK;
+        const int kx = (kb0 + kb) * Cfg::BK;
         tma_load_2d(st, &tmAhi, &full[s], kx, m0);
         tma_load_2d(st + Cfg::ATileBytes, &tmAlo, &full[s], kx, m0);
         tma_load_2d(st + 2 * Cfg::ATileBytes, &tmBhi, &full[s], kx, n0);
@@ -328,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t row = (int64_t)m0 + quarter * 32 + lane;
       const int64_t col0 = (int64_t)n0 + half * 128;
       if (row < ep.M) {
-        float* dst = ep.Y + row * ep.ldy + col0;
+        float* dst = ep.Y + blockIdx.y * ep.split_stride + row * ep.ldy + col0;
         const float* bh = sbias + half * 128;
 #pragma unroll
         for (int j = 0; j < 128; j += 4) {
@@ -403,6 +407,11 @@ int64_t dense_f32_workspace_bytes(int64_t M, int64_t N, int64_t K) {
   return 2 * al(M * Kp * 4) + 2 * al(N * Kp * 4);
 }
 
+int64_t splitk_partials_bytes(int64_t M, int64_t N, int64_t K) {
+  const int s = choose_splits(M, N, K);
+  return s > 1 ? ((int64_t)s * M * N * 4 + 255) & ~int64_t(255) : 0;
+}
+
 int split_w_f32(const float* W, int64_t ldw, int64_t K, int64_t N, float* whiT, float* wloT,
                 cudaStream_t stream) {
   const int64_t Kp = (K + 3) & ~int64_t(3);
@@ -437,8 +446,8 @@ static int ring_variant() {
 
 template <class Cfg>
 static int launch_gemm(const float* xhi, const float* xlo, const float* whiT, const float* wloT,
-                       int64_t M, int64_t N, int64_t K, const Epilogue& ep, int* status,
-                       cudaStream_t stream) {
+                       int64_t M, int64_t N, int64_t K, const Epilogue& ep, int splits,
+                       int* status, cudaStream_t stream) {
   // The dynamic shared-memory opt-in is made once per device (thread-safe).
   static std::atomic<uint64_t> attr_done{0};
   int dev = 0;
@@ -460,8 +469,10 @@ static int launch_gemm(const float* xhi, const float* xlo, const float* whiT, co
   const int tiles_m = (int)((M + kBM - 1) / kBM);
   const int tiles_n = (int)((N + kBN - 1) / kBN);
   const int num_kb = (int)((K + Cfg::BK - 1) / Cfg::BK);
-  gemm_tf32x3_kernel<Cfg><<<tiles_m * tiles_n, kThreads, Cfg::SmemBytes, stream>>>(
-      ta_hi, ta_lo, tb_hi, tb_lo, num_kb, tiles_m, tiles_n, ep, status);
+  const int kb_per_split = (num_kb + splits - 1) / splits;
+  const int nsplit = (num_kb + kb_per_split - 1) / kb_per_split;  // every split non-empty
+  gemm_tf32x3_kernel<Cfg><<<dim3(tiles_m * tiles_n, nsplit), kThreads, Cfg::SmemBytes, stream>>>(
+      ta_hi, ta_lo, tb_hi, tb_lo, num_kb, kb_per_split, tiles_m, tiles_n, ep, status);
   count_launch();
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
@@ -479,9 +490,110 @@ int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
   ep.act = act;
   ep.alpha = alpha;
   ep.vec_out = ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(Y) & 15) == 0);
+  ep.split_stride = 0;
   if (ring_variant() == 0)
-    return launch_gemm<CfgBK32S2>(xhi, xlo, whiT, wloT, M, N, K, ep, status, stream);
-  return launch_gemm<CfgBK16S4>(xhi, xlo, whiT, wloT, M, N, K, ep, status, stream);
+    return launch_gemm<CfgBK32S2>(xhi, xlo, whiT, wloT, M, N, K, ep, 1, status, stream);
+  return launch_gemm<CfgBK16S4>(xhi, xlo, whiT, wloT, M, N, K, ep, 1, status, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Split-K for problems with too few output tiles to fill 148 SMs (the 1024^3
+// dense layer has 32 tiles, the MLP's layers 172 and 64).
+//
+// Cost model: with T tiles and S splits, T*S CTAs run in ceil(T*S/148) waves
+// of CTAs that each do 1/S of the K work, plus an HBM pass that writes and
+// reads S partial tiles. S = 1 whenever the tiles already fill >= 4 waves.
+int choose_splits(int64_t M, int64_t N, int64_t K) {
+  const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+  const int64_t kb16 = (K + 15) / 16;
+  if (tiles >= 4 * 148 || kb16 < 16) return 1;
+  const double t_cta_full = 2.0 * kBM * kBN * (double)K / 1.65e12;  // s per CTA, whole K
+  double best_t = 1e30;
+  int best = 1;
+  for (int s = 1; s <= 8; ++s) {
+    if (kb16 / s < 8) break;  // at least one 128-wide K chunk per split
+    const int64_t waves = (tiles * s + 147) / 148;
+    double t = waves * t_cta_full / s;
+    if (s > 1) t += (double)(s + 1) * M * N * 4 / 6.0e12;
+    if (t < best_t * 0.97) {
+      best_t = t;
+      best = s;
+    }
+  }
+  return best;
+}
+
+__global__ void splitk_reduce_kernel(const float* __restrict__ P, int splits, int64_t stride,
+                                     int64_t M, int64_t N, const float* __restrict__ bias,
+                                     int act, float alpha, float* __restrict__ Y, int64_t ldy,
+                                     int vec) {
+  if (vec) {  // N % 4 == 0, Y 16-byte aligned, ldy % 4 == 0
+    const int64_t q = N >> 2, total = M * q;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t m = i / q, n = (i - m * q) << 2;
+      float4 a = __ldg(reinterpret_cast<const float4*>(P + m * N + n));
+      for (int s = 1; s < splits; ++s) {  // fixed order: deterministic
+        const float4 t = __ldg(reinterpret_cast<const float4*>(P + s * stride + m * N + n));
+        a.x += t.x; a.y += t.y; a.z += t.z; a.w += t.w;
+      }
+      if (bias) {
+        a.x += bias[n]; a.y += bias[n + 1]; a.z += bias[n + 2]; a.w += bias[n + 3];
+      }
+      a.x = apply_act(a.x, act, alpha);
+      a.y = apply_act(a.y, act, alpha);
+      a.z = apply_act(a.z, act, alpha);
+      a.w = apply_act(a.w, act, alpha);
+      *reinterpret_cast<float4*>(Y + m * ldy + n) = a;
+    }
+  } else {
+    const int64_t total = M * N;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t m = i / N, n = i - m * N;
+      float a = P[i];
+      for (int s = 1; s < splits; ++s) a += P[s * stride + i];
+      if (bias) a += bias[n];
+      Y[m * ldy + n] = apply_act(a, act, alpha);
+    }
+  }
+}
+
+int gemm_tf32x3_splitk(const float* xhi, const float* xlo, const float* whiT, const float* wloT,
+                       int64_t M, int64_t N, int64_t K, const float* bias, float* Y, int64_t ldy,
+                       int act, float alpha, int splits, float* partials, int* status,
+                       cudaStream_t stream) {
+  if (splits <= 1)
+    return gemm_tf32x3_presplit(xhi, xlo, whiT, wloT, M, N, K, bias, Y, ldy, act, alpha, status,
+                                stream);
+  // Partials: [splits][M][N] raw sums (no bias, no activation).
+  Epilogue ep;
+  ep.Y = partials;
+  ep.ldy = N;
+  ep.bias = nullptr;
+  ep.M = M;
+  ep.N = N;
+  ep.act = kActNone;
+  ep.alpha = 0.0f;
+  ep.vec_out = ((N & 3) == 0) && ((reinterpret_cast<uintptr_t>(partials) & 15) == 0);
+  ep.split_stride = M * N;
+  // The launcher may use fewer splits so that none is empty; recompute it.
+  const int bk = ring_variant() == 0 ? CfgBK32S2::BK : CfgBK16S4::BK;
+  const int num_kb = (int)((K + bk - 1) / bk);
+  const int kbps = (num_kb + splits - 1) / splits;
+  const int nsplit = (num_kb + kbps - 1) / kbps;
+  int rc = ring_variant() == 0
+               ? launch_gemm<CfgBK32S2>(xhi, xlo, whiT, wloT, M, N, K, ep, splits, status, stream)
+               : launch_gemm<CfgBK16S4>(xhi, xlo, whiT, wloT, M, N, K, ep, splits, status, stream);
+  if (rc != kOk) return rc;
+  const int vec = ((N & 3) == 0) && ((ldy & 3) == 0) &&
+                  ((reinterpret_cast<uintptr_t>(Y) & 15) == 0) && ep.vec_out;
+  const int64_t work = vec ? M * N / 4 : M * N;
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, 148 * 16));
+  splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(partials, nsplit, M * N, M, N, bias, act, alpha,
+                                                   Y, ldy, vec);
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
 }  // namespace b200

@@ -33,6 +33,14 @@ int split_x_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xhi, f
                 cudaStream_t stream);
 int split_w_f32(const float* W, int64_t ldw, int64_t K, int64_t N, float* whiT, float* wloT,
                 cudaStream_t stream);
+// Split-K (few-tile problems): splits chosen by a wave-count cost model;
+// partials scratch of splitk_partials_bytes() (0 when splits == 1).
+int choose_splits(int64_t M, int64_t N, int64_t K);
+int64_t splitk_partials_bytes(int64_t M, int64_t N, int64_t K);
+int gemm_tf32x3_splitk(const float* xhi, const float* xlo, const float* whiT, const float* wloT,
+                       int64_t M, int64_t N, int64_t K, const float* bias, float* Y, int64_t ldy,
+                       int act, float alpha, int splits, float* partials, int* status,
+                       cudaStream_t stream);
 int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
                          const float* wloT, int64_t M, int64_t N, int64_t K, const float* bias,
                          float* Y, int64_t ldy, int act, float alpha, int* status,

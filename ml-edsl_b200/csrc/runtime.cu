@@ -82,7 +82,7 @@ struct DeviceCtx {
   int* status = nullptr;  // device word written by timed-out kernels
   // host-pointer call buffers
   DevBuf w, whi, wlo, bias;
-  DevBuf x[kRing], xhi[kRing], xlo[kRing], y[kRing];
+  DevBuf x[kRing], xhi[kRing], xlo[kRing], y[kRing], part[kRing];
   cudaEvent_t ev_h2d[kRing], ev_comp[kRing], ev_d2h[kRing];
   // device-pointer call scratch, keyed by stream
   std::map<cudaStream_t, DevBuf> scratch;
@@ -157,7 +157,13 @@ bool bad_dims(int64_t M, int64_t N, int64_t K) { return M < 0 || N < 0 || K < 0;
 // Scratch layout inside one workspace block.
 struct SplitBufs {
   float *xhi, *xlo, *whi, *wlo;
+  float* partials;  // split-K partial sums (only when choose_splits() > 1)
 };
+
+// Scratch of the dense device path: split operands + split-K partials.
+int64_t dense_scratch_bytes(int64_t M, int64_t N, int64_t K) {
+  return dense_f32_workspace_bytes(M, N, K) + splitk_partials_bytes(M, N, K);
+}
 SplitBufs carve(void* ws, int64_t M, int64_t N, int64_t K) {
   const int64_t Kp = round_up(K, 4);
   auto al = [](int64_t b) { return round_up(b, 256); };
@@ -170,6 +176,8 @@ SplitBufs carve(void* ws, int64_t M, int64_t N, int64_t K) {
   s.whi = reinterpret_cast<float*>(p);
   p += al(N * Kp * 4);
   s.wlo = reinterpret_cast<float*>(p);
+  p += al(N * Kp * 4);
+  s.partials = reinterpret_cast<float*>(p);
   return s;
 }
 
@@ -182,8 +190,8 @@ int dense_device(DeviceCtx* c, const float* X, int64_t ldx, const float* W, int6
   int rc = split_w_f32(W, ldw, K, N, s.whi, s.wlo, st);
   if (rc == kOk) rc = split_x_f32(X, ldx, M, K, s.xhi, s.xlo, st);
   if (rc == kOk)
-    rc = gemm_tf32x3_presplit(s.xhi, s.xlo, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha,
-                              c->status, st);
+    rc = gemm_tf32x3_splitk(s.xhi, s.xlo, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha,
+                            choose_splits(M, N, K), s.partials, c->status, st);
   if (rc != kOk) return fail(rc, std::string("dense_f32 launch failed: ") +
                                      cudaGetErrorString(cudaGetLastError()));
   return kOk;
@@ -242,8 +250,13 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
     B200_CUDA(c->whi.reserve(N * Kp * 4), "alloc W split");
     B200_CUDA(c->wlo.reserve(N * Kp * 4), "alloc W split");
   }
+  const int64_t last_rows = M - (nslab - 1) * slab;
+  const int64_t part_bytes = K > 0 ? std::max(splitk_partials_bytes(slab, N, K),
+                                              splitk_partials_bytes(last_rows, N, K))
+                                   : 0;
   for (int i = 0; i < kRing && i < nslab; ++i) {
     B200_CUDA(c->y[i].reserve(slab * N * 4), "alloc Y slab");
+    if (part_bytes) B200_CUDA(c->part[i].reserve(part_bytes), "alloc split-K partials");
     if (K > 0) {
       B200_CUDA(c->x[i].reserve(slab * K * 4), "alloc X slab");
       B200_CUDA(c->xhi[i].reserve(slab * Kp * 4), "alloc X split");
@@ -286,8 +299,9 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
       float* xlo = static_cast<float*>(c->xlo[slot].p);
       rc = split_x_f32(dX, K, rows, K, xhi, xlo, c->s_comp);
       if (rc == kOk)
-        rc = gemm_tf32x3_presplit(xhi, xlo, dWhi, dWlo, rows, N, K, db, dY, N, act, alpha,
-                                  c->status, c->s_comp);
+        rc = gemm_tf32x3_splitk(xhi, xlo, dWhi, dWlo, rows, N, K, db, dY, N, act, alpha,
+                                choose_splits(rows, N, K),
+                                static_cast<float*>(c->part[slot].p), c->status, c->s_comp);
     }
     if (rc) return fail(rc, "dense kernel launch failed");
     B200_CUDA(cudaEventRecord(c->ev_comp[slot], c->s_comp), "record");
@@ -444,6 +458,7 @@ int b200_release(void) {
     c.w.release(); c.whi.release(); c.wlo.release(); c.bias.release();
     for (int i = 0; i < kRing; ++i) {
       c.x[i].release(); c.xhi[i].release(); c.xlo[i].release(); c.y[i].release();
+      c.part[i].release();
     }
     for (auto& kv : c.scratch) kv.second.release();
     c.scratch.clear();
@@ -454,7 +469,12 @@ int b200_release(void) {
 // ---------------------------------------------------------------- device API
 int64_t b200_dense_f32_workspace_bytes(int64_t M, int64_t N, int64_t K) {
   if (bad_dims(M, N, K)) return -1;
-  return dense_f32_workspace_bytes(M, N, std::max<int64_t>(K, 1));
+  return dense_scratch_bytes(M, N, std::max<int64_t>(K, 1));
+}
+
+int b200_dense_f32_splits(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 1;
+  return choose_splits(M, N, K);
 }
 
 int b200_dense_f32_ws(const float* X, int64_t ldx, const float* W, int64_t ldw, const float* b,
@@ -462,7 +482,7 @@ int b200_dense_f32_ws(const float* X, int64_t ldx, const float* W, int64_t ldw, 
                       float alpha, void* workspace, int64_t workspace_bytes, void* stream) {
   int rc = validate_dense(X, ldx, W, ldw, Y, ldy, M, N, K, act);
   if (rc) return rc;
-  const int64_t need = dense_f32_workspace_bytes(M, N, std::max<int64_t>(K, 1));
+  const int64_t need = dense_scratch_bytes(M, N, std::max<int64_t>(K, 1));
   if (K > 0 && M > 0 && N > 0) {
     if (!workspace || workspace_bytes < need)
       return fail(kErrInvalidArg, "workspace missing or smaller than "
@@ -487,7 +507,7 @@ int b200_dense_f32(const float* X, int64_t ldx, const float* W, int64_t ldw, con
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   void* ws = nullptr;
   if (M > 0 && N > 0 && K > 0) {
-    const size_t need = (size_t)dense_f32_workspace_bytes(M, N, K);
+    const size_t need = (size_t)dense_scratch_bytes(M, N, K);
     std::lock_guard<std::mutex> lk(g_mu);
     DevBuf& buf = c->scratch[st];
     if (buf.n < need) {

@@ -27,7 +27,7 @@ EXPORTED_SYMBOLS = [
     "b200_version", "b200_last_error", "b200_last_status", "b200_device_count",
     "b200_launch_count", "b200_set_default_devices", "b200_get_default_devices", "b200_release",
     "b200_dense_f32", "b200_dense_f32_workspace_bytes", "b200_dense_f32_ws",
-    "b200_dense_f32_noalloc", "b200_matmul_i32",
+    "b200_dense_f32_noalloc", "b200_dense_f32_splits", "b200_matmul_i32",
     "b200_bias_act_f32", "b200_act_f32", "b200_bias_add_i32", "b200_stream_sync",
     "b200_tf32_split_rows", "b200_tf32_split_transpose", "b200_gemm_tf32x3_presplit",
     "b200_malloc", "b200_free", "b200_memcpy_h2d", "b200_memcpy_d2h",
@@ -67,6 +67,7 @@ def _declare(lib):
                                vp], i32),
         "b200_dense_f32_noalloc": ([vp, i64, vp, i64, vp, vp, i64, i64, i64, i64, i32, f32, vp],
                                    i32),
+        "b200_dense_f32_splits": ([i64, i64, i64], i32),
         "b200_matmul_i32": ([vp, i64, vp, i64, vp, vp, i64, i64, i64, i64, vp], i32),
         "b200_bias_act_f32": ([vp, i64, vp, vp, i64, i64, i64, i32, f32, vp], i32),
         "b200_act_f32": ([vp, vp, i64, i32, f32, vp], i32),
@@ -126,6 +127,12 @@ def memref_function(name, nargs):
 
 def launch_count():
     return int(lib().b200_launch_count())
+
+
+def dense_launches(M, N, K):
+    """Kernel launches of one f32 dense layer: W split, X split, GEMM, and a
+    split-K reduction when the problem is split."""
+    return 3 + (1 if lib().b200_dense_f32_splits(M, N, K) > 1 else 0)
 
 
 def device_count():

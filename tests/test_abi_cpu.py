@@ -49,11 +49,25 @@ def test_version_and_counters():
 
 def test_workspace_formula():
     lib = _native.lib()
-    M, N, K = 100, 50, 1001
-    Kp = 1004
     al = lambda b: (b + 255) // 256 * 256
+    # many tiles: no split-K, scratch = the four split operands
+    M, N, K = 8192, 8192, 1001
+    Kp = 1004
+    assert lib.b200_dense_f32_splits(M, N, K) == 1
     assert lib.b200_dense_f32_workspace_bytes(M, N, K) == 2 * al(M * Kp * 4) + 2 * al(N * Kp * 4)
+    # one tile, long K: split-K partial sums are added to the scratch
+    M, N, K = 100, 50, 1001
+    s = lib.b200_dense_f32_splits(M, N, K)
+    assert 1 < s <= 8
+    assert lib.b200_dense_f32_workspace_bytes(M, N, K) == (
+        2 * al(M * Kp * 4) + 2 * al(N * Kp * 4) + al(s * M * N * 4))
     assert lib.b200_dense_f32_workspace_bytes(-1, 2, 3) == -1
+
+
+@pytest.mark.parametrize("M,N,K,splits", [(8192, 8192, 8192, 1), (65536, 4096, 4096, 1),
+                                          (1024, 1024, 1024, 4), (64, 80, 96, 1)])
+def test_split_k_choice(M, N, K, splits):
+    assert _native.lib().b200_dense_f32_splits(M, N, K) == splits
 
 
 def test_invalid_arguments_rejected_before_device_use():

@@ -195,3 +195,31 @@ def test_large_matmul_sampled_rows(cuda, name):
     # fp32-level accuracy, not tf32-level
     exact = A[rows].astype(np.float64) @ B.astype(np.float64)
     assert float(np.max(np.abs(got[rows] - exact))) < bound / 10
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 1024, 1024), (512, 4096, 11008), (100, 50, 1001)])
+def test_split_k_matches_unsplit(cuda, M, N, K):
+    """Split-K (chosen for few-tile problems) against the same pre-split
+    operands run without splitting; both within the f32 bound of the oracle."""
+    import torch
+    dev = torch.device("cuda:0")
+    L = _native.lib()
+    assert L.b200_dense_f32_splits(M, N, K) > 1
+    X, W, b = _inputs(M, N, K, seed=K)
+    got = dense_device(torch, X, W, b, act=1)
+    Kp = (K + 3) // 4 * 4
+    tX, tW, tb = (torch.from_numpy(a).to(dev) for a in (X, W, b))
+    xhi, xlo = torch.empty((M, Kp), device=dev), torch.empty((M, Kp), device=dev)
+    whi, wlo = torch.empty((N, Kp), device=dev), torch.empty((N, Kp), device=dev)
+    Y1 = torch.empty((M, N), device=dev)
+    s = stream_ptr(torch)
+    _native.check(L.b200_tf32_split_rows(ptr(tX), K, M, K, ptr(xhi), ptr(xlo), s))
+    _native.check(L.b200_tf32_split_transpose(ptr(tW), N, K, N, ptr(whi), ptr(wlo), s))
+    _native.check(L.b200_gemm_tf32x3_presplit(ptr(xhi), ptr(xlo), ptr(whi), ptr(wlo), ptr(tb),
+                                              ptr(Y1), N, M, N, K, 1, 0.0, s))
+    _native.check(L.b200_stream_sync(s))
+    unsplit = Y1.cpu().numpy()
+    bound = oracle.f32_bound(K, X, W)
+    assert max_err(got, unsplit) <= bound
+    ref = oracle.dense_f32(X[:256], W, b, act=1)
+    assert max_err(got[:256], ref) <= bound and max_err(unsplit[:256], ref) <= bound
