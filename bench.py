@@ -209,7 +209,7 @@ def run_reference(args):
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit_line(line)
     return 0
 
 
@@ -360,7 +360,10 @@ def run_b200(args):
         # correctness of the e2e result against the device-resident path
         step()
         torch.cuda.synchronize()
-        assert torch.equal(Yh, Y.cpu()), "e2e result differs from device path"
+        # (split-K or slab boundaries may change the K summation order)
+        bound = 1e-4 * K ** 0.5 * float(X.abs().max()) * float(W.abs().max())
+        e2e_err = float((Yh - Y.cpu()).abs().max())
+        assert e2e_err <= bound, f"e2e result differs from device path: {e2e_err} > {bound}"
         e2e = {"value": flops_job * args.steps / t_e2e / 1e12, "unit": UNIT,
                "h2d_bytes_per_step": (M * K + K * N + N) * 4, "d2h_bytes_per_step": M * N * 4,
                "ms_per_step": t_e2e / args.steps * 1e3,
@@ -426,7 +429,7 @@ def run_b200(args):
             "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
             "gpu_launches": launches, "headline_8192": headline,
         }
-        print(json.dumps(line), flush=True)
+        emit_line(line)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -478,7 +481,7 @@ def run_configs(args):
             line.update({"TFLOP/s": flops / ms / 1e9, "frac_of_3xtf32_peak": flops / ms / 1e9 / peak})
         if nbytes:
             line["GB/s"] = nbytes / ms / 1e6
-        print(json.dumps(line), flush=True)
+        emit_line(line)
 
     for name, (M, N, K), act, with_b, seed, lo in [
             ("matmul_256", (256, 256, 256), 0, False, 0, -1.0),
@@ -506,8 +509,7 @@ def run_configs(args):
     C = torch.empty_like(A)
     ms = timed(lambda: _native.check(L.b200_matmul_i32(P(A), 2048, P(B), 2048, None, P(C), 2048,
                                                       2048, 2048, 2048, sp)))
-    print(json.dumps({"config": "matmul_i32_2048", "ms": ms,
-                      "Tint-op/s": 2.0 * 2048 ** 3 / ms / 1e9}), flush=True)
+    emit_line({"config": "matmul_i32_2048", "ms": ms, "Tint-op/s": 2.0 * 2048 ** 3 / ms / 1e9})
     # unfused elementwise bias+relu over the cfg4 output shape (HBM-bound)
     Xe, be = u((65536, 4096), 9), u((4096,), 10)
     Ye = torch.empty_like(Xe)
@@ -516,8 +518,21 @@ def run_configs(args):
     emit("bias_relu_65536x4096", ms, nbytes=2.0 * 65536 * 4096 * 4 + 4096 * 4)
     return 0
 
+_STDOUT_FD = None
+
+
+def emit_line(line):
+    """Writes the one JSON result line to the real stdout (libraries such as
+    NCCL print to stdout during the run, which is redirected to stderr)."""
+    os.write(_STDOUT_FD if _STDOUT_FD is not None else 1, (json.dumps(line) + "\n").encode())
+
+
 def main():
+    global _STDOUT_FD
     args = parse_args()
+    sys.stdout.flush()
+    _STDOUT_FD = os.dup(1)
+    os.dup2(2, 1)
     if args.configs:
         return run_configs(args)
     if args.impl == "reference":
