@@ -516,6 +516,15 @@ def run_configs(args):
     ms = timed(lambda: _native.check(L.b200_bias_act_f32(P(Xe), 4096, P(be), P(Ye), 4096, 65536,
                                                          4096, 1, 0.0, sp)))
     emit("bias_relu_65536x4096", ms, nbytes=2.0 * 65536 * 4096 * 4 + 4096 * 4)
+    del Xe, be, Ye
+    # 1-D reductions / dot over 2^28 f32 (1 GiB per operand, HBM-bound)
+    n = 1 << 28
+    xr, yr = u((n,), 11), u((n,), 12)
+    out = torch.empty(1, device=dev)
+    ms = timed(lambda: _native.check(L.b200_reduce_f32(P(xr), n, 0, 0.0, P(out), sp)))
+    emit("tensor_sum_2^28", ms, nbytes=4.0 * n)
+    ms = timed(lambda: _native.check(L.b200_dot_f32(P(xr), P(yr), n, P(out), sp)))
+    emit("dot_2^28", ms, nbytes=8.0 * n)
     return 0
 
 _STDOUT_FD = None

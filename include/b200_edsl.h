@@ -48,6 +48,11 @@ extern "C" {
 #define B200_ACT_RELU 1
 #define B200_ACT_LEAKY_RELU 2
 
+#define B200_REDUCE_SUM 0  /* acc + x, the tensor_sum body */
+#define B200_REDUCE_PROD 1 /* acc * x */
+#define B200_REDUCE_MAX 2  /* x > acc ? x : acc, the tensor_max body */
+#define B200_REDUCE_MIN 3  /* x < acc ? x : acc, the tensor_min body */
+
 /* ---------------------------------------------------------------- runtime */
 
 /* Library version string. */
@@ -164,6 +169,20 @@ int b200_free(void* ptr);
 int b200_memcpy_h2d(void* dst, const void* src, int64_t bytes);
 int b200_memcpy_d2h(void* dst, const void* src, int64_t bytes);
 
+/* 1-D reductions and dot products, result in one device element `out`:
+ *   out = init (op) x[0] (op) x[1] ... ; dot: out = sum_i a[i]*b[i].
+ * Two-pass and deterministic. f32 sums/products/dots are tree-ordered (not
+ * the sequential order); max/min equal the sequential fold with the
+ * reference's bodies (NaN elements never win). i32 sums/products wrap.
+ * Replaces: linalg.dot (reference: cpp/src/builders/LinalgBuilder.cpp:66-104)
+ * and linalg.reduce with the tensor_sum / tensor_max / tensor_min bodies
+ * (cpp/src/builders/LinalgBuilder.cpp:241-279, mlir_edsl/ops/linalg.py:104-175). */
+int b200_reduce_f32(const float* x, int64_t n, int op, float init, float* out, void* stream);
+int b200_reduce_i32(const int32_t* x, int64_t n, int op, int32_t init, int32_t* out,
+                    void* stream);
+int b200_dot_f32(const float* a, const float* b, int64_t n, float* out, void* stream);
+int b200_dot_i32(const int32_t* a, const int32_t* b, int64_t n, int32_t* out, void* stream);
+
 /* --------------------------------------------------- host-pointer entry points */
 
 /* Host buffers; synchronous. Rows of X/Y are sharded over `ndev` devices
@@ -186,6 +205,12 @@ int b200_bias_add_i32_host(const int32_t* X, int64_t ldx, const int32_t* b, int3
                            int64_t ldy, int64_t M, int64_t N);
 
 int b200_act_f32_host(const float* X, float* Y, int64_t count, int act, float alpha);
+
+/* Host buffers in, host scalar `*result` out (synchronous). */
+int b200_reduce_f32_host(const float* x, int64_t n, int op, float init, float* result);
+int b200_reduce_i32_host(const int32_t* x, int64_t n, int op, int32_t init, int32_t* result);
+int b200_dot_f32_host(const float* a, const float* b, int64_t n, float* result);
+int b200_dot_i32_host(const int32_t* a, const int32_t* b, int64_t n, int32_t* result);
 
 /* ------------------------------------------------- memref-descriptor entry points
  * A rank-2 memref is passed as 7 arguments
@@ -221,6 +246,16 @@ void b200_memref_bias_add_f32(B200_MEMREF2(X), B200_MEMREF1(b), B200_MEMREF2(Y))
 void b200_memref_bias_relu_f32(B200_MEMREF2(X), B200_MEMREF1(b), B200_MEMREF2(Y));
 /* Y = relu(X), f32 rank 2 (reference library_call "relu"). */
 void b200_memref_relu_f32(B200_MEMREF2(X), B200_MEMREF2(Y));
+
+/* Scalar-returning functions (a JIT'd `-> f32` / `-> i32` function returns
+ * its scalar; reference: mlir_edsl/backend.py:192-194): dot(a, b) with two
+ * rank-1 descriptors (10 arguments), tensor_sum / tensor_max / tensor_min
+ * with one (5 arguments). On failure they return 0; see b200_last_status(). */
+float b200_memref_dot_f32(B200_MEMREF1(a), B200_MEMREF1(b));
+int32_t b200_memref_dot_i32(B200_MEMREF1(a), B200_MEMREF1(b));
+float b200_memref_sum_f32(B200_MEMREF1(a));
+float b200_memref_max_f32(B200_MEMREF1(a));
+float b200_memref_min_f32(B200_MEMREF1(a));
 
 #ifdef __cplusplus
 }

@@ -18,6 +18,7 @@ enum Status : int {
 };
 
 enum Act : int { kActNone = 0, kActRelu = 1, kActLeakyRelu = 2 };
+enum RedOp : int { kRedSum = 0, kRedProd = 1, kRedMax = 2, kRedMin = 3 };
 
 // Number of kernels this library has launched (process-wide).
 void count_launch();
@@ -59,5 +60,13 @@ int bias_add_i32(const int32_t* X, int64_t ldx, const int32_t* b, int32_t* Y, in
                  int64_t M, int64_t N, cudaStream_t stream);
 int fill_bias_act_f32(const float* b, float* Y, int64_t ldy, int64_t M, int64_t N, int act,
                       float alpha, cudaStream_t stream);
+
+// ---- 1-D reductions / dot (reduce.cu). `y` non-null: dot product (op = sum).
+// `scratch` holds reduce_scratch_bytes(); `out` is one device element.
+int64_t reduce_scratch_bytes();
+int reduce_f32(const float* x, const float* y, int64_t n, int op, float init, float* out,
+               void* scratch, cudaStream_t st);
+int reduce_i32(const int32_t* x, const int32_t* y, int64_t n, int op, int32_t init, int32_t* out,
+               void* scratch, cudaStream_t st);
 
 }  // namespace b200

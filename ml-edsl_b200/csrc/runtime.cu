@@ -12,11 +12,13 @@
 #include <atomic>
 #include <cstdio>
 #include <cstdlib>
+#include <cmath>
 #include <cstring>
 #include <map>
 #include <mutex>
 #include <string>
 #include <thread>
+#include <type_traits>
 #include <vector>
 #include "../../include/b200_edsl.h"
 #include "kernels.h"
@@ -411,6 +413,62 @@ int elementwise_host(size_t in_bytes_x, const void* X, size_t in_bytes_b, const 
   return kOk;
 }
 
+
+// Host-pointer reduction / dot on the current device: copy in, two-pass
+// reduce into a device scalar, copy the scalar out.
+template <class T>
+int reduce_host_impl(const T* x, const T* y, int64_t n, int op, T init, T* result) {
+  DeviceCtx* c = nullptr;
+  int rc = current_ctx(&c);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(c->mu);
+  const size_t bytes = (size_t)std::max<int64_t>(n, 1) * sizeof(T);
+  B200_CUDA(c->x[0].reserve(bytes), "alloc x");
+  if (y) B200_CUDA(c->w.reserve(bytes), "alloc y");
+  B200_CUDA(c->y[0].reserve((size_t)reduce_scratch_bytes() + 256), "alloc partials");
+  cudaStream_t s = c->s_comp;
+  if (n) B200_CUDA(cudaMemcpyAsync(c->x[0].p, x, n * sizeof(T), cudaMemcpyHostToDevice, s), "H2D x");
+  if (y && n)
+    B200_CUDA(cudaMemcpyAsync(c->w.p, y, n * sizeof(T), cudaMemcpyHostToDevice, s), "H2D y");
+  char* scratch = static_cast<char*>(c->y[0].p);
+  T* dout = reinterpret_cast<T*>(scratch + reduce_scratch_bytes());
+  if constexpr (std::is_same<T, float>::value)
+    rc = reduce_f32(static_cast<const float*>(c->x[0].p), y ? static_cast<const float*>(c->w.p) : nullptr,
+                    n, op, init, dout, scratch, s);
+  else
+    rc = reduce_i32(static_cast<const int32_t*>(c->x[0].p),
+                    y ? static_cast<const int32_t*>(c->w.p) : nullptr, n, op, init, dout, scratch, s);
+  if (rc) return fail(rc, "reduction launch failed");
+  B200_CUDA(cudaMemcpyAsync(result, dout, sizeof(T), cudaMemcpyDeviceToHost, s), "D2H result");
+  B200_CUDA(cudaStreamSynchronize(s), "sync");
+  return kOk;
+}
+
+// Device-pointer reduction: partials in the per-(device, stream) scratch.
+template <class T>
+int reduce_device_impl(const T* x, const T* y, int64_t n, int op, T init, T* out, void* stream) {
+  if (n < 0 || op < kRedSum || op > kRedMin) return fail(kErrInvalidArg, "bad reduction arguments");
+  if (!out || (n > 0 && !x)) return fail(kErrInvalidArg, "null buffer");
+  DeviceCtx* c = nullptr;
+  int rc = current_ctx(&c);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* ws = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    DevBuf& buf = c->scratch[st];
+    if (buf.n < (size_t)reduce_scratch_bytes()) {
+      B200_CUDA(cudaStreamSynchronize(st), "sync before scratch growth");
+      B200_CUDA(buf.reserve(reduce_scratch_bytes()), "alloc scratch");
+    }
+    ws = buf.p;
+  }
+  if constexpr (std::is_same<T, float>::value)
+    rc = reduce_f32(x, y, n, op, init, out, ws, st);
+  else
+    rc = reduce_i32(x, y, n, op, init, out, ws, st);
+  return rc ? fail(rc, "reduction launch failed") : kOk;
+}
 }  // namespace
 
 int report_error(int code, const char* msg) { return fail(code, msg); }
@@ -629,6 +687,50 @@ int b200_memcpy_d2h(void* dst, const void* src, int64_t bytes) {
   return succeed();
 }
 
+
+// ---------------------------------------------------------------- reductions / dot
+int b200_reduce_f32(const float* x, int64_t n, int op, float init, float* out, void* stream) {
+  int rc = reduce_device_impl<float>(x, nullptr, n, op, init, out, stream);
+  return rc ? rc : succeed();
+}
+int b200_reduce_i32(const int32_t* x, int64_t n, int op, int32_t init, int32_t* out,
+                    void* stream) {
+  int rc = reduce_device_impl<int32_t>(x, nullptr, n, op, init, out, stream);
+  return rc ? rc : succeed();
+}
+int b200_dot_f32(const float* a, const float* b, int64_t n, float* out, void* stream) {
+  if (n > 0 && !b) return fail(kErrInvalidArg, "null buffer");
+  int rc = reduce_device_impl<float>(a, b, n, kRedSum, 0.0f, out, stream);
+  return rc ? rc : succeed();
+}
+int b200_dot_i32(const int32_t* a, const int32_t* b, int64_t n, int32_t* out, void* stream) {
+  if (n > 0 && !b) return fail(kErrInvalidArg, "null buffer");
+  int rc = reduce_device_impl<int32_t>(a, b, n, kRedSum, 0, out, stream);
+  return rc ? rc : succeed();
+}
+int b200_reduce_f32_host(const float* x, int64_t n, int op, float init, float* result) {
+  if (n < 0 || op < kRedSum || op > kRedMin || !result || (n > 0 && !x))
+    return fail(kErrInvalidArg, "bad reduction arguments");
+  int rc = reduce_host_impl<float>(x, nullptr, n, op, init, result);
+  return rc ? rc : succeed();
+}
+int b200_reduce_i32_host(const int32_t* x, int64_t n, int op, int32_t init, int32_t* result) {
+  if (n < 0 || op < kRedSum || op > kRedMin || !result || (n > 0 && !x))
+    return fail(kErrInvalidArg, "bad reduction arguments");
+  int rc = reduce_host_impl<int32_t>(x, nullptr, n, op, init, result);
+  return rc ? rc : succeed();
+}
+int b200_dot_f32_host(const float* a, const float* b, int64_t n, float* result) {
+  if (n < 0 || !result || (n > 0 && (!a || !b))) return fail(kErrInvalidArg, "bad dot arguments");
+  int rc = reduce_host_impl<float>(a, b, n, kRedSum, 0.0f, result);
+  return rc ? rc : succeed();
+}
+int b200_dot_i32_host(const int32_t* a, const int32_t* b, int64_t n, int32_t* result) {
+  if (n < 0 || !result || (n > 0 && (!a || !b))) return fail(kErrInvalidArg, "bad dot arguments");
+  int rc = reduce_host_impl<int32_t>(a, b, n, kRedSum, 0, result);
+  return rc ? rc : succeed();
+}
+
 // ---------------------------------------------------------------- host API
 int b200_dense_f32_host(const float* X, int64_t ldx, const float* W, int64_t ldw, const float* b,
                         float* Y, int64_t ldy, int64_t M, int64_t N, int64_t K, int act,
@@ -815,6 +917,42 @@ void b200_memref_bias_relu_f32(B200_MEMREF2(X), B200_MEMREF1(b), B200_MEMREF2(Y)
 }
 void b200_memref_relu_f32(B200_MEMREF2(X), B200_MEMREF2(Y)) {
   memref_bias_act(M2(X), nullptr, 0, 0, 1, false, M2(Y), kActRelu);
+}
+
+// Scalar-returning memref entry points (rank-1 descriptors: alloc, aligned,
+// offset, size, stride). On failure they return 0 and set b200_last_status().
+static bool memref1_view(const char* name, void* aligned, int64_t st0) {
+  return memref1_ok(name, aligned, st0);
+}
+float b200_memref_dot_f32(B200_MEMREF1(a), B200_MEMREF1(b)) {
+  float r = 0.0f;
+  if (!memref1_view("lhs", a_aligned, a_st0) || !memref1_view("rhs", b_aligned, b_st0)) return r;
+  if (a_s0 != b_s0) return fail(kErrInvalidArg, "dot operands differ in length"), r;
+  b200_dot_f32_host(at<float>(a_aligned, a_off), at<float>(b_aligned, b_off), a_s0, &r);
+  return r;
+}
+int32_t b200_memref_dot_i32(B200_MEMREF1(a), B200_MEMREF1(b)) {
+  int32_t r = 0;
+  if (!memref1_view("lhs", a_aligned, a_st0) || !memref1_view("rhs", b_aligned, b_st0)) return r;
+  if (a_s0 != b_s0) return fail(kErrInvalidArg, "dot operands differ in length"), r;
+  b200_dot_i32_host(at<int32_t>(a_aligned, a_off), at<int32_t>(b_aligned, b_off), a_s0, &r);
+  return r;
+}
+static float memref_reduce_f32(void* al, int64_t off, int64_t n, int64_t st0, int op,
+                               float init) {
+  float r = 0.0f;
+  if (!memref1_view("input", al, st0)) return r;
+  b200_reduce_f32_host(at<float>(al, off), n, op, init, &r);
+  return r;
+}
+float b200_memref_sum_f32(B200_MEMREF1(a)) {
+  return memref_reduce_f32(a_aligned, a_off, a_s0, a_st0, kRedSum, 0.0f);
+}
+float b200_memref_max_f32(B200_MEMREF1(a)) {
+  return memref_reduce_f32(a_aligned, a_off, a_s0, a_st0, kRedMax, -INFINITY);
+}
+float b200_memref_min_f32(B200_MEMREF1(a)) {
+  return memref_reduce_f32(a_aligned, a_off, a_s0, a_st0, kRedMin, INFINITY);
 }
 
 }  // extern "C"

@@ -16,7 +16,9 @@ Functions are traced symbolically, pattern-matched to fused kernels
 from .ast import (ADD, DIV, MUL, SUB, BinaryOp, Constant, LinalgActivation, LinalgBinaryOp,
                   LinalgMatmul, Parameter, Value)
 from .functions import MLFunction, ml_function
-from .ops import add, div, leaky_relu, matmul, mul, relu, sub
+from .ops import (If, add, div, dot, eq, ge, gt, le, leaky_relu, lt, matmul, mul, ne, reduce,
+                  relu, sub, tensor_max, tensor_min, tensor_sum)
+from .ast import CompareOp, IfOp, LinalgDot, LinalgReduce, to_value
 from .types import DYN, Tensor, TensorType, ScalarType, f32, i1, i32
 
 try:
@@ -33,6 +35,9 @@ __all__ = [
     "ml_function", "MLFunction",
     "i32", "f32", "i1", "DYN", "Tensor", "TensorType", "ScalarType",
     "add", "sub", "mul", "div", "matmul", "relu", "leaky_relu",
+    "dot", "reduce", "tensor_sum", "tensor_max", "tensor_min", "If",
+    "lt", "le", "gt", "ge", "eq", "ne", "to_value", "CompareOp", "IfOp", "LinalgDot",
+    "LinalgReduce",
     "ADD", "SUB", "MUL", "DIV",
     "Value", "Constant", "Parameter", "BinaryOp", "LinalgMatmul", "LinalgBinaryOp",
     "LinalgActivation",

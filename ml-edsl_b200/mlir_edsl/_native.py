@@ -21,6 +21,7 @@ ERROR_NAMES = {
     7: "B200_ERR_TOO_LARGE",
 }
 ACT_NONE, ACT_RELU, ACT_LEAKY_RELU = 0, 1, 2
+REDUCE_SUM, REDUCE_PROD, REDUCE_MAX, REDUCE_MIN = 0, 1, 2, 3
 
 # Every symbol include/b200_edsl.h declares (checked by the CPU test-suite).
 EXPORTED_SYMBOLS = [
@@ -33,6 +34,10 @@ EXPORTED_SYMBOLS = [
     "b200_malloc", "b200_free", "b200_memcpy_h2d", "b200_memcpy_d2h",
     "b200_dense_f32_host", "b200_matmul_i32_host", "b200_bias_act_f32_host",
     "b200_bias_add_i32_host", "b200_act_f32_host",
+    "b200_reduce_f32", "b200_reduce_i32", "b200_dot_f32", "b200_dot_i32",
+    "b200_reduce_f32_host", "b200_reduce_i32_host", "b200_dot_f32_host", "b200_dot_i32_host",
+    "b200_memref_dot_f32", "b200_memref_dot_i32", "b200_memref_sum_f32", "b200_memref_max_f32",
+    "b200_memref_min_f32",
     "b200_memref_matmul_f32", "b200_memref_matmul_relu_f32", "b200_memref_dense_f32",
     "b200_memref_dense_relu_f32", "b200_memref_matmul_i32", "b200_memref_dense_i32",
     "b200_memref_bias_add_f32", "b200_memref_bias_relu_f32", "b200_memref_relu_f32",
@@ -87,6 +92,14 @@ def _declare(lib):
         "b200_bias_act_f32_host": ([vp, i64, vp, vp, i64, i64, i64, i32, f32], i32),
         "b200_bias_add_i32_host": ([vp, i64, vp, vp, i64, i64, i64], i32),
         "b200_act_f32_host": ([vp, vp, i64, i32, f32], i32),
+        "b200_reduce_f32": ([vp, i64, i32, f32, vp, vp], i32),
+        "b200_reduce_i32": ([vp, i64, i32, c.c_int32, vp, vp], i32),
+        "b200_dot_f32": ([vp, vp, i64, vp, vp], i32),
+        "b200_dot_i32": ([vp, vp, i64, vp, vp], i32),
+        "b200_reduce_f32_host": ([vp, i64, i32, f32, vp], i32),
+        "b200_reduce_i32_host": ([vp, i64, i32, c.c_int32, vp], i32),
+        "b200_dot_f32_host": ([vp, vp, i64, vp], i32),
+        "b200_dot_i32_host": ([vp, vp, i64, vp], i32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

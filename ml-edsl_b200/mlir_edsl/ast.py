@@ -73,6 +73,24 @@ class Value:
         from .ops import matmul
         return matmul(self, other)
 
+    # comparisons (scalar values inside reduce bodies); == and != keep Python
+    # identity semantics here, use ops.eq / ops.ne instead
+    def __lt__(self, other):
+        from .ops import lt
+        return lt(self, other)
+
+    def __le__(self, other):
+        from .ops import le
+        return le(self, other)
+
+    def __gt__(self, other):
+        from .ops import gt
+        return gt(self, other)
+
+    def __ge__(self, other):
+        from .ops import ge
+        return ge(self, other)
+
     def __rmatmul__(self, other):
         from .ops import matmul
         return matmul(other, self)
@@ -263,3 +281,131 @@ class BinaryOp(Value):
 
     def get_children(self):
         return [self.lhs, self.rhs]
+
+
+# ----------------------------------------------------------------------------
+# Comparisons, value selection, dot and reduce (1-D reductions).
+# reference: mlir_edsl/ops/comparison.py, mlir_edsl/ast/nodes/control_flow.py
+# (IfOp), mlir_edsl/ast/nodes/linalg.py:15-72 (LinalgDot), :366-475
+# (LinalgReduce and its element / accumulator placeholders).
+LT, LE, GT, GE, EQ, NE = "lt", "le", "gt", "ge", "eq", "ne"
+
+
+class CompareOp(Value):
+    """Scalar comparison producing i1."""
+
+    def __init__(self, pred: str, lhs: Value, rhs: Value):
+        super().__init__()
+        self.pred, self.lhs, self.rhs = pred, lhs, rhs
+        lt, rt = lhs.infer_type(), rhs.infer_type()
+        if not (isinstance(lt, ScalarType) and isinstance(rt, ScalarType)):
+            raise TypeError(f"comparison requires scalar operands, got {lt} and {rt}")
+        if lt != rt:
+            raise TypeError(f"Type mismatch in comparison: {lt} vs {rt}")
+
+    def infer_type(self):
+        return i1
+
+    def get_children(self):
+        return [self.lhs, self.rhs]
+
+    def _describe(self):
+        return f"CompareOp({self.pred})"
+
+
+class IfOp(Value):
+    """Value selection: then_value if cond else else_value."""
+
+    def __init__(self, cond: Value, then_value: Value, else_value: Value):
+        super().__init__()
+        self.cond, self.then_value, self.else_value = cond, then_value, else_value
+        if cond.infer_type() != i1:
+            raise TypeError(f"If condition must be i1, got {cond.infer_type()}")
+        tt, et = then_value.infer_type(), else_value.infer_type()
+        if tt != et:
+            raise TypeError(f"If branches must have the same type, got {tt} and {et}")
+        self._out_type = tt
+
+    def infer_type(self):
+        return self._out_type
+
+    def get_children(self):
+        return [self.cond, self.then_value, self.else_value]
+
+
+class LinalgDot(Value):
+    """Dot product of two 1-D tensors; returns a scalar of the element type."""
+
+    def __init__(self, lhs: Value, rhs: Value):
+        super().__init__()
+        self.lhs, self.rhs = lhs, rhs
+        lt, rt = lhs.infer_type(), rhs.infer_type()
+        if not isinstance(lt, TensorType) or lt.ndim != 1:
+            raise TypeError(f"linalg.dot: lhs must be a 1D tensor, got {lt}")
+        if not isinstance(rt, TensorType) or rt.ndim != 1:
+            raise TypeError(f"linalg.dot: rhs must be a 1D tensor, got {rt}")
+        if lt.element_type != rt.element_type:
+            raise TypeError(f"linalg.dot: operand element types must match, "
+                            f"got {lt.element_type} and {rt.element_type}")
+        if lt.shape[0] != -1 and rt.shape[0] != -1 and lt.shape[0] != rt.shape[0]:
+            raise TypeError(f"linalg.dot: operand lengths must match, "
+                            f"got {lt.shape} and {rt.shape}")
+        self._out_type = lt.element_type
+
+    def infer_type(self):
+        return self._out_type
+
+    def get_children(self):
+        return [self.lhs, self.rhs]
+
+
+class LinalgReduceElement(Value):
+    """Placeholder for the current element in a reduce body."""
+
+    def __init__(self, element_type):
+        super().__init__()
+        self._t = element_type
+
+    def infer_type(self):
+        return self._t
+
+
+class LinalgReduceAccumulator(Value):
+    """Placeholder for the running accumulator in a reduce body."""
+
+    def __init__(self, element_type):
+        super().__init__()
+        self._t = element_type
+
+    def infer_type(self):
+        return self._t
+
+
+class LinalgReduce(Value):
+    """Fold of a 1-D tensor: acc = init; acc = fn(element, acc) per element."""
+
+    def __init__(self, input: Value, init: Value, fn):
+        super().__init__()
+        self.input, self.init = input, init
+        it = input.infer_type()
+        if not isinstance(it, TensorType) or it.ndim != 1:
+            raise TypeError(f"linalg.reduce: input must be a 1D tensor, got {it}")
+        self._element_type = it.element_type
+        init_t = init.infer_type()
+        if not isinstance(init_t, ScalarType) or init_t != self._element_type:
+            raise TypeError(f"linalg.reduce: init must be a scalar of element type "
+                            f"{self._element_type}, got {init_t}")
+        self.element = LinalgReduceElement(self._element_type)
+        self.accumulator = LinalgReduceAccumulator(self._element_type)
+        self.body = fn(self.element, self.accumulator)
+        bt = self.body.infer_type()
+        if bt != self._element_type:
+            raise TypeError(f"linalg.reduce body must return element type "
+                            f"{self._element_type}, got {bt}")
+
+    def infer_type(self):
+        return self._element_type
+
+    def get_children(self):
+        # the body refers to placeholders only; it is matched, not executed
+        return [self.input, self.init]

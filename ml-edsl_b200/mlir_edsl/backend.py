@@ -65,6 +65,35 @@ def _output_descriptor(shape, dtype):
     return c_types, [ptr, ptr, 0] + list(shape) + strides, buf
 
 
+_DEFAULT_INIT = {0: 0.0, 2: float("-inf"), 3: float("inf")}
+
+
+def _to_python(v):
+    """Scalar results are returned as Python numbers, as the reference's
+    ctypes scalar returns are."""
+    v = np.asarray(v)
+    return float(v) if v.dtype.kind == "f" else int(v)
+
+
+def _host_binop(op, dtype, a, b):
+    """Scalar arithmetic on reduction results: f32 (IEEE single) or i32
+    (wrapping; division truncates toward zero like arith.divsi)."""
+    if dtype == "f32":
+        a, b = np.float32(a), np.float32(b)
+        with np.errstate(all="ignore"):
+            return [a + b, a - b, a * b, a / b][op]
+    a, b = int(a), int(b)
+    if op == 3:
+        if b == 0:
+            raise ZeroDivisionError("i32 division by zero")
+        q = abs(a) // abs(b)
+        r = q if (a >= 0) == (b >= 0) else -q
+    else:
+        r = [a + b, a - b, a * b][op]
+    r &= 0xFFFFFFFF
+    return np.int32(r - (1 << 32) if r >= 1 << 31 else r)
+
+
 def _memref_symbol(step) -> Union[str, None]:
     """The memref entry point implementing a single step, if one exists."""
     if step.op == "gemm_f32":
@@ -105,28 +134,66 @@ class B200Backend:
     def execute_function(self, name: str, *args):
         param_types, return_type = self._signatures[name]
         plan = self._plans[name]
-        if not isinstance(return_type, TensorType):
-            raise RuntimeError(f"execute_function: b200 target returns tensors, got {return_type}")
-        arrays = []
+        values = []
         for pt, val in zip(param_types, args):
-            expected = SCALAR_TYPE_TO_NUMPY_DTYPE[pt.element_type.kind]
-            if val.dtype != expected:
-                raise TypeError(f"ndarray dtype {val.dtype} does not match expected "
-                                f"{np.dtype(expected)} for {pt}")
-            arrays.append(np.ascontiguousarray(val))
+            if isinstance(pt, TensorType):
+                expected = SCALAR_TYPE_TO_NUMPY_DTYPE[pt.element_type.kind]
+                if val.dtype != expected:
+                    raise TypeError(f"ndarray dtype {val.dtype} does not match expected "
+                                    f"{np.dtype(expected)} for {pt}")
+                values.append(np.ascontiguousarray(val))
+            else:
+                values.append(SCALAR_TYPE_TO_NUMPY_DTYPE[pt.kind](val))
         before = _native.launch_count()
         try:
             if plan.output.kind == "param":
-                return arrays[plan.output.index].copy()
+                v = values[plan.output.index]
+                return v.copy() if isinstance(v, np.ndarray) else _to_python(v)
+            if plan.output.kind == "const":
+                return _to_python(plan.consts[plan.output.index])
             if len(plan.steps) == 1 and all(r.kind == "param" for r in plan.steps[0].inputs):
-                sym = _memref_symbol(plan.steps[0])
+                step = plan.steps[0]
+                if step.shape == ():
+                    return self._run_scalar_host(step, values)
+                sym = _memref_symbol(step)
                 if sym is not None:
-                    return self._run_memref(sym, plan, param_types, arrays)
-            return self._run_device(plan, param_types, arrays)
+                    return self._run_memref(sym, plan, param_types, values)
+            return self._run_device(plan, param_types, values)
         finally:
             self.last_launches = _native.launch_count() - before
 
     execute_gpu_function = execute_function
+
+    def _run_scalar_host(self, step, values):
+        """One dot / reduce over parameters: the reference's scalar-returning
+        memref ABI where a symbol exists, else the host entry point."""
+        L = _native.lib()
+        vp = ctypes.c_void_p
+        desc1 = lambda a: [vp(a.ctypes.data), vp(a.ctypes.data), 0, a.size, 1]
+        ins = [values[r.index] for r in step.inputs]
+        f32 = step.dtype == "f32"
+        sym, res_t = None, ctypes.c_float if f32 else ctypes.c_int32
+        if step.op.startswith("dot"):
+            sym = "b200_memref_dot_f32" if f32 else "b200_memref_dot_i32"
+        elif f32 and step.init == _DEFAULT_INIT.get(step.red_op):
+            sym = {0: "b200_memref_sum_f32", 2: "b200_memref_max_f32",
+                   3: "b200_memref_min_f32"}.get(step.red_op)
+        if sym is not None:
+            args = sum((desc1(a) for a in ins), [])
+            types = [vp, vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64] * len(ins)
+            fn_ptr = ctypes.cast(getattr(L, sym), ctypes.c_void_p).value
+            r = ctypes.CFUNCTYPE(res_t, *types)(fn_ptr)(*args)
+            _native.check_last()
+            return float(np.float32(r)) if f32 else int(r)
+        out = np.zeros(1, np.float32 if f32 else np.int32)
+        x = ins[0]
+        if f32:
+            _native.check(L.b200_reduce_f32_host(vp(x.ctypes.data), x.size, step.red_op,
+                                                 float(step.init), vp(out.ctypes.data)))
+        else:
+            _native.check(L.b200_reduce_i32_host(vp(x.ctypes.data), x.size, step.red_op,
+                                                 int(step.init), vp(out.ctypes.data)))
+        return _to_python(out[0])
 
     def _run_memref(self, sym, plan, param_types, arrays):
         step = plan.steps[0]
@@ -157,7 +224,8 @@ class B200Backend:
 
         try:
             dparams = {}
-            needed = {r.index for s in plan.steps for r in s.inputs if r.kind == "param"}
+            needed = {r.index for s in plan.steps for r in s.inputs
+                      if r.kind == "param" and s.op != "scalar_op"}
             for i in sorted(needed):
                 a = arrays[i]
                 p = dmalloc(a.nbytes)
@@ -172,8 +240,8 @@ class B200Backend:
                 return arrays[r.index].shape if r.kind == "param" else plan.steps[r.index].shape
 
             for s in plan.steps:
-                nelem = int(np.prod(s.shape))
-                out = dmalloc(nelem * 4)
+                nelem = int(np.prod(s.shape))  # 1 for scalar results
+                out = dmalloc(nelem * 4) if s.op != "scalar_op" else None
                 douts.append(out)
                 if s.op in ("gemm_f32", "gemm_i32"):
                     a, b = s.inputs[0], s.inputs[1]
@@ -199,11 +267,49 @@ class B200Backend:
                     M, N = s.shape
                     _native.check(L.b200_bias_add_i32(dref(s.inputs[0]), N, dref(s.inputs[1]),
                                                       out, N, M, N, None))
+                elif s.op in ("dot_f32", "dot_i32"):
+                    a, b = s.inputs
+                    n = int(np.prod(shape_of(a)))
+                    fn = L.b200_dot_f32 if s.dtype == "f32" else L.b200_dot_i32
+                    _native.check(fn(dref(a), dref(b), n, out, None))
+                elif s.op in ("reduce_f32", "reduce_i32"):
+                    x = s.inputs[0]
+                    n = int(np.prod(shape_of(x)))
+                    if s.dtype == "f32":
+                        _native.check(L.b200_reduce_f32(dref(x), n, s.red_op, float(s.init), out,
+                                                        None))
+                    else:
+                        _native.check(L.b200_reduce_i32(dref(x), n, s.red_op, int(s.init), out,
+                                                        None))
+                elif s.op == "scalar_op":
+                    pass  # evaluated on the host below
                 else:
                     raise RuntimeError(f"unknown step {s.op}")
-            final = plan.steps[plan.output.index]
-            res = np.empty(final.shape, np.float32 if final.dtype == "f32" else np.int32)
             _native.check(L.b200_stream_sync(None))
+            host_vals = {}
+
+            def scalar(r: Ref):
+                if r.kind == "const":
+                    return plan.consts[r.index]
+                if r.kind == "param":
+                    return arrays[r.index]
+                if r.index not in host_vals:
+                    st = plan.steps[r.index]
+                    if st.op == "scalar_op":
+                        host_vals[r.index] = _host_binop(st.scalar_op, st.dtype,
+                                                         scalar(st.inputs[0]),
+                                                         scalar(st.inputs[1]))
+                    else:
+                        v = np.zeros(1, np.float32 if st.dtype == "f32" else np.int32)
+                        _native.check(L.b200_memcpy_d2h(v.ctypes.data_as(ctypes.c_void_p),
+                                                        douts[r.index], v.nbytes))
+                        host_vals[r.index] = v[0]
+                return host_vals[r.index]
+
+            final = plan.steps[plan.output.index]
+            if final.shape == ():
+                return _to_python(scalar(plan.output))
+            res = np.empty(final.shape, np.float32 if final.dtype == "f32" else np.int32)
             _native.check(L.b200_memcpy_d2h(res.ctypes.data_as(ctypes.c_void_p),
                                             douts[plan.output.index], res.nbytes))
             return res

@@ -50,3 +50,75 @@ def mul(left, right):
 
 def div(left, right):
     return _dispatch_binary_op(DIV, to_value(left), to_value(right))
+
+
+# --------------------------------------------------------------------------
+# Comparisons, If, dot and reductions
+# (reference: mlir_edsl/ops/comparison.py, ops/control_flow.py,
+#  ops/linalg.py:7-25 dot, :88-175 reduce / tensor_sum / tensor_max / tensor_min)
+def _cmp(pred, left, right):
+    from .ast import CompareOp
+    return CompareOp(pred, to_value(left), to_value(right))
+
+
+def lt(left, right):
+    return _cmp("lt", left, right)
+
+
+def le(left, right):
+    return _cmp("le", left, right)
+
+
+def gt(left, right):
+    return _cmp("gt", left, right)
+
+
+def ge(left, right):
+    return _cmp("ge", left, right)
+
+
+def eq(left, right):
+    return _cmp("eq", left, right)
+
+
+def ne(left, right):
+    return _cmp("ne", left, right)
+
+
+def If(cond, then_value, else_value):
+    """Value selection (the value form of the reference's If)."""
+    from .ast import IfOp
+    return IfOp(cond, to_value(then_value), to_value(else_value))
+
+
+def dot(a: Value, b: Value):
+    """Dot product of two 1-D tensors -> scalar."""
+    from .ast import LinalgDot
+    return LinalgDot(a, b)
+
+
+def reduce(arr: Value, init: Value, fn):
+    """Fold a 1-D tensor: acc = init; acc = fn(element, acc) for each element."""
+    from .ast import LinalgReduce
+    return LinalgReduce(arr, to_value(init), fn)
+
+
+def tensor_sum(arr: Value):
+    """Sum of a 1-D tensor (init 0)."""
+    from .ast import Constant, LinalgReduce
+    zero = Constant(0.0) if arr.infer_type().element_type.is_float() else Constant(0)
+    return LinalgReduce(arr, zero, lambda elem, acc: acc + elem)
+
+
+def tensor_max(arr: Value):
+    """Maximum of a 1-D f32 tensor (init -inf; NaN elements never win)."""
+    from .ast import Constant, IfOp, LinalgReduce
+    return LinalgReduce(arr, Constant(float("-inf")),
+                        lambda elem, acc: IfOp(elem > acc, elem, acc))
+
+
+def tensor_min(arr: Value):
+    """Minimum of a 1-D f32 tensor (init +inf)."""
+    from .ast import Constant, IfOp, LinalgReduce
+    return LinalgReduce(arr, Constant(float("inf")),
+                        lambda elem, acc: IfOp(elem < acc, elem, acc))

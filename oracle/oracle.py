@@ -17,6 +17,9 @@ LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
 
 ACT_NONE, ACT_RELU, ACT_LEAKY_RELU = 0, 1, 2
 MODE_AUTO, MODE_FMA, MODE_MULADD = -1, 0, 1
+REDUCE_SUM, REDUCE_PROD, REDUCE_MAX, REDUCE_MIN = 0, 1, 2, 3
+REDUCE_INIT = {REDUCE_SUM: 0.0, REDUCE_PROD: 1.0, REDUCE_MAX: float("-inf"),
+               REDUCE_MIN: float("inf")}
 
 _lib = None
 
@@ -43,6 +46,14 @@ def _load():
         lib.oracle_matmul_i32.restype = None
         lib.oracle_bias_act_f32.argtypes = [f32p, f32p, f32p, i64, i64, ctypes.c_int, ctypes.c_float]
         lib.oracle_bias_act_f32.restype = None
+        lib.oracle_reduce_f32.argtypes = [f32p, i64, ctypes.c_int, ctypes.c_float]
+        lib.oracle_reduce_f32.restype = ctypes.c_float
+        lib.oracle_reduce_i32.argtypes = [i32p, i64, ctypes.c_int, ctypes.c_int32]
+        lib.oracle_reduce_i32.restype = ctypes.c_int32
+        lib.oracle_dot_f32.argtypes = [f32p, f32p, i64]
+        lib.oracle_dot_f32.restype = ctypes.c_float
+        lib.oracle_dot_i32.argtypes = [i32p, i32p, i64]
+        lib.oracle_dot_i32.restype = ctypes.c_int32
         lib.oracle_fma_mode.argtypes = [i64, i64, i64]
         lib.oracle_fma_mode.restype = ctypes.c_int
         _lib = lib
@@ -96,6 +107,39 @@ def bias_act_f32(X, b=None, act=ACT_NONE, alpha=0.0):
     _load().oracle_bias_act_f32(_p(X, ctypes.c_float), _p(b, ctypes.c_float),
                                 _p(Y, ctypes.c_float), M, N, act, alpha)
     return Y
+
+
+def reduce_f32(x, op, init=None):
+    """Sequential fold of a 1-D f32 tensor (linalg.reduce semantics)."""
+    x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    init = REDUCE_INIT[op] if init is None else init
+    return np.float32(_load().oracle_reduce_f32(_p(x, ctypes.c_float), x.size, op, init))
+
+
+def reduce_i32(x, op, init=None):
+    x = np.ascontiguousarray(x, dtype=np.int32).ravel()
+    if init is None:
+        init = {REDUCE_SUM: 0, REDUCE_PROD: 1, REDUCE_MAX: -2**31, REDUCE_MIN: 2**31 - 1}[op]
+    return np.int32(_load().oracle_reduce_i32(_p(x, ctypes.c_int32), x.size, op, init))
+
+
+def dot_f32(a, b):
+    a = np.ascontiguousarray(a, dtype=np.float32).ravel()
+    b = np.ascontiguousarray(b, dtype=np.float32).ravel()
+    return np.float32(_load().oracle_dot_f32(_p(a, ctypes.c_float), _p(b, ctypes.c_float), a.size))
+
+
+def dot_i32(a, b):
+    a = np.ascontiguousarray(a, dtype=np.int32).ravel()
+    b = np.ascontiguousarray(b, dtype=np.int32).ravel()
+    return np.int32(_load().oracle_dot_i32(_p(a, ctypes.c_int32), _p(b, ctypes.c_int32), a.size))
+
+
+def sum_bound(x):
+    """Tolerance for a reordered f32 sum: both orders are within
+    n * 2^-24 * sum|x| of the exact sum (standard recursive-summation bound)."""
+    x = np.asarray(x, np.float64).ravel()
+    return 2.0 * max(x.size, 1) * 2.0 ** -24 * float(np.sum(np.abs(x))) + 1e-30
 
 
 def f32_bound(K, A, B):

@@ -186,3 +186,51 @@ void oracle_bias_act_f32(const float* X, const float* b, float* Y, int64_t M, in
       Y[i * N + j] = act_apply(y, act, alpha);
     }
 }
+
+/* ---- 1-D reductions and dot: the sequential fold linalg.reduce / linalg.dot
+ * define. dot: 0-D accumulator filled with 0, acc = acc + a[i]*b[i] with the
+ * product rounded first (cpp/src/builders/LinalgBuilder.cpp:66-104).
+ * reduce: acc = init, then acc = body(x[i], acc) for i ascending
+ * (LinalgBuilder.cpp:241-279) with the library's bodies
+ * (mlir_edsl/ops/linalg.py:104-175): sum acc + x, product acc * x,
+ * max If(x > acc, x, acc), min If(x < acc, x, acc). */
+enum { RED_SUM = 0, RED_PROD = 1, RED_MAX = 2, RED_MIN = 3 };
+
+float oracle_reduce_f32(const float* x, int64_t n, int op, float init) {
+  float acc = init;
+  for (int64_t i = 0; i < n; ++i) {
+    const float v = x[i];
+    if (op == RED_SUM) acc = acc + v;
+    else if (op == RED_PROD) acc = acc * v;
+    else if (op == RED_MAX) acc = (v > acc) ? v : acc;
+    else acc = (v < acc) ? v : acc;
+  }
+  return acc;
+}
+
+int32_t oracle_reduce_i32(const int32_t* x, int64_t n, int op, int32_t init) {
+  uint32_t acc = (uint32_t)init;
+  for (int64_t i = 0; i < n; ++i) {
+    const int32_t v = x[i];
+    if (op == RED_SUM) acc += (uint32_t)v;
+    else if (op == RED_PROD) acc *= (uint32_t)v;
+    else if (op == RED_MAX) acc = (v > (int32_t)acc) ? (uint32_t)v : acc;
+    else acc = (v < (int32_t)acc) ? (uint32_t)v : acc;
+  }
+  return (int32_t)acc;
+}
+
+float oracle_dot_f32(const float* a, const float* b, int64_t n) {
+  float acc = 0.0f;
+  for (int64_t i = 0; i < n; ++i) {
+    const float p = a[i] * b[i];
+    acc = acc + p;
+  }
+  return acc;
+}
+
+int32_t oracle_dot_i32(const int32_t* a, const int32_t* b, int64_t n) {
+  uint32_t acc = 0u;
+  for (int64_t i = 0; i < n; ++i) acc += (uint32_t)a[i] * (uint32_t)b[i];
+  return (int32_t)acc;
+}

@@ -75,6 +75,41 @@ def main():
              {"X": Xr}, np.maximum(f64(Xr), 0.0), rtol=1e-5),
         case("leaky_relu_2d", "tests/linalg/test_map_execution.py:151-161", "leaky_relu",
              {"X": Xr}, np.where(Xr > 0, f64(Xr), f64(Xr) * 0.1), rtol=1e-4, alpha=0.1),
+        # linalg.dot / reduce (scalar results)
+        case("dot_all_ones", "tests/linalg/test_dot_execution.py:18-26", "dot",
+             {"a": np.ones(4, f), "b": np.ones(4, f)}, 4.0, atol=1e-5),
+        case("dot_known", "tests/linalg/test_dot_execution.py:28-36", "dot",
+             {"a": np.array([1, 2, 3, 4], f), "b": np.ones(4, f)}, 10.0, atol=1e-5),
+        case("dot_squares", "tests/linalg/test_dot_execution.py:38-46", "dot",
+             {"a": np.array([1, 2, 3], f), "b": np.array([1, 2, 3], f)}, 14.0, atol=1e-5),
+        case("dot_i32", "tests/linalg/test_dot_execution.py:48-56", "dot_i32",
+             {"a": np.array([1, 2, 3, 4], np.int32), "b": np.array([4, 3, 2, 1], np.int32)}, 20),
+        case("dot_zeros", "tests/linalg/test_dot_execution.py:58-66", "dot",
+             {"a": np.array([1, 2, 3], f), "b": np.zeros(3, f)}, 0.0, atol=1e-5),
+        case("dot_single", "tests/linalg/test_dot_execution.py:68-76", "dot",
+             {"a": np.array([3.0], f), "b": np.array([7.0], f)}, 21.0, atol=1e-5),
+        case("sum_positive", "tests/linalg/test_reduce_execution.py:21-27", "sum",
+             {"a": np.array([1, 2, 3, 4], f)}, 10.0, atol=1e-5),
+        case("sum_negatives", "tests/linalg/test_reduce_execution.py:29-35", "sum",
+             {"a": np.array([-1, 2, -3, 4], f)}, 2.0, atol=1e-5),
+        case("sum_single", "tests/linalg/test_reduce_execution.py:45-51", "sum",
+             {"a": np.array([42.0], f)}, 42.0, atol=1e-5),
+        case("sum_8", "tests/linalg/test_reduce_execution.py:53-59", "sum",
+             {"a": np.arange(1, 9, dtype=f)}, 36.0, atol=1e-4),
+        case("max_positive", "tests/linalg/test_reduce_execution.py:67-73", "max",
+             {"a": np.array([1, 4, 2, 3], f)}, 4.0, atol=1e-5),
+        case("max_negatives", "tests/linalg/test_reduce_execution.py:75-81", "max",
+             {"a": np.array([-1, -4, -2, -3], f)}, -1.0, atol=1e-5),
+        case("max_last", "tests/linalg/test_reduce_execution.py:91-97", "max",
+             {"a": np.array([1, 2, 3, 9], f)}, 9.0, atol=1e-5),
+        case("min_positive", "tests/linalg/test_reduce_execution.py:105-111", "min",
+             {"a": np.array([3, 1, 4, 2], f)}, 1.0, atol=1e-5),
+        case("min_negatives", "tests/linalg/test_reduce_execution.py:113-119", "min",
+             {"a": np.array([1, -2, 3, -4], f)}, -4.0, atol=1e-5),
+        case("min_first", "tests/linalg/test_reduce_execution.py:129-135", "min",
+             {"a": np.array([-9, 2, 3, 4], f)}, -9.0, atol=1e-5),
+        case("product", "tests/linalg/test_reduce_execution.py:151-157", "prod",
+             {"a": np.array([1, 2, 3, 4], f)}, 24.0, atol=1e-4),
     ]
     with open(os.path.join(HERE, "known_answers.json"), "w") as fh:
         json.dump({"generator": "tests/golden/make_golden.py", "cases": cases}, fh, indent=1)

@@ -269,3 +269,67 @@ def test_variant_cache_per_dyn_shape():
     assert set(mm._compiled_variants) == {((2, 3), (3, 4)), ((5, 6), (6, 7))}
     names = {v.name for v in mm._compiled_variants.values()}
     assert all("__" in n for n in names)
+
+
+# ------------------------------------------------------------------ dot / reduce
+def test_dot_validation():
+    """reference: tests/linalg/test_dot_execution.py:84-100"""
+    from mlir_edsl import dot
+    from mlir_edsl.ast import Constant
+    with pytest.raises(TypeError, match="1D tensor"):
+        dot(Constant(5), Constant(5))
+    with pytest.raises(TypeError, match="element types must match"):
+        dot(Parameter("a", Tensor[f32, 2]), Parameter("b", Tensor[i32, 2]))
+    with pytest.raises(TypeError, match="lengths must match"):
+        dot(Parameter("a", Tensor[f32, 3]), Parameter("b", Tensor[f32, 4]))
+
+
+def test_reduce_validation():
+    """reference: tests/linalg/test_reduce_execution.py:173-197"""
+    from mlir_edsl import reduce, to_value
+    with pytest.raises(TypeError, match="1D tensor"):
+        reduce(Parameter("a", Tensor[f32, 2, 2]), to_value(0.0), lambda e, a: a + e)
+    with pytest.raises(TypeError, match="init must be a scalar"):
+        reduce(Parameter("a", Tensor[f32, 3]), to_value(0), lambda e, a: a + e)
+    with pytest.raises(TypeError, match="body must return element type"):
+        reduce(Parameter("a", Tensor[f32, 3]), to_value(0.0), lambda e, a: to_value(1))
+
+
+@pytest.mark.parametrize("body,red", [
+    ("tensor_sum(a)", 0), ("tensor_max(a)", 2), ("tensor_min(a)", 3),
+    ("reduce(a, to_value(1.0), lambda e, acc: acc * e)", 1),
+    ("reduce(a, to_value(0.0), lambda e, acc: e + acc)", 0),
+    ("reduce(a, to_value(0.0), lambda e, acc: If(acc < e, e, acc))", 2),
+])
+def test_reduce_bodies_lower(body, red):
+    import mlir_edsl as m
+    ns = {}
+    exec(f"def f(a: Tensor[f32, 8]) -> f32:\n    return {body}\n", vars(m), ns)
+    p = _plan(ns["f"])
+    assert p.steps[0].op == "reduce_f32" and p.steps[0].red_op == red
+
+
+def test_unsupported_reduce_body_raises():
+    import mlir_edsl as m
+    ns = {}
+    exec("def f(a: Tensor[f32, 8]) -> f32:\n"
+         "    return reduce(a, to_value(0.0), lambda e, acc: acc + e * e)\n", vars(m), ns)
+    with pytest.raises(NotImplementedError, match="reduce bodies"):
+        _plan(ns["f"])
+
+
+def test_scalar_tail_is_a_host_step():
+    from mlir_edsl import tensor_sum, to_value
+
+    def f(a: Tensor[f32, 4]) -> f32:
+        return tensor_sum(a) * to_value(2.0)
+    p = _plan(f)
+    assert [s.op for s in p.steps] == ["reduce_f32", "scalar_op"]
+    assert p.consts == [2.0]
+
+
+def test_host_binop_i32_semantics():
+    from mlir_edsl.backend import _host_binop
+    assert _host_binop(0, "i32", 2**31 - 1, 1) == -2**31
+    assert _host_binop(3, "i32", -7, 2) == -3  # truncates toward zero
+    assert _host_binop(2, "f32", 0.1, 3.0) == np.float32(np.float32(0.1) * np.float32(3.0))

@@ -8,8 +8,8 @@ import numpy as np
 import pytest
 
 import oracle
-from mlir_edsl import (DYN, Tensor, f32, get_backend, i32, leaky_relu, matmul, ml_function,
-                       relu)
+from mlir_edsl import (DYN, Tensor, dot, f32, get_backend, i32, leaky_relu, matmul, ml_function,
+                       reduce, relu, tensor_max, tensor_min, tensor_sum, to_value)
 
 pytestmark = pytest.mark.gpu
 
@@ -39,6 +39,23 @@ def _fn_for(c):
         def fn(X: Tensor[f32, M, K], W: Tensor[f32, K, N], b: Tensor[f32, N]) -> Tensor[f32, M, N]:
             return X @ W + b
         return fn, [ins["X"], ins["W"], ins["b"]]
+    if op in ("dot", "dot_i32"):
+        dt = i32 if op == "dot_i32" else f32
+        n = shp["a"][0]
+
+        @ml_function(target="b200")
+        def fn(a: Tensor[dt, n], b: Tensor[dt, n]) -> dt:
+            return dot(a, b)
+        return fn, [ins["a"], ins["b"]]
+    if op in ("sum", "max", "min", "prod"):
+        n = shp["a"][0]
+        body = {"sum": tensor_sum, "max": tensor_max, "min": tensor_min,
+                "prod": lambda a: reduce(a, to_value(1.0), lambda e, acc: acc * e)}[op]
+
+        @ml_function(target="b200")
+        def fn(a: Tensor[f32, n]) -> f32:
+            return body(a)
+        return fn, [ins["a"]]
     if op == "bias_add":
         M, N = shp["X"]
 
@@ -70,7 +87,7 @@ def test_known_answers_through_frontend(cuda, c):
     fn, args = _fn_for(c)
     got = fn(*args)
     exp = np.array(c["expected"])
-    if c["op"] == "matmul_i32":
+    if c["op"] in ("matmul_i32", "dot_i32"):
         np.testing.assert_array_equal(got, exp)
     else:
         np.testing.assert_allclose(got, exp, rtol=c["rtol"], atol=max(c["atol"], 1e-6))

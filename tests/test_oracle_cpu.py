@@ -30,6 +30,14 @@ def run_oracle(c):
         return oracle.dense_f32(ins["X"], ins["W"], ins["b"])
     if op == "bias_add":
         return oracle.bias_act_f32(ins["X"], ins["b"])
+    if op == "dot":
+        return oracle.dot_f32(ins["a"], ins["b"])
+    if op == "dot_i32":
+        return oracle.dot_i32(ins["a"], ins["b"])
+    if op in ("sum", "max", "min", "prod"):
+        red = {"sum": oracle.REDUCE_SUM, "max": oracle.REDUCE_MAX, "min": oracle.REDUCE_MIN,
+               "prod": oracle.REDUCE_PROD}[op]
+        return oracle.reduce_f32(ins["a"], red)
     X = ins["X"]
     X2 = X.reshape(1, -1) if X.ndim == 1 else X
     act = oracle.ACT_RELU if op == "relu" else oracle.ACT_LEAKY_RELU
@@ -40,7 +48,7 @@ def run_oracle(c):
 def test_oracle_known_answers(c):
     got = run_oracle(c)
     exp = np.array(c["expected"])
-    if c["op"] == "matmul_i32":
+    if c["op"] in ("matmul_i32", "dot_i32"):
         np.testing.assert_array_equal(got, exp)
     else:
         np.testing.assert_allclose(got, exp, rtol=c["rtol"], atol=c["atol"])
@@ -139,3 +147,27 @@ def test_dense_1024_config_within_bound():
     Y = oracle.dense_f32(g["X"], g["W"], g["b"], act=oracle.ACT_RELU)
     exact = np.maximum(g["X"].astype(np.float64) @ g["W"] + g["b"], 0)
     assert np.max(np.abs(Y - exact)) <= oracle.f32_bound(1024, g["X"], g["W"])
+
+
+def test_reductions_match_float64_and_numpy():
+    rng = np.random.default_rng(12)
+    x = rng.standard_normal(100_003).astype(np.float32)
+    y = rng.standard_normal(100_003).astype(np.float32)
+    assert abs(oracle.reduce_f32(x, oracle.REDUCE_SUM) - x.astype(np.float64).sum()) <= \
+        oracle.sum_bound(x)
+    assert oracle.reduce_f32(x, oracle.REDUCE_MAX) == x.max()
+    assert oracle.reduce_f32(x, oracle.REDUCE_MIN) == x.min()
+    exact = float(np.dot(x.astype(np.float64), y.astype(np.float64)))
+    assert abs(oracle.dot_f32(x, y) - exact) <= oracle.sum_bound(x * y)
+
+
+def test_max_skips_nan_like_the_reference_body():
+    x = np.array([1.0, np.nan, 5.0, 2.0], np.float32)
+    assert oracle.reduce_f32(x, oracle.REDUCE_MAX) == 5.0  # If(elem > acc, ...) is false for NaN
+    assert oracle.reduce_f32(x, oracle.REDUCE_MIN) == 1.0
+
+
+def test_i32_reductions_wrap():
+    x = np.array([2**31 - 1, 1, 5], np.int32)
+    assert oracle.reduce_i32(x, oracle.REDUCE_SUM) == np.int32(-2**31 + 5)
+    assert oracle.dot_i32(np.array([65536], np.int32), np.array([65536], np.int32)) == 0
