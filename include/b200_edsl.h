@@ -163,6 +163,15 @@ int b200_gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* w
                               const float* wloT, const float* b, float* Y, int64_t ldy, int64_t M,
                               int64_t N, int64_t K, int act, float alpha, void* stream);
 
+/* Y = act(X @ W + b) with W given pre-split (b200_tf32_split_transpose):
+ * the weight-stationary form of b200_dense_f32, which skips the W split on
+ * every call. X is split by the HBM-bound split pass into runtime scratch
+ * (or, with B200_FUSE_A=1 and 16-byte aligned X rows, inside the GEMM);
+ * few-tile problems add a split-K reduction. */
+int b200_dense_f32_wsplit(const float* X, int64_t ldx, const float* whiT, const float* wloT,
+                          const float* b, float* Y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                          int act, float alpha, void* stream);
+
 /* Device buffers on the current device (synchronous copies). */
 int b200_malloc(void** ptr, int64_t bytes);
 int b200_free(void* ptr);

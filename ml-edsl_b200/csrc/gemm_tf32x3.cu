@@ -178,7 +178,32 @@ struct Epilogue {
   int64_t split_stride;  // split-K: split s writes its partial at Y + s * split_stride
 };
 
+// UMMA shared-memory descriptors of the four operand tiles of stage base `st`
+// at k-step k (8 tf32 = 32 bytes along the row).
 template <class Cfg>
+struct UmmaDesc {
+  static __device__ __forceinline__ uint64_t at(uint32_t addr) {
+    return umma_desc_k<Cfg::UmmaLayout, Cfg::SBO>(addr);
+  }
+  static __device__ __forceinline__ uint64_t a_hi(uint32_t st, int k) { return at(st + k * 32); }
+  static __device__ __forceinline__ uint64_t a_lo(uint32_t st, int k) {
+    return at(st + Cfg::ATileBytes + k * 32);
+  }
+  static __device__ __forceinline__ uint64_t b_hi(uint32_t st, int k) {
+    return at(st + 2 * Cfg::ATileBytes + k * 32);
+  }
+  static __device__ __forceinline__ uint64_t b_lo(uint32_t st, int k) {
+    return at(st + 2 * Cfg::ATileBytes + Cfg::BTileBytes + k * 32);
+  }
+};
+
+// kFusedA: the A operand arrives as raw f32 X tiles (one TMA load into the
+// A_hi slot). The tensor core reads a tf32 operand from f32 bits by ignoring
+// the low 13 mantissa bits, so the raw tile serves as A_hi unchanged; the
+// epilogue warps derive A_lo = x - hi into the A_lo slot and release it to
+// the MMA through conv[s]. The MMA issues the two products that use A_hi as
+// soon as the tile lands and the lo * B_hi product after conv[s].
+template <class Cfg, bool kFusedA>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAhi,
                        const __grid_constant__ CUtensorMap tmAlo,
@@ -192,7 +217,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + Cfg::Stages;                                   // MMA -> TMA
   uint64_t* tfull = empty + Cfg::Stages;   // MMA -> epilogue: chunk accumulator ready
   uint64_t* tempty = tfull + 2;        // epilogue -> MMA: chunk accumulator drained
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* conv = tempty + 2;         // epilogue -> MMA: A tile split (kFusedA)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(conv + Cfg::Stages);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* sbias = reinterpret_cast<float*>(smem + Cfg::BiasOffset);
 
@@ -223,6 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], kEpiWarps);
     }
+    for (int s = 0; s < Cfg::Stages; ++s) mbar_init(&conv[s], kEpiWarps);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -254,10 +281,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             !mbar_wait(&empty[s], (round - 1) & 1, status, kDevTimeoutEmpty, abort_flag))
           break;
         uint8_t* st = smem + s * Cfg::StageBytes;
-        mbar_arrive_expect_tx(&full[s], Cfg::StageBytes);
         const int kx = (kb0 + kb) * Cfg::BK;
-        tma_load_2d(st, &tmAhi, &full[s], kx, m0);
-        tma_load_2d(st + Cfg::ATileBytes, &tmAlo, &full[s], kx, m0);
+        if constexpr (kFusedA) {
+          mbar_arrive_expect_tx(&full[s], Cfg::ATileBytes + 2 * Cfg::BTileBytes);
+          tma_load_2d(st, &tmAhi, &full[s], kx, m0);  // raw f32 X tile
+        } else {
+          mbar_arrive_expect_tx(&full[s], Cfg::StageBytes);
+          tma_load_2d(st, &tmAhi, &full[s], kx, m0);
+          tma_load_2d(st + Cfg::ATileBytes, &tmAlo, &full[s], kx, m0);
+        }
         tma_load_2d(st + 2 * Cfg::ATileBytes, &tmBhi, &full[s], kx, n0);
         tma_load_2d(st + 2 * Cfg::ATileBytes + Cfg::BTileBytes, &tmBlo, &full[s], kx, n0);
       }
@@ -283,15 +315,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * kBN;
         const uint32_t st = smem_u32(smem + s * Cfg::StageBytes);
+        using D = UmmaDesc<Cfg>;
+        if constexpr (kFusedA) {
 #pragma unroll
-        for (int k = 0; k < Cfg::BK / 8; ++k) {  // tf32 UMMA consumes K = 8 (32 B)
-          const uint64_t a_hi = umma_desc_k<Cfg::UmmaLayout, Cfg::SBO>(st + k * 32);
-          const uint64_t a_lo = umma_desc_k<Cfg::UmmaLayout, Cfg::SBO>(st + Cfg::ATileBytes + k * 32);
-          const uint64_t b_hi = umma_desc_k<Cfg::UmmaLayout, Cfg::SBO>(st + 2 * Cfg::ATileBytes + k * 32);
-          const uint64_t b_lo = umma_desc_k<Cfg::UmmaLayout, Cfg::SBO>(st + 2 * Cfg::ATileBytes + Cfg::BTileBytes + k * 32);
-          umma_tf32(d_tmem, a_lo, b_hi, idesc, (chunk_start && k == 0) ? 0u : 1u);
-          umma_tf32(d_tmem, a_hi, b_lo, idesc, 1u);
-          umma_tf32(d_tmem, a_hi, b_hi, idesc, 1u);
+          for (int k = 0; k < Cfg::BK / 8; ++k) {
+            umma_tf32(d_tmem, D::a_hi(st, k), D::b_lo(st, k), idesc,
+                      (chunk_start && k == 0) ? 0u : 1u);
+            umma_tf32(d_tmem, D::a_hi(st, k), D::b_hi(st, k), idesc, 1u);
+          }
+          if (!mbar_wait(&conv[s], round & 1, status, kDevTimeoutFull, abort_flag)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < Cfg::BK / 8; ++k)
+            umma_tf32(d_tmem, D::a_lo(st, k), D::b_hi(st, k), idesc, 1u);
+        } else {
+#pragma unroll
+          for (int k = 0; k < Cfg::BK / 8; ++k) {  // tf32 UMMA consumes K = 8 (32 B)
+            umma_tf32(d_tmem, D::a_lo(st, k), D::b_hi(st, k), idesc,
+                      (chunk_start && k == 0) ? 0u : 1u);
+            umma_tf32(d_tmem, D::a_hi(st, k), D::b_lo(st, k), idesc, 1u);
+            umma_tf32(d_tmem, D::a_hi(st, k), D::b_hi(st, k), idesc, 1u);
+          }
         }
         umma_commit(&empty[s]);  // stage s may be refilled once these MMAs finish
         if (chunk_end) umma_commit(&tfull[buf]);
@@ -307,13 +351,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
     bool ok = true;
-#pragma unroll 1
-    for (int c = 0; c < num_chunks; ++c) {
+    // Adds chunk c's partial sums (TMEM buffer c % 2) into acc, frees it.
+    auto drain = [&](int c) -> bool {
       const int buf = c & 1;
-      if (!mbar_wait(&tfull[buf], (c >> 1) & 1, status, kDevTimeoutAccum, abort_flag)) {
-        ok = false;
-        break;
-      }
+      if (!mbar_wait(&tfull[buf], (c >> 1) & 1, status, kDevTimeoutAccum, abort_flag))
+        return false;
       tc_fence_after();
       const uint32_t taddr = tmem_base + lane_off + buf * kBN + half * 128;
 #pragma unroll
@@ -327,6 +369,45 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
+      return true;
+    };
+    if constexpr (kFusedA) {
+      // Split every A tile as it lands; drain chunk c once the conversion has
+      // run kDrainLag k-blocks past its last one, so the MMA always has split
+      // tiles queued while the drain runs.
+      constexpr int kDrainLag = 2;
+      const int et = threadIdx.x - 64;  // 0..255
+      int next = 0;
+#pragma unroll 1
+      for (int kb = 0; kb < num_kb && ok; ++kb) {
+        const int s = kb % Cfg::Stages;
+        if (!mbar_wait(&full[s], (kb / Cfg::Stages) & 1, status, kDevTimeoutFull, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const float4* a = reinterpret_cast<const float4*>(smem + s * Cfg::StageBytes);
+        float4* lo = reinterpret_cast<float4*>(smem + s * Cfg::StageBytes + Cfg::ATileBytes);
+#pragma unroll
+        for (int i = et; i < Cfg::ATileBytes / 16; i += 32 * kEpiWarps) {
+          const float4 v = a[i];
+          float4 h, l;  // h is what the tensor core reads from v
+          tf32_split(v.x, h.x, l.x);
+          tf32_split(v.y, h.y, l.y);
+          tf32_split(v.z, h.z, l.z);
+          tf32_split(v.w, h.w, l.w);
+          lo[i] = l;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[s]);
+        while (ok && next < num_chunks &&
+               min((next + 1) * Cfg::ChunkKB, num_kb) - 1 + kDrainLag <= kb)
+          ok = drain(next++);
+      }
+      while (ok && next < num_chunks) ok = drain(next++);
+    } else {
+#pragma unroll 1
+      for (int c = 0; c < num_chunks && ok; ++c) ok = drain(c);
     }
     if (ok && !*abort_flag) {
       const int64_t row = (int64_t)m0 + quarter * 32 + lane;
@@ -444,37 +525,60 @@ static int ring_variant() {
   return v;
 }
 
-template <class Cfg>
-static int launch_gemm(const float* xhi, const float* xlo, const float* whiT, const float* wloT,
-                       int64_t M, int64_t N, int64_t K, const Epilogue& ep, int splits,
-                       int* status, cudaStream_t stream) {
+template <class Cfg, bool kFusedA>
+static int launch_gemm(const CUtensorMap& ta_hi, const CUtensorMap& ta_lo,
+                       const CUtensorMap& tb_hi, const CUtensorMap& tb_lo, int64_t M, int64_t N,
+                       int64_t K, const Epilogue& ep, int splits, int* status,
+                       cudaStream_t stream) {
   // The dynamic shared-memory opt-in is made once per device (thread-safe).
   static std::atomic<uint64_t> attr_done{0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return kErrCuda;
   const uint64_t bit = 1ull << (dev & 63);
   if (!(attr_done.load() & bit)) {
-    if (cudaFuncSetAttribute(gemm_tf32x3_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(gemm_tf32x3_kernel<Cfg, kFusedA>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Cfg::SmemBytes) != cudaSuccess)
       return kErrCuda;
     attr_done.fetch_or(bit);
   }
-  const int64_t Kp = (K + 3) & ~int64_t(3);
-  CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
-  int rc = make_tmap(&ta_hi, xhi, K, M, Kp, kBM, Cfg::BK);
-  if (rc == kOk) rc = make_tmap(&ta_lo, xlo, K, M, Kp, kBM, Cfg::BK);
-  if (rc == kOk) rc = make_tmap(&tb_hi, whiT, K, N, Kp, kBN, Cfg::BK);
-  if (rc == kOk) rc = make_tmap(&tb_lo, wloT, K, N, Kp, kBN, Cfg::BK);
-  if (rc != kOk) return rc;
   const int tiles_m = (int)((M + kBM - 1) / kBM);
   const int tiles_n = (int)((N + kBN - 1) / kBN);
   const int num_kb = (int)((K + Cfg::BK - 1) / Cfg::BK);
   const int kb_per_split = (num_kb + splits - 1) / splits;
   const int nsplit = (num_kb + kb_per_split - 1) / kb_per_split;  // every split non-empty
-  gemm_tf32x3_kernel<Cfg><<<dim3(tiles_m * tiles_n, nsplit), kThreads, Cfg::SmemBytes, stream>>>(
-      ta_hi, ta_lo, tb_hi, tb_lo, num_kb, kb_per_split, tiles_m, tiles_n, ep, status);
+  gemm_tf32x3_kernel<Cfg, kFusedA>
+      <<<dim3(tiles_m * tiles_n, nsplit), kThreads, Cfg::SmemBytes, stream>>>(
+          ta_hi, ta_lo, tb_hi, tb_lo, num_kb, kb_per_split, tiles_m, tiles_n, ep, status);
   count_launch();
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+// A from pre-split xhi/xlo ([M, Kp]) or, fused, from raw X (pitch ldx).
+template <class Cfg>
+static int run_gemm(const float* xa, const float* xlo, int64_t ldx, bool fused,
+                    const float* whiT, const float* wloT, int64_t M, int64_t N, int64_t K,
+                    const Epilogue& ep, int splits, int* status, cudaStream_t stream) {
+  const int64_t Kp = (K + 3) & ~int64_t(3);
+  CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
+  int rc = make_tmap(&ta_hi, xa, K, M, fused ? ldx : Kp, kBM, Cfg::BK);
+  if (rc == kOk) rc = make_tmap(&ta_lo, fused ? xa : xlo, K, M, fused ? ldx : Kp, kBM, Cfg::BK);
+  if (rc == kOk) rc = make_tmap(&tb_hi, whiT, K, N, Kp, kBN, Cfg::BK);
+  if (rc == kOk) rc = make_tmap(&tb_lo, wloT, K, N, Kp, kBN, Cfg::BK);
+  if (rc != kOk) return rc;
+  if (fused)
+    return launch_gemm<Cfg, true>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, ep, splits, status, stream);
+  return launch_gemm<Cfg, false>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, ep, splits, status, stream);
+}
+
+static int dispatch_gemm(const float* xa, const float* xlo, int64_t ldx, bool fused,
+                         const float* whiT, const float* wloT, int64_t M, int64_t N, int64_t K,
+                         const Epilogue& ep, int splits, int* status, cudaStream_t stream) {
+  if (ring_variant() == 0)
+    return run_gemm<CfgBK32S2>(xa, xlo, ldx, fused, whiT, wloT, M, N, K, ep, splits, status,
+                               stream);
+  return run_gemm<CfgBK16S4>(xa, xlo, ldx, fused, whiT, wloT, M, N, K, ep, splits, status,
+                             stream);
 }
 
 int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
@@ -491,9 +595,7 @@ int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
   ep.alpha = alpha;
   ep.vec_out = ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(Y) & 15) == 0);
   ep.split_stride = 0;
-  if (ring_variant() == 0)
-    return launch_gemm<CfgBK32S2>(xhi, xlo, whiT, wloT, M, N, K, ep, 1, status, stream);
-  return launch_gemm<CfgBK16S4>(xhi, xlo, whiT, wloT, M, N, K, ep, 1, status, stream);
+  return dispatch_gemm(xhi, xlo, 0, false, whiT, wloT, M, N, K, ep, 1, status, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -559,20 +661,28 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ P, int splits, in
   }
 }
 
-int gemm_tf32x3_splitk(const float* xhi, const float* xlo, const float* whiT, const float* wloT,
-                       int64_t M, int64_t N, int64_t K, const float* bias, float* Y, int64_t ldy,
-                       int act, float alpha, int splits, float* partials, int* status,
-                       cudaStream_t stream) {
-  if (splits <= 1)
-    return gemm_tf32x3_presplit(xhi, xlo, whiT, wloT, M, N, K, bias, Y, ldy, act, alpha, status,
-                                stream);
-  // Partials: [splits][M][N] raw sums (no bias, no activation).
+// Shared launcher of the split-K and fused paths: GEMM (+ reduce when split).
+static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool fused,
+                            const float* whiT, const float* wloT, int64_t M, int64_t N, int64_t K,
+                            const float* bias, float* Y, int64_t ldy, int act, float alpha,
+                            int splits, float* partials, int* status, cudaStream_t stream) {
   Epilogue ep;
+  ep.M = M;
+  ep.N = N;
+  if (splits <= 1) {
+    ep.Y = Y;
+    ep.ldy = ldy;
+    ep.bias = bias;
+    ep.act = act;
+    ep.alpha = alpha;
+    ep.vec_out = ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(Y) & 15) == 0);
+    ep.split_stride = 0;
+    return dispatch_gemm(xa, xlo, ldx, fused, whiT, wloT, M, N, K, ep, 1, status, stream);
+  }
+  // Partials: [splits][M][N] raw sums (no bias, no activation).
   ep.Y = partials;
   ep.ldy = N;
   ep.bias = nullptr;
-  ep.M = M;
-  ep.N = N;
   ep.act = kActNone;
   ep.alpha = 0.0f;
   ep.vec_out = ((N & 3) == 0) && ((reinterpret_cast<uintptr_t>(partials) & 15) == 0);
@@ -582,9 +692,7 @@ int gemm_tf32x3_splitk(const float* xhi, const float* xlo, const float* whiT, co
   const int num_kb = (int)((K + bk - 1) / bk);
   const int kbps = (num_kb + splits - 1) / splits;
   const int nsplit = (num_kb + kbps - 1) / kbps;
-  int rc = ring_variant() == 0
-               ? launch_gemm<CfgBK32S2>(xhi, xlo, whiT, wloT, M, N, K, ep, splits, status, stream)
-               : launch_gemm<CfgBK16S4>(xhi, xlo, whiT, wloT, M, N, K, ep, splits, status, stream);
+  int rc = dispatch_gemm(xa, xlo, ldx, fused, whiT, wloT, M, N, K, ep, splits, status, stream);
   if (rc != kOk) return rc;
   const int vec = ((N & 3) == 0) && ((ldy & 3) == 0) &&
                   ((reinterpret_cast<uintptr_t>(Y) & 15) == 0) && ep.vec_out;
@@ -594,6 +702,27 @@ int gemm_tf32x3_splitk(const float* xhi, const float* xlo, const float* whiT, co
                                                    Y, ldy, vec);
   count_launch();
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int gemm_tf32x3_splitk(const float* xhi, const float* xlo, const float* whiT, const float* wloT,
+                       int64_t M, int64_t N, int64_t K, const float* bias, float* Y, int64_t ldy,
+                       int act, float alpha, int splits, float* partials, int* status,
+                       cudaStream_t stream) {
+  return gemm_with_splits(xhi, xlo, 0, false, whiT, wloT, M, N, K, bias, Y, ldy, act, alpha,
+                          splits, partials, status, stream);
+}
+
+bool fused_a_ok(const float* X, int64_t ldx) {
+  return ((ldx & 3) == 0) && ((reinterpret_cast<uintptr_t>(X) & 15) == 0);
+}
+
+int gemm_tf32x3_fused(const float* X, int64_t ldx, const float* whiT, const float* wloT,
+                      int64_t M, int64_t N, int64_t K, const float* bias, float* Y, int64_t ldy,
+                      int act, float alpha, int splits, float* partials, int* status,
+                      cudaStream_t stream) {
+  if (!fused_a_ok(X, ldx)) return kErrInvalidArg;
+  return gemm_with_splits(X, nullptr, ldx, true, whiT, wloT, M, N, K, bias, Y, ldy, act, alpha,
+                          splits, partials, status, stream);
 }
 
 }  // namespace b200

@@ -183,6 +183,18 @@ SplitBufs carve(void* ws, int64_t M, int64_t N, int64_t K) {
   return s;
 }
 
+// B200_FUSE_A=1 moves the A-operand split into the GEMM (X rows must be
+// 16-byte aligned). Off by default: on B200 it measured slower (201 vs 231
+// TFLOP/s on the 65536 x 4096 x 4096 dense layer) than the separate
+// HBM-bound split pass, which costs ~4% of the step.
+bool fuse_a(const float* X, int64_t ldx) {
+  static const bool enabled = [] {
+    const char* e = getenv("B200_FUSE_A");
+    return e && e[0] == '1';
+  }();
+  return enabled && fused_a_ok(X, ldx);
+}
+
 int dense_device(DeviceCtx* c, const float* X, int64_t ldx, const float* W, int64_t ldw,
                  const float* b, float* Y, int64_t ldy, int64_t M, int64_t N, int64_t K, int act,
                  float alpha, void* ws, cudaStream_t st) {
@@ -190,10 +202,16 @@ int dense_device(DeviceCtx* c, const float* X, int64_t ldx, const float* W, int6
   if (K == 0) return fill_bias_act_f32(b, Y, ldy, M, N, act, alpha, st);
   SplitBufs s = carve(ws, M, N, K);
   int rc = split_w_f32(W, ldw, K, N, s.whi, s.wlo, st);
-  if (rc == kOk) rc = split_x_f32(X, ldx, M, K, s.xhi, s.xlo, st);
-  if (rc == kOk)
-    rc = gemm_tf32x3_splitk(s.xhi, s.xlo, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha,
-                            choose_splits(M, N, K), s.partials, c->status, st);
+  if (fuse_a(X, ldx)) {
+    if (rc == kOk)
+      rc = gemm_tf32x3_fused(X, ldx, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha,
+                             choose_splits(M, N, K), s.partials, c->status, st);
+  } else {
+    if (rc == kOk) rc = split_x_f32(X, ldx, M, K, s.xhi, s.xlo, st);
+    if (rc == kOk)
+      rc = gemm_tf32x3_splitk(s.xhi, s.xlo, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha,
+                              choose_splits(M, N, K), s.partials, c->status, st);
+  }
   if (rc != kOk) return fail(rc, std::string("dense_f32 launch failed: ") +
                                      cudaGetErrorString(cudaGetLastError()));
   return kOk;
@@ -297,13 +315,19 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
     if (K == 0) {
       rc = fill_bias_act_f32(db, dY, N, rows, N, act, alpha, c->s_comp);
     } else {
-      float* xhi = static_cast<float*>(c->xhi[slot].p);
-      float* xlo = static_cast<float*>(c->xlo[slot].p);
-      rc = split_x_f32(dX, K, rows, K, xhi, xlo, c->s_comp);
-      if (rc == kOk)
-        rc = gemm_tf32x3_splitk(xhi, xlo, dWhi, dWlo, rows, N, K, db, dY, N, act, alpha,
-                                choose_splits(rows, N, K),
-                                static_cast<float*>(c->part[slot].p), c->status, c->s_comp);
+      float* part = static_cast<float*>(c->part[slot].p);
+      const int splits = choose_splits(rows, N, K);
+      if (fuse_a(dX, K)) {
+        rc = gemm_tf32x3_fused(dX, K, dWhi, dWlo, rows, N, K, db, dY, N, act, alpha, splits,
+                               part, c->status, c->s_comp);
+      } else {
+        float* xhi = static_cast<float*>(c->xhi[slot].p);
+        float* xlo = static_cast<float*>(c->xlo[slot].p);
+        rc = split_x_f32(dX, K, rows, K, xhi, xlo, c->s_comp);
+        if (rc == kOk)
+          rc = gemm_tf32x3_splitk(xhi, xlo, dWhi, dWlo, rows, N, K, db, dY, N, act, alpha,
+                                  splits, part, c->status, c->s_comp);
+      }
     }
     if (rc) return fail(rc, "dense kernel launch failed");
     B200_CUDA(cudaEventRecord(c->ev_comp[slot], c->s_comp), "record");
@@ -657,6 +681,55 @@ int b200_gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* w
   if (M == 0 || N == 0) return succeed();
   if (K == 0) rc = fill_bias_act_f32(b, Y, ldy, M, N, act, alpha, st);
   else rc = gemm_tf32x3_presplit(xhi, xlo, whiT, wloT, M, N, K, b, Y, ldy, act, alpha, c->status, st);
+  return rc ? fail(rc, "gemm launch failed") : succeed();
+}
+
+int b200_dense_f32_wsplit(const float* X, int64_t ldx, const float* whiT, const float* wloT,
+                          const float* b, float* Y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                          int act, float alpha, void* stream) {
+  int rc = validate_dense(X, ldx, whiT, N, Y, ldy, M, N, K, act);
+  if (rc) return rc;
+  if (M > 0 && N > 0 && K > 0) {
+    if (!wloT) return fail(kErrInvalidArg, "null lo operand");
+    if ((reinterpret_cast<uintptr_t>(whiT) | reinterpret_cast<uintptr_t>(wloT)) & 15)
+      return fail(kErrInvalidArg, "split operands must be 16-byte aligned");
+  }
+  DeviceCtx* c = nullptr;
+  if ((rc = current_ctx(&c))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (M == 0 || N == 0) return succeed();
+  if (K == 0) {
+    rc = fill_bias_act_f32(b, Y, ldy, M, N, act, alpha, st);
+    return rc ? fail(rc, "launch failed") : succeed();
+  }
+  const int splits = choose_splits(M, N, K);
+  const bool fused = fuse_a(X, ldx);
+  // Scratch: [X hi | X lo] (separate split pass) then the split-K partials.
+  const int64_t Kp = round_up(K, 4);
+  const int64_t xsplit = fused ? 0 : 2 * round_up(M * Kp * 4, 256);
+  void* ws = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    DevBuf& buf = c->scratch[st];
+    const size_t need = (size_t)(xsplit + splitk_partials_bytes(M, N, K)) + 256;
+    if (buf.n < need) {
+      B200_CUDA(cudaStreamSynchronize(st), "sync before scratch growth");
+      B200_CUDA(buf.reserve(need), "alloc scratch");
+    }
+    ws = buf.p;
+  }
+  float* part = reinterpret_cast<float*>(static_cast<char*>(ws) + xsplit);
+  if (fused) {
+    rc = gemm_tf32x3_fused(X, ldx, whiT, wloT, M, N, K, b, Y, ldy, act, alpha, splits, part,
+                           c->status, st);
+  } else {
+    float* xhi = static_cast<float*>(ws);
+    float* xlo = reinterpret_cast<float*>(static_cast<char*>(ws) + xsplit / 2);
+    rc = split_x_f32(X, ldx, M, K, xhi, xlo, st);
+    if (rc == kOk)
+      rc = gemm_tf32x3_splitk(xhi, xlo, whiT, wloT, M, N, K, b, Y, ldy, act, alpha, splits, part,
+                              c->status, st);
+  }
   return rc ? fail(rc, "gemm launch failed") : succeed();
 }
 

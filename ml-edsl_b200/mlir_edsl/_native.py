@@ -31,6 +31,7 @@ EXPORTED_SYMBOLS = [
     "b200_dense_f32_noalloc", "b200_dense_f32_splits", "b200_matmul_i32",
     "b200_bias_act_f32", "b200_act_f32", "b200_bias_add_i32", "b200_stream_sync",
     "b200_tf32_split_rows", "b200_tf32_split_transpose", "b200_gemm_tf32x3_presplit",
+    "b200_dense_f32_wsplit",
     "b200_malloc", "b200_free", "b200_memcpy_h2d", "b200_memcpy_d2h",
     "b200_dense_f32_host", "b200_matmul_i32_host", "b200_bias_act_f32_host",
     "b200_bias_add_i32_host", "b200_act_f32_host",
@@ -82,6 +83,8 @@ def _declare(lib):
         "b200_tf32_split_transpose": ([vp, i64, i64, i64, vp, vp, vp], i32),
         "b200_gemm_tf32x3_presplit": ([vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i32, f32, vp],
                                       i32),
+        "b200_dense_f32_wsplit": ([vp, i64, vp, vp, vp, vp, i64, i64, i64, i64, i32, f32, vp],
+                                  i32),
         "b200_malloc": ([c.POINTER(vp), i64], i32),
         "b200_free": ([vp], i32),
         "b200_memcpy_h2d": ([vp, vp, i64], i32),
@@ -143,9 +146,12 @@ def launch_count():
 
 
 def dense_launches(M, N, K):
-    """Kernel launches of one f32 dense layer: W split, X split, GEMM, and a
-    split-K reduction when the problem is split."""
-    return 3 + (1 if lib().b200_dense_f32_splits(M, N, K) > 1 else 0)
+    """Kernel launches of one f32 dense layer through b200_dense_f32: W split,
+    X split, GEMM, and a split-K reduction when the problem is split (with
+    B200_FUSE_A=1 and aligned X the X split runs inside the GEMM instead)."""
+    fused = os.environ.get("B200_FUSE_A") == "1" and K % 4 == 0
+    n = 2 if fused else 3
+    return n + (1 if lib().b200_dense_f32_splits(M, N, K) > 1 else 0)
 
 
 def device_count():

@@ -223,3 +223,66 @@ def test_split_k_matches_unsplit(cuda, M, N, K):
     assert max_err(got, unsplit) <= bound
     ref = oracle.dense_f32(X[:256], W, b, act=1)
     assert max_err(got[:256], ref) <= bound and max_err(unsplit[:256], ref) <= bound
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 512, 200), (8192, 4096, 512), (1000, 1000, 1000)])
+def test_fused_x_split_matches_split_pass(cuda, M, N, K):
+    """The GEMM that derives X's tf32 lo part itself (b200_dense_f32_wsplit, W
+    pre-split; the raw tile is read as the hi part) against the separate split
+    pass + GEMM."""
+    import torch
+    dev = torch.device("cuda:0")
+    L = _native.lib()
+    X, W, b = _inputs(M, N, K, seed=M + K)
+    Kp = (K + 3) // 4 * 4
+    tX, tW, tb = (torch.from_numpy(a).to(dev) for a in (X, W, b))
+    xhi, xlo = torch.empty((M, Kp), device=dev), torch.empty((M, Kp), device=dev)
+    whi, wlo = torch.empty((N, Kp), device=dev), torch.empty((N, Kp), device=dev)
+    Y1, Y2 = torch.empty((M, N), device=dev), torch.empty((M, N), device=dev)
+    s = stream_ptr(torch)
+    _native.check(L.b200_tf32_split_rows(ptr(tX), K, M, K, ptr(xhi), ptr(xlo), s))
+    _native.check(L.b200_tf32_split_transpose(ptr(tW), N, K, N, ptr(whi), ptr(wlo), s))
+    _native.check(L.b200_gemm_tf32x3_presplit(ptr(xhi), ptr(xlo), ptr(whi), ptr(wlo), ptr(tb),
+                                              ptr(Y1), N, M, N, K, 1, 0.0, s))
+    _native.check(L.b200_dense_f32_wsplit(ptr(tX), K, ptr(whi), ptr(wlo), ptr(tb), ptr(Y2), N,
+                                          M, N, K, 1, 0.0, s))
+    _native.check(L.b200_stream_sync(s))
+    a, f = Y1.cpu().numpy(), Y2.cpu().numpy()
+    # same products, different MMA issue order: equal up to accumulation rounding
+    assert max_err(a, f) <= oracle.f32_bound(K, X, W) / 100
+    ref = oracle.dense_f32(X[:128], W, b, act=1)
+    assert max_err(f[:128], ref) <= oracle.f32_bound(K, X, W)
+
+
+_FUSED_SCRIPT = r"""
+import sys, numpy as np, torch
+sys.path[:0] = sys.argv[1:4]
+import oracle
+from gpu_util import dense_device, max_err
+for (M, N, K) in [(512, 512, 4096), (300, 500, 1000), (1000, 999, 1001)]:
+    rng = np.random.default_rng(K)
+    X = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    W = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    b = rng.uniform(-1, 1, (N,)).astype(np.float32)
+    got = dense_device(torch, X, W, b, act=0)
+    exact = X.astype(np.float64) @ W.astype(np.float64) + b
+    assert float(np.max(np.abs(got - exact))) < 2e-4, (M, N, K)
+    ref = oracle.dense_f32(X, W, b)
+    assert max_err(got, ref) <= oracle.f32_bound(K, X, W), (M, N, K)
+print("ok")
+"""
+
+
+def test_fused_a_split_option(cuda):
+    """B200_FUSE_A=1 (in a child process: the option is read once per
+    process): the GEMM reads the raw X tile as the tf32 hi operand and derives
+    lo itself; fp32-level accuracy shows the tensor core truncates f32 to tf32."""
+    import os
+    import subprocess
+    import sys
+    from conftest import PKG_PARENT, ROOT
+    env = dict(os.environ, B200_FUSE_A="1")
+    tests_dir = os.path.dirname(os.path.abspath(__file__))
+    r = subprocess.run([sys.executable, "-c", _FUSED_SCRIPT, ROOT, PKG_PARENT, tests_dir],
+                       env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]

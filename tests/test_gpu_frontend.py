@@ -139,7 +139,11 @@ def test_stacked_dense_nets(cuda, depth):
     for i in range(depth):
         h = np.maximum(h @ args[1 + 2 * i] + args[2 + 2 * i], 0.0)
     np.testing.assert_allclose(got, h, rtol=1e-4, atol=1e-5)
-    assert get_backend().last_launches == 3 * depth  # split W, split X, GEMM per layer (no split-K at these sizes)
+    from mlir_edsl import _native
+    dims = [s[0] for s in shapes[1::2]] + [shapes[-2][1]]  # K of each layer, then last N
+    M = shapes[0][0]
+    assert get_backend().last_launches == sum(
+        _native.dense_launches(M, dims[i + 1], dims[i]) for i in range(depth))
 
 
 def test_dense_relu_dispatch_is_one_fused_gemm(cuda):
@@ -149,7 +153,9 @@ def test_dense_relu_dispatch_is_one_fused_gemm(cuda):
     rng = np.random.default_rng(2)
     X, W, b = (rng.standard_normal(s).astype(np.float32) for s in [(64, 96), (96, 80), (80,)])
     got = dense(X, W, b)
-    assert get_backend().last_launches == 3  # W split, X split, one fused GEMM+bias+relu
+    from mlir_edsl import _native
+    # W split, X split, one GEMM with fused bias + relu
+    assert get_backend().last_launches == _native.dense_launches(64, 80, 96)
     np.testing.assert_allclose(got, np.maximum(X.astype(np.float64) @ W + b, 0), rtol=1e-4,
                                atol=1e-4)
 
