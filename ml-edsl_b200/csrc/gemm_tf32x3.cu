@@ -123,6 +123,36 @@ __global__ void split_rows_kernel(const float* __restrict__ X, int64_t ldx, int6
   }
 }
 
+// Pre-pass 1b: lo part only, lo[M,Kp]. The GEMM then reads X itself as the
+// hi operand: the tensor core reads a tf32 operand from f32 bits by dropping
+// the low 13 mantissa bits, which is exactly the hi of tf32_split (for Inf
+// and NaN too), so the products are bit-identical to the full split's.
+__global__ void split_rows_lo_kernel(const float* __restrict__ X, int64_t ldx, int64_t M,
+                                     int64_t K, int64_t Kp, float* __restrict__ lo) {
+  const int64_t q_per_row = Kp >> 2;
+  const int64_t total = M * q_per_row;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / q_per_row;
+    const int64_t k = (i - m * q_per_row) << 2;
+    float v[4];
+    if (k + 4 <= K) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(X + m * ldx + k));
+      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = (k + j < K) ? __ldg(X + m * ldx + k + j) : 0.0f;
+    }
+    float h;
+    float4 l;
+    tf32_split(v[0], h, l.x);
+    tf32_split(v[1], h, l.y);
+    tf32_split(v[2], h, l.z);
+    tf32_split(v[3], h, l.w);
+    *reinterpret_cast<float4*>(lo + m * Kp + k) = l;
+  }
+}
+
 // Pre-pass 2: W[K,N] (row pitch ldw) -> hiT[N,Kp], loT[N,Kp] (K-major).
 __global__ void split_transpose_kernel(const float* __restrict__ W, int64_t ldw, int64_t K,
                                        int64_t N, int64_t Kp, float* __restrict__ hiT,
@@ -554,14 +584,15 @@ static int launch_gemm(const CUtensorMap& ta_hi, const CUtensorMap& ta_lo,
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
-// A from pre-split xhi/xlo ([M, Kp]) or, fused, from raw X (pitch ldx).
+// A operand: hi from `xa` with row pitch ldx (the pre-split xhi with pitch
+// Kp, or raw X), lo from xlo (pitch Kp); fused: lo derived in the kernel.
 template <class Cfg>
 static int run_gemm(const float* xa, const float* xlo, int64_t ldx, bool fused,
                     const float* whiT, const float* wloT, int64_t M, int64_t N, int64_t K,
                     const Epilogue& ep, int splits, int* status, cudaStream_t stream) {
   const int64_t Kp = (K + 3) & ~int64_t(3);
   CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
-  int rc = make_tmap(&ta_hi, xa, K, M, fused ? ldx : Kp, kBM, Cfg::BK);
+  int rc = make_tmap(&ta_hi, xa, K, M, ldx, kBM, Cfg::BK);
   if (rc == kOk) rc = make_tmap(&ta_lo, fused ? xa : xlo, K, M, fused ? ldx : Kp, kBM, Cfg::BK);
   if (rc == kOk) rc = make_tmap(&tb_hi, whiT, K, N, Kp, kBN, Cfg::BK);
   if (rc == kOk) rc = make_tmap(&tb_lo, wloT, K, N, Kp, kBN, Cfg::BK);
@@ -595,7 +626,8 @@ int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
   ep.alpha = alpha;
   ep.vec_out = ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(Y) & 15) == 0);
   ep.split_stride = 0;
-  return dispatch_gemm(xhi, xlo, 0, false, whiT, wloT, M, N, K, ep, 1, status, stream);
+  return dispatch_gemm(xhi, xlo, (K + 3) & ~int64_t(3), false, whiT, wloT, M, N, K, ep, 1, status,
+                       stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -708,7 +740,27 @@ int gemm_tf32x3_splitk(const float* xhi, const float* xlo, const float* whiT, co
                        int64_t M, int64_t N, int64_t K, const float* bias, float* Y, int64_t ldy,
                        int act, float alpha, int splits, float* partials, int* status,
                        cudaStream_t stream) {
-  return gemm_with_splits(xhi, xlo, 0, false, whiT, wloT, M, N, K, bias, Y, ldy, act, alpha,
+  return gemm_with_splits(xhi, xlo, (K + 3) & ~int64_t(3), false, whiT, wloT, M, N, K, bias, Y,
+                          ldy, act, alpha, splits, partials, status, stream);
+}
+
+int split_x_lo_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xlo,
+                   cudaStream_t stream) {
+  const int64_t Kp = (K + 3) & ~int64_t(3);
+  const int64_t total = M * (Kp / 4);
+  int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
+  if (blocks < 1) blocks = 1;
+  split_rows_lo_kernel<<<blocks, 256, 0, stream>>>(X, ldx, M, K, Kp, xlo);
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int gemm_tf32x3_xraw(const float* X, int64_t ldx, const float* xlo, const float* whiT,
+                     const float* wloT, int64_t M, int64_t N, int64_t K, const float* bias,
+                     float* Y, int64_t ldy, int act, float alpha, int splits, float* partials,
+                     int* status, cudaStream_t stream) {
+  if (!fused_a_ok(X, ldx)) return kErrInvalidArg;
+  return gemm_with_splits(X, xlo, ldx, false, whiT, wloT, M, N, K, bias, Y, ldy, act, alpha,
                           splits, partials, status, stream);
 }
 

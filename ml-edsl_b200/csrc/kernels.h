@@ -42,6 +42,15 @@ int gemm_tf32x3_splitk(const float* xhi, const float* xlo, const float* whiT, co
                        int64_t M, int64_t N, int64_t K, const float* bias, float* Y, int64_t ldy,
                        int act, float alpha, int splits, float* partials, int* status,
                        cudaStream_t stream);
+// Raw-X A operand (X rows 16-byte aligned: fused_a_ok): the split pass
+// writes only the lo part [M, Kp]; the GEMM reads X itself as the hi part.
+int split_x_lo_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xlo,
+                   cudaStream_t stream);
+int gemm_tf32x3_xraw(const float* X, int64_t ldx, const float* xlo, const float* whiT,
+                     const float* wloT, int64_t M, int64_t N, int64_t K, const float* bias,
+                     float* Y, int64_t ldy, int act, float alpha, int splits, float* partials,
+                     int* status, cudaStream_t stream);
+
 // Fused A split: raw X (pitch ldx, 16-byte aligned rows: fused_a_ok) is
 // split to tf32 hi/lo inside the GEMM; W pre-split as whiT/wloT.
 bool fused_a_ok(const float* X, int64_t ldx);

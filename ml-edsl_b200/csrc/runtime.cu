@@ -206,6 +206,11 @@ int dense_device(DeviceCtx* c, const float* X, int64_t ldx, const float* W, int6
     if (rc == kOk)
       rc = gemm_tf32x3_fused(X, ldx, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha,
                              choose_splits(M, N, K), s.partials, c->status, st);
+  } else if (fused_a_ok(X, ldx)) {  // X is the hi part; only lo is written
+    if (rc == kOk) rc = split_x_lo_f32(X, ldx, M, K, s.xlo, st);
+    if (rc == kOk)
+      rc = gemm_tf32x3_xraw(X, ldx, s.xlo, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha,
+                            choose_splits(M, N, K), s.partials, c->status, st);
   } else {
     if (rc == kOk) rc = split_x_f32(X, ldx, M, K, s.xhi, s.xlo, st);
     if (rc == kOk)
@@ -320,6 +325,12 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
       if (fuse_a(dX, K)) {
         rc = gemm_tf32x3_fused(dX, K, dWhi, dWlo, rows, N, K, db, dY, N, act, alpha, splits,
                                part, c->status, c->s_comp);
+      } else if (fused_a_ok(dX, K)) {
+        float* xlo = static_cast<float*>(c->xlo[slot].p);
+        rc = split_x_lo_f32(dX, K, rows, K, xlo, c->s_comp);
+        if (rc == kOk)
+          rc = gemm_tf32x3_xraw(dX, K, xlo, dWhi, dWlo, rows, N, K, db, dY, N, act, alpha, splits,
+                                part, c->status, c->s_comp);
       } else {
         float* xhi = static_cast<float*>(c->xhi[slot].p);
         float* xlo = static_cast<float*>(c->xlo[slot].p);
@@ -722,6 +733,12 @@ int b200_dense_f32_wsplit(const float* X, int64_t ldx, const float* whiT, const 
   if (fused) {
     rc = gemm_tf32x3_fused(X, ldx, whiT, wloT, M, N, K, b, Y, ldy, act, alpha, splits, part,
                            c->status, st);
+  } else if (fused_a_ok(X, ldx)) {
+    float* xlo = reinterpret_cast<float*>(static_cast<char*>(ws) + xsplit / 2);
+    rc = split_x_lo_f32(X, ldx, M, K, xlo, st);
+    if (rc == kOk)
+      rc = gemm_tf32x3_xraw(X, ldx, xlo, whiT, wloT, M, N, K, b, Y, ldy, act, alpha, splits, part,
+                            c->status, st);
   } else {
     float* xhi = static_cast<float*>(ws);
     float* xlo = reinterpret_cast<float*>(static_cast<char*>(ws) + xsplit / 2);
