@@ -182,6 +182,65 @@ __global__ void split_transpose_kernel(const float* __restrict__ W, int64_t ldw,
   }
 }
 
+// Pre-pass 3: both splits in one launch (fewer launches for small layers).
+// Blocks [0, x_blocks) split X (lo only when hi == nullptr, full otherwise);
+// the rest split-transpose W, one 32 x 32 tile per block. 256 threads.
+__global__ void __launch_bounds__(256)
+    split_xw_kernel(const float* __restrict__ X, int64_t ldx, int64_t M, int x_blocks,
+                    float* __restrict__ xhi, float* __restrict__ xlo,
+                    const float* __restrict__ W, int64_t ldw, int64_t K, int64_t N, int64_t Kp,
+                    int tiles_n, float* __restrict__ whiT, float* __restrict__ wloT) {
+  if ((int)blockIdx.x < x_blocks) {
+    const int64_t q_per_row = Kp >> 2;
+    const int64_t total = M * q_per_row;
+    const int vec_in = ((ldx & 3) == 0) && ((reinterpret_cast<uintptr_t>(X) & 15) == 0);
+    for (int64_t i = blockIdx.x * 256ll + threadIdx.x; i < total; i += (int64_t)x_blocks * 256) {
+      const int64_t m = i / q_per_row;
+      const int64_t k = (i - m * q_per_row) << 2;
+      float v[4];
+      if (vec_in && k + 4 <= K) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(X + m * ldx + k));
+        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = (k + j < K) ? __ldg(X + m * ldx + k + j) : 0.0f;
+      }
+      float4 h, l;
+      tf32_split(v[0], h.x, l.x);
+      tf32_split(v[1], h.y, l.y);
+      tf32_split(v[2], h.z, l.z);
+      tf32_split(v[3], h.w, l.w);
+      if (xhi) *reinterpret_cast<float4*>(xhi + m * Kp + k) = h;
+      *reinterpret_cast<float4*>(xlo + m * Kp + k) = l;
+    }
+    return;
+  }
+  __shared__ float th[32][33];
+  __shared__ float tl[32][33];
+  const int t = blockIdx.x - x_blocks;
+  const int64_t n0 = (int64_t)(t % tiles_n) * 32;
+  const int64_t k0 = (int64_t)(t / tiles_n) * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int64_t k = k0 + ty + 8 * j, n = n0 + tx;
+    const float x = (k < K && n < N) ? __ldg(W + k * ldw + n) : 0.0f;
+    float h, l;
+    tf32_split(x, h, l);
+    th[ty + 8 * j][tx] = h;
+    tl[ty + 8 * j][tx] = l;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int64_t n = n0 + ty + 8 * j, k = k0 + tx;
+    if (n < N && k < Kp) {
+      whiT[n * Kp + k] = th[tx][ty + 8 * j];
+      wloT[n * Kp + k] = tl[tx][ty + 8 * j];
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float apply_act(float x, int act, float alpha) {
   if (act == kActRelu) {
@@ -518,9 +577,13 @@ int64_t dense_f32_workspace_bytes(int64_t M, int64_t N, int64_t K) {
   return 2 * al(M * Kp * 4) + 2 * al(N * Kp * 4);
 }
 
+// Split-K partials are stored with a row pitch padded to 4 floats, so the
+// GEMM epilogue always writes them with 16-byte vector stores.
+static int64_t partials_pitch(int64_t N) { return (N + 3) & ~int64_t(3); }
+
 int64_t splitk_partials_bytes(int64_t M, int64_t N, int64_t K) {
   const int s = choose_splits(M, N, K);
-  return s > 1 ? ((int64_t)s * M * N * 4 + 255) & ~int64_t(255) : 0;
+  return s > 1 ? ((int64_t)s * M * partials_pitch(N) * 4 + 255) & ~int64_t(255) : 0;
 }
 
 int split_w_f32(const float* W, int64_t ldw, int64_t K, int64_t N, float* whiT, float* wloT,
@@ -658,17 +721,17 @@ int choose_splits(int64_t M, int64_t N, int64_t K) {
 }
 
 __global__ void splitk_reduce_kernel(const float* __restrict__ P, int splits, int64_t stride,
-                                     int64_t M, int64_t N, const float* __restrict__ bias,
-                                     int act, float alpha, float* __restrict__ Y, int64_t ldy,
-                                     int vec) {
+                                     int64_t ldp, int64_t M, int64_t N,
+                                     const float* __restrict__ bias, int act, float alpha,
+                                     float* __restrict__ Y, int64_t ldy, int vec) {
   if (vec) {  // N % 4 == 0, Y 16-byte aligned, ldy % 4 == 0
     const int64_t q = N >> 2, total = M * q;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
       const int64_t m = i / q, n = (i - m * q) << 2;
-      float4 a = __ldg(reinterpret_cast<const float4*>(P + m * N + n));
+      float4 a = __ldg(reinterpret_cast<const float4*>(P + m * ldp + n));
       for (int s = 1; s < splits; ++s) {  // fixed order: deterministic
-        const float4 t = __ldg(reinterpret_cast<const float4*>(P + s * stride + m * N + n));
+        const float4 t = __ldg(reinterpret_cast<const float4*>(P + s * stride + m * ldp + n));
         a.x += t.x; a.y += t.y; a.z += t.z; a.w += t.w;
       }
       if (bias) {
@@ -685,8 +748,8 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ P, int splits, in
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
       const int64_t m = i / N, n = i - m * N;
-      float a = P[i];
-      for (int s = 1; s < splits; ++s) a += P[s * stride + i];
+      float a = P[m * ldp + n];
+      for (int s = 1; s < splits; ++s) a += P[s * stride + m * ldp + n];
       if (bias) a += bias[n];
       Y[m * ldy + n] = apply_act(a, act, alpha);
     }
@@ -711,14 +774,15 @@ static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool
     ep.split_stride = 0;
     return dispatch_gemm(xa, xlo, ldx, fused, whiT, wloT, M, N, K, ep, 1, status, stream);
   }
-  // Partials: [splits][M][N] raw sums (no bias, no activation).
+  // Partials: [splits][M][ldp] raw sums (no bias, no activation).
+  const int64_t ldp = partials_pitch(N);
   ep.Y = partials;
-  ep.ldy = N;
+  ep.ldy = ldp;
   ep.bias = nullptr;
   ep.act = kActNone;
   ep.alpha = 0.0f;
-  ep.vec_out = ((N & 3) == 0) && ((reinterpret_cast<uintptr_t>(partials) & 15) == 0);
-  ep.split_stride = M * N;
+  ep.vec_out = (reinterpret_cast<uintptr_t>(partials) & 15) == 0;
+  ep.split_stride = M * ldp;
   // The launcher may use fewer splits so that none is empty; recompute it.
   const int bk = ring_variant() == 0 ? CfgBK32S2::BK : CfgBK16S4::BK;
   const int num_kb = (int)((K + bk - 1) / bk);
@@ -730,8 +794,8 @@ static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool
                   ((reinterpret_cast<uintptr_t>(Y) & 15) == 0) && ep.vec_out;
   const int64_t work = vec ? M * N / 4 : M * N;
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, 148 * 16));
-  splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(partials, nsplit, M * N, M, N, bias, act, alpha,
-                                                   Y, ldy, vec);
+  splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(partials, nsplit, M * ldp, ldp, M, N, bias,
+                                                   act, alpha, Y, ldy, vec);
   count_launch();
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
@@ -742,6 +806,20 @@ int gemm_tf32x3_splitk(const float* xhi, const float* xlo, const float* whiT, co
                        cudaStream_t stream) {
   return gemm_with_splits(xhi, xlo, (K + 3) & ~int64_t(3), false, whiT, wloT, M, N, K, bias, Y,
                           ldy, act, alpha, splits, partials, status, stream);
+}
+
+int split_xw_f32(const float* X, int64_t ldx, int64_t M, const float* W, int64_t ldw,
+                 int64_t K, int64_t N, float* xhi, float* xlo, float* whiT, float* wloT,
+                 cudaStream_t stream) {
+  const int64_t Kp = (K + 3) & ~int64_t(3);
+  const int64_t xq = M * (Kp / 4);
+  const int x_blocks = (int)std::max<int64_t>(1, std::min<int64_t>((xq + 255) / 256, 148 * 16));
+  const int tiles_n = (int)((N + 31) / 32);
+  const int64_t w_blocks = (int64_t)tiles_n * ((Kp + 31) / 32);
+  split_xw_kernel<<<(unsigned)(x_blocks + w_blocks), 256, 0, stream>>>(
+      X, ldx, M, x_blocks, xhi, xlo, W, ldw, K, N, Kp, tiles_n, whiT, wloT);
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
 int split_x_lo_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xlo,

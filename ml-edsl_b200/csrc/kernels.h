@@ -42,6 +42,12 @@ int gemm_tf32x3_splitk(const float* xhi, const float* xlo, const float* whiT, co
                        int64_t M, int64_t N, int64_t K, const float* bias, float* Y, int64_t ldy,
                        int act, float alpha, int splits, float* partials, int* status,
                        cudaStream_t stream);
+// Both splits in one launch: X -> (xhi,) xlo (xhi == nullptr: lo only) and
+// W -> whiT, wloT.
+int split_xw_f32(const float* X, int64_t ldx, int64_t M, const float* W, int64_t ldw,
+                 int64_t K, int64_t N, float* xhi, float* xlo, float* whiT, float* wloT,
+                 cudaStream_t stream);
+
 // Raw-X A operand (X rows 16-byte aligned: fused_a_ok): the split pass
 // writes only the lo part [M, Kp]; the GEMM reads X itself as the hi part.
 int split_x_lo_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xlo,

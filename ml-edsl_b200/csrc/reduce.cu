@@ -10,7 +10,7 @@
 //     (mlir_edsl/ops/linalg.py:104-175) and a product body (acc * elem).
 //
 // Two passes, deterministic: pass 1 has each of up to kMaxBlocks blocks fold a
-// contiguous range of the input (coalesced loads) into one
+// contiguous range of the input (16-byte loads, 4 in flight) into one
 // partial; pass 2 (one block) folds the partials in block order and finally
 // combines the init as the first operand, as the sequential fold does. The
 // max/min combine keeps the left (earlier) operand unless the right one is
@@ -19,6 +19,7 @@
 #include <cuda_runtime.h>
 #include <algorithm>
 #include <cstdint>
+#include <cstring>
 #include "kernels.h"
 
 namespace b200 {
@@ -89,17 +90,70 @@ __device__ __forceinline__ T block_fold(int op, T v) {
   return v;
 }
 
-// Pass 1. Block b folds elements [b*chunk, min(n, (b+1)*chunk)); inside the
-// block, thread t folds its strided elements in index order. With `y`
-// non-null the element is x[i]*y[i] (dot product, op = sum).
+// Pass 1. Block b folds elements [b*chunk, min(n, (b+1)*chunk)). Inside the
+// block, each thread folds its elements in index order: with 16-byte aligned
+// inputs and chunk a multiple of 4, thread t takes 4-element groups t,
+// t+256, ... (four 16-byte loads in flight per iteration), then the ragged
+// tail element-wise. With `y` non-null the element is x[i]*y[i] (dot, sum).
+template <class T>
+__device__ __forceinline__ T fold4(int op, T acc, const T (&v)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) acc = Ops<T>::combine(op, acc, v[j]);
+  return acc;
+}
+
 template <class T>
 __global__ void __launch_bounds__(kRedThreads)
     reduce_pass1(const T* __restrict__ x, const T* __restrict__ y, int64_t n, int64_t chunk,
-                 int op, T* __restrict__ partials) {
+                 int op, int vec, T* __restrict__ partials) {
   const int64_t lo = (int64_t)blockIdx.x * chunk;
   const int64_t hi = min(n, lo + chunk);
   T acc = Ops<T>::identity(op);
-  for (int64_t i = lo + threadIdx.x; i < hi; i += kRedThreads) {
+  int64_t tail = lo;
+  if (vec) {
+    using V = int4;  // 16 bytes of T
+    const int64_t ng = (hi - lo) >> 2;  // whole groups of 4
+    const V* xv = reinterpret_cast<const V*>(x + lo);
+    const V* yv = y ? reinterpret_cast<const V*>(y + lo) : nullptr;
+    int64_t g = threadIdx.x;
+    for (; g + 3 * kRedThreads < ng; g += 4 * kRedThreads) {
+      V a[4], b[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) a[u] = __ldg(xv + g + u * kRedThreads);
+      if (yv) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) b[u] = __ldg(yv + g + u * kRedThreads);
+      }
+      // fold groups g, g+256, g+512, g+768: this thread's groups in index order
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        T v[4];
+        memcpy(v, &a[u], 16);
+        if (yv) {
+          T w[4];
+          memcpy(w, &b[u], 16);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) v[j] = Ops<T>::mul(v[j], w[j]);
+        }
+        acc = fold4<T>(op, acc, v);
+      }
+    }
+    for (; g < ng; g += kRedThreads) {
+      T v[4];
+      const V a = __ldg(xv + g);
+      memcpy(v, &a, 16);
+      if (yv) {
+        T w[4];
+        const V b = __ldg(yv + g);
+        memcpy(w, &b, 16);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = Ops<T>::mul(v[j], w[j]);
+      }
+      acc = fold4<T>(op, acc, v);
+    }
+    tail = lo + (ng << 2);
+  }
+  for (int64_t i = tail + threadIdx.x; i < hi; i += kRedThreads) {
     T v = __ldg(x + i);
     if (y) v = Ops<T>::mul(v, __ldg(y + i));  // rounded product, then the add
     acc = Ops<T>::combine(op, acc, v);
@@ -127,10 +181,12 @@ template <class T>
 static int reduce_impl(const T* x, const T* y, int64_t n, int op, T init, T* out, void* scratch,
                        cudaStream_t st) {
   int64_t blocks = std::min<int64_t>(kMaxBlocks, std::max<int64_t>(1, (n + 4095) / 4096));
-  const int64_t chunk = std::max<int64_t>(1, (n + blocks - 1) / blocks);
+  int64_t chunk = std::max<int64_t>(1, (n + blocks - 1) / blocks);
+  const int vec = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+  if (vec) chunk = (chunk + 3) & ~int64_t(3);  // groups of 4 never straddle blocks
   blocks = std::max<int64_t>(1, (n + chunk - 1) / chunk);
   T* partials = static_cast<T*>(scratch);
-  reduce_pass1<T><<<(unsigned)blocks, kRedThreads, 0, st>>>(x, y, n, chunk, op, partials);
+  reduce_pass1<T><<<(unsigned)blocks, kRedThreads, 0, st>>>(x, y, n, chunk, op, vec, partials);
   count_launch();
   reduce_pass2<T><<<1, kRedThreads, 0, st>>>(partials, (int)blocks, op, init, out);
   count_launch();

@@ -201,21 +201,23 @@ int dense_device(DeviceCtx* c, const float* X, int64_t ldx, const float* W, int6
   if (M == 0 || N == 0) return kOk;
   if (K == 0) return fill_bias_act_f32(b, Y, ldy, M, N, act, alpha, st);
   SplitBufs s = carve(ws, M, N, K);
-  int rc = split_w_f32(W, ldw, K, N, s.whi, s.wlo, st);
+  const int splits = choose_splits(M, N, K);
+  int rc;
   if (fuse_a(X, ldx)) {
+    rc = split_w_f32(W, ldw, K, N, s.whi, s.wlo, st);
     if (rc == kOk)
-      rc = gemm_tf32x3_fused(X, ldx, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha,
-                             choose_splits(M, N, K), s.partials, c->status, st);
+      rc = gemm_tf32x3_fused(X, ldx, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha, splits,
+                             s.partials, c->status, st);
   } else if (fused_a_ok(X, ldx)) {  // X is the hi part; only lo is written
-    if (rc == kOk) rc = split_x_lo_f32(X, ldx, M, K, s.xlo, st);
+    rc = split_xw_f32(X, ldx, M, W, ldw, K, N, nullptr, s.xlo, s.whi, s.wlo, st);
     if (rc == kOk)
-      rc = gemm_tf32x3_xraw(X, ldx, s.xlo, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha,
-                            choose_splits(M, N, K), s.partials, c->status, st);
+      rc = gemm_tf32x3_xraw(X, ldx, s.xlo, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha, splits,
+                            s.partials, c->status, st);
   } else {
-    if (rc == kOk) rc = split_x_f32(X, ldx, M, K, s.xhi, s.xlo, st);
+    rc = split_xw_f32(X, ldx, M, W, ldw, K, N, s.xhi, s.xlo, s.whi, s.wlo, st);
     if (rc == kOk)
-      rc = gemm_tf32x3_splitk(s.xhi, s.xlo, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha,
-                              choose_splits(M, N, K), s.partials, c->status, st);
+      rc = gemm_tf32x3_splitk(s.xhi, s.xlo, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha, splits,
+                              s.partials, c->status, st);
   }
   if (rc != kOk) return fail(rc, std::string("dense_f32 launch failed: ") +
                                      cudaGetErrorString(cudaGetLastError()));
@@ -297,8 +299,11 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
     B200_CUDA(cudaMemcpy2DAsync(dW, N * 4, W, ldw * 4, N * 4, K, cudaMemcpyHostToDevice,
                                 c->s_comp),
               "H2D W");
-    rc = split_w_f32(dW, N, K, N, dWhi, dWlo, c->s_comp);
-    if (rc) return fail(rc, "split W launch failed");
+    // A single-slab call splits W together with X (one launch) below.
+    if (nslab > 1 || fuse_a(static_cast<float*>(c->x[0].p), K)) {
+      rc = split_w_f32(dW, N, K, N, dWhi, dWlo, c->s_comp);
+      if (rc) return fail(rc, "split W launch failed");
+    }
   }
 
   for (int64_t i = 0; i < nslab; ++i) {
@@ -327,14 +332,16 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
                                part, c->status, c->s_comp);
       } else if (fused_a_ok(dX, K)) {
         float* xlo = static_cast<float*>(c->xlo[slot].p);
-        rc = split_x_lo_f32(dX, K, rows, K, xlo, c->s_comp);
+        rc = nslab == 1 ? split_xw_f32(dX, K, rows, dW, N, K, N, nullptr, xlo, dWhi, dWlo, c->s_comp)
+                        : split_x_lo_f32(dX, K, rows, K, xlo, c->s_comp);
         if (rc == kOk)
           rc = gemm_tf32x3_xraw(dX, K, xlo, dWhi, dWlo, rows, N, K, db, dY, N, act, alpha, splits,
                                 part, c->status, c->s_comp);
       } else {
         float* xhi = static_cast<float*>(c->xhi[slot].p);
         float* xlo = static_cast<float*>(c->xlo[slot].p);
-        rc = split_x_f32(dX, K, rows, K, xhi, xlo, c->s_comp);
+        rc = nslab == 1 ? split_xw_f32(dX, K, rows, dW, N, K, N, xhi, xlo, dWhi, dWlo, c->s_comp)
+                        : split_x_f32(dX, K, rows, K, xhi, xlo, c->s_comp);
         if (rc == kOk)
           rc = gemm_tf32x3_splitk(xhi, xlo, dWhi, dWlo, rows, N, K, db, dY, N, act, alpha,
                                   splits, part, c->status, c->s_comp);

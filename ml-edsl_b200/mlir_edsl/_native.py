@@ -146,12 +146,10 @@ def launch_count():
 
 
 def dense_launches(M, N, K):
-    """Kernel launches of one f32 dense layer through b200_dense_f32: W split,
-    X split, GEMM, and a split-K reduction when the problem is split (with
-    B200_FUSE_A=1 and aligned X the X split runs inside the GEMM instead)."""
-    fused = os.environ.get("B200_FUSE_A") == "1" and K % 4 == 0
-    n = 2 if fused else 3
-    return n + (1 if lib().b200_dense_f32_splits(M, N, K) > 1 else 0)
+    """Kernel launches of one f32 dense layer through b200_dense_f32: one
+    split pass (X and W together), the GEMM, and a split-K reduction when the
+    problem is split."""
+    return 2 + (1 if lib().b200_dense_f32_splits(M, N, K) > 1 else 0)
 
 
 def device_count():
