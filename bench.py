@@ -509,7 +509,19 @@ def run_configs(args):
     C = torch.empty_like(A)
     ms = timed(lambda: _native.check(L.b200_matmul_i32(P(A), 2048, P(B), 2048, None, P(C), 2048,
                                                       2048, 2048, 2048, sp)))
-    emit_line({"config": "matmul_i32_2048", "ms": ms, "Tint-op/s": 2.0 * 2048 ** 3 / ms / 1e9})
+    line = {"config": "matmul_i32_2048", "ms": ms, "Tint-op/s": 2.0 * 2048 ** 3 / ms / 1e9}
+    # roofline: measured INT32 multiply-add issue rate (lib/libb200probe.so)
+    probe = ctypes.CDLL(os.path.join(ROOT, "ml-edsl_b200", "lib", "libb200probe.so"))
+    probe.b200_probe_imad.restype = ctypes.c_float
+    probe.b200_probe_imad.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    pb, pit = 148 * 8, 2000
+    pout = torch.empty(pb * 256, dtype=torch.int32, device=dev)
+    pms = probe.b200_probe_imad(pb, pit, P(pout))
+    if pms > 0:
+        peak_ops = 2.0 * pb * 256 * pit * 128 / pms / 1e9  # multiply + add per IMAD
+        line.update({"imad_peak_Tint-op/s": peak_ops,
+                     "frac_of_imad_peak": line["Tint-op/s"] / peak_ops})
+    emit_line(line)
     # unfused elementwise bias+relu over the cfg4 output shape (HBM-bound)
     Xe, be = u((65536, 4096), 9), u((4096,), 10)
     Ye = torch.empty_like(Xe)

@@ -18,7 +18,7 @@ namespace b200 {
 
 constexpr int kIBM = 128, kIBN = 128, kIBK = 16;
 
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 2)  // two CTAs per SM (<= 128 registers)
     gemm_i32_kernel(const int32_t* __restrict__ A, int64_t lda, const int32_t* __restrict__ B,
                     int64_t ldb, int32_t* __restrict__ C, int64_t ldc, int64_t M, int64_t N,
                     int64_t K, const int32_t* __restrict__ bias) {
@@ -36,25 +36,44 @@ __global__ void __launch_bounds__(256)
   const int b_k = tid >> 4, b_col = (tid & 15) * 8;
   uint32_t ra[8], rb[8];
 
+  // 16-byte global loads when the rows are 16-byte aligned and in range.
+  const bool vec_a = ((lda & 3) == 0) && ((reinterpret_cast<uintptr_t>(A) & 15) == 0);
+  const bool vec_b = ((ldb & 3) == 0) && ((reinterpret_cast<uintptr_t>(B) & 15) == 0);
   auto load_tiles = [&](int64_t k0) {
     const int64_t gm = m0 + a_row;
+    const int64_t ga = k0 + a_k;
+    if (vec_a && gm < M && ga + 8 <= K) {
+      const uint4 u0 = __ldg(reinterpret_cast<const uint4*>(A + gm * lda + ga));
+      const uint4 u1 = __ldg(reinterpret_cast<const uint4*>(A + gm * lda + ga + 4));
+      ra[0] = u0.x; ra[1] = u0.y; ra[2] = u0.z; ra[3] = u0.w;
+      ra[4] = u1.x; ra[5] = u1.y; ra[6] = u1.z; ra[7] = u1.w;
+    } else {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int64_t gk = k0 + a_k + j;
-      ra[j] = (gm < M && gk < K) ? (uint32_t)__ldg(A + gm * lda + gk) : 0u;
+      for (int j = 0; j < 8; ++j) {
+        const int64_t gk = ga + j;
+        ra[j] = (gm < M && gk < K) ? (uint32_t)__ldg(A + gm * lda + gk) : 0u;
+      }
     }
     const int64_t gk = k0 + b_k;
+    const int64_t gn0 = n0 + b_col;
+    if (vec_b && gk < K && gn0 + 8 <= N) {
+      const uint4 u0 = __ldg(reinterpret_cast<const uint4*>(B + gk * ldb + gn0));
+      const uint4 u1 = __ldg(reinterpret_cast<const uint4*>(B + gk * ldb + gn0 + 4));
+      rb[0] = u0.x; rb[1] = u0.y; rb[2] = u0.z; rb[3] = u0.w;
+      rb[4] = u1.x; rb[5] = u1.y; rb[6] = u1.z; rb[7] = u1.w;
+    } else {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int64_t gn = n0 + b_col + j;
-      rb[j] = (gk < K && gn < N) ? (uint32_t)__ldg(B + gk * ldb + gn) : 0u;
+      for (int j = 0; j < 8; ++j) {
+        const int64_t gn = gn0 + j;
+        rb[j] = (gk < K && gn < N) ? (uint32_t)__ldg(B + gk * ldb + gn) : 0u;
+      }
     }
   };
   auto store_tiles = [&](int buf) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) As[buf][a_k + j][a_row] = ra[j];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) Bs[buf][b_k][b_col + j] = rb[j];
+    *reinterpret_cast<uint4*>(&Bs[buf][b_k][b_col]) = make_uint4(rb[0], rb[1], rb[2], rb[3]);
+    *reinterpret_cast<uint4*>(&Bs[buf][b_k][b_col + 4]) = make_uint4(rb[4], rb[5], rb[6], rb[7]);
   };
 
   uint32_t acc[8][8];
