@@ -192,6 +192,21 @@ int b200_reduce_i32(const int32_t* x, int64_t n, int op, int32_t init, int32_t* 
 int b200_dot_f32(const float* a, const float* b, int64_t n, float* out, void* stream);
 int b200_dot_i32(const int32_t* a, const int32_t* b, int64_t n, int32_t* out, void* stream);
 
+/* Failure detection without a GPU fault. Every wait inside this library's
+ * kernels is bounded; one that runs out records a code in the device status
+ * word and the kernel returns, so the context stays usable and the next
+ * b200_stream_sync() reports B200_ERR_DEVICE_TIMEOUT (the reference has no
+ * device-side detection; its checkCU turns CUDA errors into exceptions,
+ * reference: cpp/src/MLIRExecutor.cpp:160-167).
+ * b200_selftest_wait_timeout launches one kernel whose wait can never be
+ * satisfied, with a limit of limit_ns, to exercise that path.
+ * b200_debug_fail_alloc(n): the n-th next device allocation of the runtime
+ * fails with B200_ERR_OUT_OF_MEMORY (0 disables), host-side fault injection
+ * (the reference's analogue is inject_test_failure,
+ * reference: cpp/src/MLIRCompiler.cpp:331-348). */
+int b200_selftest_wait_timeout(int64_t limit_ns, void* stream);
+int b200_debug_fail_alloc(int n);
+
 /* --------------------------------------------------- host-pointer entry points */
 
 /* Host buffers; synchronous. Rows of X/Y are sharded over `ndev` devices

@@ -531,6 +531,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Failure-detection self-test: one thread waits, with the GEMM's bounded
+// wait, on an mbarrier that nothing ever arrives on. After `limit_ns` the
+// wait gives up and records kDevTimeoutSelfTest in the status word, exactly
+// as a stalled GEMM role would; the kernel then returns normally.
+__global__ void wait_timeout_selftest_kernel(uint64_t limit_ns, int* status) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0)
+    mbar_wait_for(&bar, 0, status, kDevTimeoutSelfTest, &abort_flag, limit_ns);
+}
+
+int wait_timeout_selftest(uint64_t limit_ns, int* status, cudaStream_t stream) {
+  wait_timeout_selftest_kernel<<<1, 32, 0, stream>>>(limit_ns, status);
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------

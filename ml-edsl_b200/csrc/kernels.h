@@ -69,6 +69,9 @@ int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
                          float* Y, int64_t ldy, int act, float alpha, int* status,
                          cudaStream_t stream);
 
+// Failure-detection self-test (a bounded wait that always runs out).
+int wait_timeout_selftest(uint64_t limit_ns, int* status, cudaStream_t stream);
+
 // ---- i32 GEMM (gemm_i32.cu): C = A*B mod 2^32
 int gemm_i32(const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb, int32_t* C,
              int64_t ldc, int64_t M, int64_t N, int64_t K, const int32_t* bias,

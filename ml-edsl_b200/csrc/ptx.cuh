@@ -20,6 +20,7 @@ enum DeviceStatus : int {
   kDevTimeoutFull = 1,     // consumer waited too long for a TMA stage
   kDevTimeoutEmpty = 2,    // producer waited too long for a free stage
   kDevTimeoutAccum = 3,    // epilogue waited too long for the accumulator
+  kDevTimeoutSelfTest = 4, // the self-test wait (nothing ever arrives) ran out
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -66,19 +67,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait on `bar` reaching phase `parity`. Returns false on timeout
 // (after recording `code` in *status); also returns false early when another
 // role of the CTA has already recorded a failure (*abort_flag != 0).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code,
-                                          volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* status,
+                                              int code, volatile int* abort_flag,
+                                              uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > B200_WAIT_NS) {
+    if (globaltimer() - t0 > limit_ns) {
       if (status) atomicCAS(status, 0, code);
       *abort_flag = 1;
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code,
+                                          volatile int* abort_flag) {
+  return mbar_wait_for(bar, parity, status, code, abort_flag, B200_WAIT_NS);
 }
 
 // ---------------------------------------------------------------- TMA

@@ -54,6 +54,10 @@ int succeed() {
     if (e_ != cudaSuccess) return fail_cuda(e_, what); \
   } while (0)
 
+// Host-side fault injection: when > 0, the n-th next device allocation made
+// by the runtime fails with cudaErrorMemoryAllocation (b200_debug_fail_alloc).
+std::atomic<int> g_fail_alloc_in{0};
+
 struct DevBuf {
   void* p = nullptr;
   size_t n = 0;
@@ -63,6 +67,8 @@ struct DevBuf {
     if (p) cudaFree(p);
     p = nullptr;
     n = 0;
+    const int k = g_fail_alloc_in.load();
+    if (k > 0 && g_fail_alloc_in.fetch_sub(1) == 1) return cudaErrorMemoryAllocation;
     cudaError_t e = cudaMalloc(&p, need);
     if (e == cudaSuccess) n = need;
     return e;
@@ -826,6 +832,22 @@ int b200_dot_i32_host(const int32_t* a, const int32_t* b, int64_t n, int32_t* re
   if (n < 0 || !result || (n > 0 && (!a || !b))) return fail(kErrInvalidArg, "bad dot arguments");
   int rc = reduce_host_impl<int32_t>(a, b, n, kRedSum, 0, result);
   return rc ? rc : succeed();
+}
+
+// ---------------------------------------------------------------- failure detection
+int b200_selftest_wait_timeout(int64_t limit_ns, void* stream) {
+  if (limit_ns <= 0) return fail(kErrInvalidArg, "limit_ns must be positive");
+  DeviceCtx* c = nullptr;
+  int rc = current_ctx(&c);
+  if (rc) return rc;
+  rc = wait_timeout_selftest((uint64_t)limit_ns, c->status, static_cast<cudaStream_t>(stream));
+  return rc ? fail(rc, "self-test launch failed") : succeed();
+}
+
+int b200_debug_fail_alloc(int n) {
+  if (n < 0) return fail(kErrInvalidArg, "n must be >= 0");
+  g_fail_alloc_in.store(n);
+  return succeed();
 }
 
 // ---------------------------------------------------------------- host API

@@ -1,0 +1,54 @@
+"""Failure detection on the GPU without a GPU fault: a bounded device wait
+that runs out is reported as B200_ERR_DEVICE_TIMEOUT and leaves the context
+usable; an injected allocation failure surfaces as B200_ERR_OUT_OF_MEMORY and
+the next call succeeds."""
+import ctypes
+import time
+
+import numpy as np
+import pytest
+
+import oracle
+from gpu_util import dense_device, max_err, stream_ptr
+from mlir_edsl import _native
+
+pytestmark = pytest.mark.gpu
+
+
+def test_device_wait_timeout_is_reported_and_context_survives(cuda):
+    import torch
+    L = _native.lib()
+    s = stream_ptr(torch)
+    t0 = time.perf_counter()
+    _native.check(L.b200_selftest_wait_timeout(50_000_000, s))  # 50 ms, nothing arrives
+    rc = L.b200_stream_sync(s)
+    elapsed = time.perf_counter() - t0
+    assert rc == 5, rc  # B200_ERR_DEVICE_TIMEOUT
+    assert b"bounded wait (code 4)" in L.b200_last_error()
+    assert 0.04 < elapsed < 5.0
+    # the status was read and cleared; the context still computes correctly
+    assert L.b200_stream_sync(s) == 0
+    rng = np.random.default_rng(0)
+    X = rng.uniform(-1, 1, (256, 300)).astype(np.float32)
+    W = rng.uniform(-1, 1, (300, 200)).astype(np.float32)
+    b = rng.uniform(-1, 1, (200,)).astype(np.float32)
+    got = dense_device(torch, X, W, b, act=1)
+    assert max_err(got, oracle.dense_f32(X, W, b, act=1)) <= oracle.f32_bound(300, X, W)
+
+
+def test_injected_allocation_failure(cuda):
+    L = _native.lib()
+    _native.check(L.b200_release())  # the next host call must allocate again
+    rng = np.random.default_rng(1)
+    X = rng.uniform(-1, 1, (64, 48)).astype(np.float32)
+    W = rng.uniform(-1, 1, (48, 40)).astype(np.float32)
+    Y = np.zeros((64, 40), np.float32)
+    c = ctypes.c_void_p
+    _native.check(L.b200_debug_fail_alloc(1))
+    rc = L.b200_dense_f32_host(c(X.ctypes.data), 48, c(W.ctypes.data), 40, None,
+                               c(Y.ctypes.data), 40, 64, 40, 48, 0, 0.0, 1)
+    assert rc == 6 and b"alloc" in L.b200_last_error()
+    rc = L.b200_dense_f32_host(c(X.ctypes.data), 48, c(W.ctypes.data), 40, None,
+                               c(Y.ctypes.data), 40, 64, 40, 48, 0, 0.0, 1)
+    assert rc == 0
+    assert max_err(Y, oracle.dense_f32(X, W)) <= oracle.f32_bound(48, X, W)
