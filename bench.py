@@ -364,7 +364,30 @@ def run_b200(args):
         bound = 1e-4 * K ** 0.5 * float(X.abs().max()) * float(W.abs().max())
         e2e_err = float((Yh - Y.cpu()).abs().max())
         assert e2e_err <= bound, f"e2e result differs from device path: {e2e_err} > {bound}"
+        # e2e roofline: the same bytes copied alone (H2D and D2H concurrently
+        # on two streams, pinned buffers), i.e. the PCIe floor of one step
+        dX, dW, db, dY = torch.empty_like(X), torch.empty_like(W), torch.empty_like(b), \
+            torch.empty_like(Y)
+        s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+
+        def copies():
+            with torch.cuda.stream(s_in):
+                dX.copy_(Xh, non_blocking=True)
+                dW.copy_(Wh, non_blocking=True)
+                db.copy_(bh, non_blocking=True)
+            with torch.cuda.stream(s_out):
+                Yh.copy_(dY, non_blocking=True)
+        copies()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(3):
+            copies()
+        torch.cuda.synchronize()
+        copy_floor_ms = (time.perf_counter() - t0) / 3 * 1e3
+        del dX, dW, db, dY
         e2e = {"value": flops_job * args.steps / t_e2e / 1e12, "unit": UNIT,
+               "copy_floor_ms": copy_floor_ms,
+               "frac_of_copy_floor": copy_floor_ms / (t_e2e / args.steps * 1e3),
                "h2d_bytes_per_step": (M * K + K * N + N) * 4, "d2h_bytes_per_step": M * N * 4,
                "ms_per_step": t_e2e / args.steps * 1e3,
                "api": "b200_memref_dense_relu_f32 (reference flattened-memref ABI), pinned host "

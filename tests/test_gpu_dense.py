@@ -289,3 +289,23 @@ def test_fused_a_split_option(cuda):
     r = subprocess.run([sys.executable, "-c", _FUSED_SCRIPT, ROOT, PKG_PARENT, tests_dir],
                        env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
+
+
+def test_host_api_sharded_over_two_devices(cuda):
+    """One process, rows sharded over 2 GPUs (one host thread each, W and b
+    replicated): same result as on one GPU. Skipped with fewer devices."""
+    L = _native.lib()
+    if L.b200_device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    M, N, K = 5001, 384, 1024
+    X, W, b = _inputs(M, N, K, seed=77)
+    c = ctypes.c_void_p
+    Y1 = np.full((M, N), np.nan, np.float32)
+    Y2 = np.full((M, N), np.nan, np.float32)
+    for Y, ndev in ((Y1, 1), (Y2, 2)):
+        _native.check(L.b200_dense_f32_host(c(X.ctypes.data), K, c(W.ctypes.data), N,
+                                            c(b.ctypes.data), c(Y.ctypes.data), N, M, N, K, 1,
+                                            0.0, ndev))
+    bound = oracle.f32_bound(K, X, W)
+    assert max_err(Y1, Y2) <= bound
+    assert max_err(Y2[-300:], oracle.dense_f32(X[-300:], W, b, act=1)) <= bound
