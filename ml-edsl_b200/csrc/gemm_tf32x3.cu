@@ -26,7 +26,8 @@
 // round-to-nearest adds; two TMEM chunk buffers let the MMAs of chunk c+1 run
 // while the epilogue warps drain chunk c.
 //
-// Main kernel (one 128 x 256 output tile per CTA, 320 threads):
+// Main kernel (persistent: one CTA per SM walks 128 x 256 output tiles, or
+// (tile, K-split) units, in a grouped raster; 320 threads):
 //   warp 0      TMA producer: 4 tiles (A_hi, A_lo, B_hi, B_lo) per k-block
 //               into a shared-memory ring: 4 stages of 48 KB (BK = 16,
 //               64-byte swizzle) by default; a 2 x 96 KB ring (BK = 32,
@@ -298,7 +299,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                        const __grid_constant__ CUtensorMap tmAlo,
                        const __grid_constant__ CUtensorMap tmBhi,
                        const __grid_constant__ CUtensorMap tmBlo, int num_kb_total,
-                       int kb_per_split, int tiles_m, int tiles_n, Epilogue ep, int* status) {
+                       int kb_per_split, int tiles_m, int tiles_n, int num_units, Epilogue ep,
+                       int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -309,25 +311,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* conv = tempty + 2;         // epilogue -> MMA: A tile split (kFusedA)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(conv + Cfg::Stages);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* sbias = reinterpret_cast<float*>(smem + Cfg::BiasOffset);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int tiles = tiles_m * tiles_n;
 
-  // Grouped raster so that one wave of CTAs shares A rows and B columns in L2.
-  const int tiles_per_group = kGroupM * tiles_n;
-  const int group = blockIdx.x / tiles_per_group;
-  const int first_m = group * kGroupM;
-  const int group_rows = min(tiles_m - first_m, kGroupM);
-  const int in_group = blockIdx.x - group * tiles_per_group;
-  const int tile_m = first_m + in_group % group_rows;
-  const int tile_n = in_group / group_rows;
-  const int m0 = tile_m * kBM;
-  const int n0 = tile_n * kBN;
-  // Split-K: blockIdx.y selects a contiguous range of k-blocks.
-  const int kb0 = blockIdx.y * kb_per_split;
-  const int num_kb = min(num_kb_total - kb0, kb_per_split);
-  const int num_chunks = (num_kb + Cfg::ChunkKB - 1) / Cfg::ChunkKB;
+  // Work unit u = split * tiles + tile; tiles in a grouped raster so that
+  // CTAs running at the same time share A rows and B columns in L2.
+  struct Unit {
+    int m0, n0, kb0, nkb, split;
+  };
+  auto unit_of = [&](int u) {
+    Unit w;
+    const int tile = u % tiles;
+    w.split = u / tiles;
+    const int tiles_per_group = kGroupM * tiles_n;
+    const int group = tile / tiles_per_group;
+    const int first_m = group * kGroupM;
+    const int group_rows = min(tiles_m - first_m, kGroupM);
+    const int in_group = tile - group * tiles_per_group;
+    w.m0 = (first_m + in_group % group_rows) * kBM;
+    w.n0 = (in_group / group_rows) * kBN;
+    w.kb0 = w.split * kb_per_split;
+    w.nkb = min(num_kb_total - w.kb0, kb_per_split);
+    return w;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < Cfg::Stages; ++s) {
@@ -349,85 +357,100 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmBlo);
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
-  if (warp >= 2) {
-    for (int i = threadIdx.x - 64; i < kBN; i += 32 * kEpiWarps) {
-      const int64_t n = n0 + i;
-      sbias[i] = (ep.bias != nullptr && n < ep.N) ? ep.bias[n] : 0.0f;
-    }
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // Ring stages and TMEM chunk buffers are counted across all units of the
+  // CTA, so their mbarrier phases run on from one tile to the next.
   if (warp == 0) {
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % Cfg::Stages;
-        const int round = kb / Cfg::Stages;
-        if (round > 0 &&
-            !mbar_wait(&empty[s], (round - 1) & 1, status, kDevTimeoutEmpty, abort_flag))
-          break;
-        uint8_t* st = smem + s * Cfg::StageBytes;
-        const int kx = (kb0 + kb) * Cfg::BK;
-        if constexpr (kFusedA) {
-          mbar_arrive_expect_tx(&full[s], Cfg::ATileBytes + 2 * Cfg::BTileBytes);
-          tma_load_2d(st, &tmAhi, &full[s], kx, m0);  // raw f32 X tile
-        } else {
-          mbar_arrive_expect_tx(&full[s], Cfg::StageBytes);
-          tma_load_2d(st, &tmAhi, &full[s], kx, m0);
-          tma_load_2d(st + Cfg::ATileBytes, &tmAlo, &full[s], kx, m0);
+      int it = 0;
+      for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
+        const Unit w = unit_of(u);
+        for (int kb = 0; kb < w.nkb; ++kb, ++it) {
+          const int s = it % Cfg::Stages;
+          const int round = it / Cfg::Stages;
+          if (round > 0 &&
+              !mbar_wait(&empty[s], (round - 1) & 1, status, kDevTimeoutEmpty, abort_flag))
+            break;
+          uint8_t* st = smem + s * Cfg::StageBytes;
+          const int kx = (w.kb0 + kb) * Cfg::BK;
+          if constexpr (kFusedA) {
+            mbar_arrive_expect_tx(&full[s], Cfg::ATileBytes + 2 * Cfg::BTileBytes);
+            tma_load_2d(st, &tmAhi, &full[s], kx, w.m0);  // raw f32 X tile
+          } else {
+            mbar_arrive_expect_tx(&full[s], Cfg::StageBytes);
+            tma_load_2d(st, &tmAhi, &full[s], kx, w.m0);
+            tma_load_2d(st + Cfg::ATileBytes, &tmAlo, &full[s], kx, w.m0);
+          }
+          tma_load_2d(st + 2 * Cfg::ATileBytes, &tmBhi, &full[s], kx, w.n0);
+          tma_load_2d(st + 2 * Cfg::ATileBytes + Cfg::BTileBytes, &tmBlo, &full[s], kx, w.n0);
         }
-        tma_load_2d(st + 2 * Cfg::ATileBytes, &tmBhi, &full[s], kx, n0);
-        tma_load_2d(st + 2 * Cfg::ATileBytes + Cfg::BTileBytes, &tmBlo, &full[s], kx, n0);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_tf32_f32(kBM, kBN);
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % Cfg::Stages;
-        const int round = kb / Cfg::Stages;
-        const int chunk = kb / Cfg::ChunkKB;
-        const int buf = chunk & 1;
-        const bool chunk_start = (kb % Cfg::ChunkKB) == 0;
-        const bool chunk_end = (kb % Cfg::ChunkKB) == Cfg::ChunkKB - 1 || kb == num_kb - 1;
-        if (chunk_start && chunk >= 2) {
-          if (!mbar_wait(&tempty[buf], ((chunk >> 1) - 1) & 1, status, kDevTimeoutAccum,
-                         abort_flag))
+      using D = UmmaDesc<Cfg>;
+      int it = 0, cc = 0;  // k-blocks and TMEM chunks issued by this CTA
+      bool ok = true;
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const Unit w = unit_of(u);
+        for (int kb = 0; kb < w.nkb; ++kb, ++it) {
+          const int s = it % Cfg::Stages;
+          const int round = it / Cfg::Stages;
+          const int buf = cc & 1;
+          const bool chunk_start = (kb % Cfg::ChunkKB) == 0;
+          const bool chunk_end = (kb % Cfg::ChunkKB) == Cfg::ChunkKB - 1 || kb == w.nkb - 1;
+          if (chunk_start && cc >= 2) {
+            if (!mbar_wait(&tempty[buf], ((cc >> 1) - 1) & 1, status, kDevTimeoutAccum,
+                           abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+          }
+          if (!mbar_wait(&full[s], round & 1, status, kDevTimeoutFull, abort_flag)) {
+            ok = false;
             break;
-          tc_fence_after();
-        }
-        if (!mbar_wait(&full[s], round & 1, status, kDevTimeoutFull, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * kBN;
-        const uint32_t st = smem_u32(smem + s * Cfg::StageBytes);
-        using D = UmmaDesc<Cfg>;
-        if constexpr (kFusedA) {
-#pragma unroll
-          for (int k = 0; k < Cfg::BK / 8; ++k) {
-            umma_tf32(d_tmem, D::a_hi(st, k), D::b_lo(st, k), idesc,
-                      (chunk_start && k == 0) ? 0u : 1u);
-            umma_tf32(d_tmem, D::a_hi(st, k), D::b_hi(st, k), idesc, 1u);
           }
-          if (!mbar_wait(&conv[s], round & 1, status, kDevTimeoutFull, abort_flag)) break;
           tc_fence_after();
+          const uint32_t d_tmem = tmem_base + buf * kBN;
+          const uint32_t st = smem_u32(smem + s * Cfg::StageBytes);
+          if constexpr (kFusedA) {
 #pragma unroll
-          for (int k = 0; k < Cfg::BK / 8; ++k)
-            umma_tf32(d_tmem, D::a_lo(st, k), D::b_hi(st, k), idesc, 1u);
-        } else {
+            for (int k = 0; k < Cfg::BK / 8; ++k) {
+              umma_tf32(d_tmem, D::a_hi(st, k), D::b_lo(st, k), idesc,
+                        (chunk_start && k == 0) ? 0u : 1u);
+              umma_tf32(d_tmem, D::a_hi(st, k), D::b_hi(st, k), idesc, 1u);
+            }
+            if (!mbar_wait(&conv[s], round & 1, status, kDevTimeoutFull, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
 #pragma unroll
-          for (int k = 0; k < Cfg::BK / 8; ++k) {  // tf32 UMMA consumes K = 8 (32 B)
-            umma_tf32(d_tmem, D::a_lo(st, k), D::b_hi(st, k), idesc,
-                      (chunk_start && k == 0) ? 0u : 1u);
-            umma_tf32(d_tmem, D::a_hi(st, k), D::b_lo(st, k), idesc, 1u);
-            umma_tf32(d_tmem, D::a_hi(st, k), D::b_hi(st, k), idesc, 1u);
+            for (int k = 0; k < Cfg::BK / 8; ++k)
+              umma_tf32(d_tmem, D::a_lo(st, k), D::b_hi(st, k), idesc, 1u);
+          } else {
+#pragma unroll
+            for (int k = 0; k < Cfg::BK / 8; ++k) {  // tf32 UMMA consumes K = 8 (32 B)
+              umma_tf32(d_tmem, D::a_lo(st, k), D::b_hi(st, k), idesc,
+                        (chunk_start && k == 0) ? 0u : 1u);
+              umma_tf32(d_tmem, D::a_hi(st, k), D::b_lo(st, k), idesc, 1u);
+              umma_tf32(d_tmem, D::a_hi(st, k), D::b_hi(st, k), idesc, 1u);
+            }
+          }
+          umma_commit(&empty[s]);  // stage s may be refilled once these MMAs finish
+          if (chunk_end) {
+            umma_commit(&tfull[buf]);
+            ++cc;
           }
         }
-        umma_commit(&empty[s]);  // stage s may be refilled once these MMAs finish
-        if (chunk_end) umma_commit(&tfull[buf]);
       }
     }
   } else {
@@ -437,13 +460,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = (warp - 2) >> 2;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     float acc[128];
-#pragma unroll
-    for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
     bool ok = true;
-    // Adds chunk c's partial sums (TMEM buffer c % 2) into acc, frees it.
-    auto drain = [&](int c) -> bool {
-      const int buf = c & 1;
-      if (!mbar_wait(&tfull[buf], (c >> 1) & 1, status, kDevTimeoutAccum, abort_flag))
+    int ce = 0;  // TMEM chunks drained by this CTA
+    int it = 0;  // k-blocks converted (kFusedA)
+    // Adds the next chunk's partial sums (TMEM buffer ce % 2) into acc, frees it.
+    auto drain = [&]() -> bool {
+      const int buf = ce & 1;
+      if (!mbar_wait(&tfull[buf], (ce >> 1) & 1, status, kDevTimeoutAccum, abort_flag))
         return false;
       tc_fence_after();
       const uint32_t taddr = tmem_base + lane_off + buf * kBN + half * 128;
@@ -458,58 +481,77 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
+      ++ce;
       return true;
     };
-    if constexpr (kFusedA) {
-      // Split every A tile as it lands; drain chunk c once the conversion has
-      // run kDrainLag k-blocks past its last one, so the MMA always has split
-      // tiles queued while the drain runs.
-      constexpr int kDrainLag = 2;
-      const int et = threadIdx.x - 64;  // 0..255
-      int next = 0;
 #pragma unroll 1
-      for (int kb = 0; kb < num_kb && ok; ++kb) {
-        const int s = kb % Cfg::Stages;
-        if (!mbar_wait(&full[s], (kb / Cfg::Stages) & 1, status, kDevTimeoutFull, abort_flag)) {
-          ok = false;
-          break;
-        }
-        const float4* a = reinterpret_cast<const float4*>(smem + s * Cfg::StageBytes);
-        float4* lo = reinterpret_cast<float4*>(smem + s * Cfg::StageBytes + Cfg::ATileBytes);
+    for (int u = blockIdx.x; u < num_units && ok && !*abort_flag; u += gridDim.x) {
+      const Unit w = unit_of(u);
+      const int num_chunks = (w.nkb + Cfg::ChunkKB - 1) / Cfg::ChunkKB;
 #pragma unroll
-        for (int i = et; i < Cfg::ATileBytes / 16; i += 32 * kEpiWarps) {
-          const float4 v = a[i];
-          float4 h, l;  // h is what the tensor core reads from v
-          tf32_split(v.x, h.x, l.x);
-          tf32_split(v.y, h.y, l.y);
-          tf32_split(v.z, h.z, l.z);
-          tf32_split(v.w, h.w, l.w);
-          lo[i] = l;
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&conv[s]);
-        while (ok && next < num_chunks &&
-               min((next + 1) * Cfg::ChunkKB, num_kb) - 1 + kDrainLag <= kb)
-          ok = drain(next++);
-      }
-      while (ok && next < num_chunks) ok = drain(next++);
-    } else {
+      for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
+      if constexpr (kFusedA) {
+        // Derive every A tile's lo part as it lands; drain chunk c once the
+        // conversion has run kDrainLag k-blocks past its last one, so the MMA
+        // always has converted tiles queued while the drain runs.
+        constexpr int kDrainLag = 2;
+        const int et = threadIdx.x - 64;  // 0..255
+        int next = 0;
 #pragma unroll 1
-      for (int c = 0; c < num_chunks && ok; ++c) ok = drain(c);
-    }
-    if (ok && !*abort_flag) {
-      const int64_t row = (int64_t)m0 + quarter * 32 + lane;
-      const int64_t col0 = (int64_t)n0 + half * 128;
+        for (int kb = 0; kb < w.nkb && ok; ++kb, ++it) {
+          const int s = it % Cfg::Stages;
+          if (!mbar_wait(&full[s], (it / Cfg::Stages) & 1, status, kDevTimeoutFull,
+                         abort_flag)) {
+            ok = false;
+            break;
+          }
+          const float4* a = reinterpret_cast<const float4*>(smem + s * Cfg::StageBytes);
+          float4* lo = reinterpret_cast<float4*>(smem + s * Cfg::StageBytes + Cfg::ATileBytes);
+#pragma unroll
+          for (int i = et; i < Cfg::ATileBytes / 16; i += 32 * kEpiWarps) {
+            const float4 v = a[i];
+            float4 h, l;  // h is what the tensor core reads from v
+            tf32_split(v.x, h.x, l.x);
+            tf32_split(v.y, h.y, l.y);
+            tf32_split(v.z, h.z, l.z);
+            tf32_split(v.w, h.w, l.w);
+            lo[i] = l;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&conv[s]);
+          while (ok && next < num_chunks &&
+                 min((next + 1) * Cfg::ChunkKB, w.nkb) - 1 + kDrainLag <= kb) {
+            ok = drain();
+            ++next;
+          }
+        }
+        while (ok && next < num_chunks) {
+          ok = drain();
+          ++next;
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < num_chunks && ok; ++c) ok = drain();
+      }
+      if (!ok || *abort_flag) break;
+      // The MMAs of the next unit proceed into the two TMEM buffers while
+      // this tile is stored.
+      const int64_t row = (int64_t)w.m0 + quarter * 32 + lane;
+      const int64_t col0 = (int64_t)w.n0 + half * 128;
       if (row < ep.M) {
-        float* dst = ep.Y + blockIdx.y * ep.split_stride + row * ep.ldy + col0;
-        const float* bh = sbias + half * 128;
+        float* dst = ep.Y + w.split * ep.split_stride + row * ep.ldy + col0;
 #pragma unroll
         for (int j = 0; j < 128; j += 4) {
-          const float v0 = apply_act(acc[j] + bh[j], ep.act, ep.alpha);
-          const float v1 = apply_act(acc[j + 1] + bh[j + 1], ep.act, ep.alpha);
-          const float v2 = apply_act(acc[j + 2] + bh[j + 2], ep.act, ep.alpha);
-          const float v3 = apply_act(acc[j + 3] + bh[j + 3], ep.act, ep.alpha);
+          float bb[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            bb[q] = (ep.bias != nullptr && col0 + j + q < ep.N) ? __ldg(ep.bias + col0 + j + q)
+                                                                : 0.0f;
+          const float v0 = apply_act(acc[j] + bb[0], ep.act, ep.alpha);
+          const float v1 = apply_act(acc[j + 1] + bb[1], ep.act, ep.alpha);
+          const float v2 = apply_act(acc[j + 2] + bb[2], ep.act, ep.alpha);
+          const float v3 = apply_act(acc[j + 3] + bb[3], ep.act, ep.alpha);
           if (ep.vec_out && col0 + j + 4 <= ep.N) {
             *reinterpret_cast<float4*>(dst + j) = make_float4(v0, v1, v2, v3);
           } else {
@@ -663,9 +705,23 @@ static int launch_gemm(const CUtensorMap& ta_hi, const CUtensorMap& ta_lo,
   const int num_kb = (int)((K + Cfg::BK - 1) / Cfg::BK);
   const int kb_per_split = (num_kb + splits - 1) / splits;
   const int nsplit = (num_kb + kb_per_split - 1) / kb_per_split;  // every split non-empty
-  gemm_tf32x3_kernel<Cfg, kFusedA>
-      <<<dim3(tiles_m * tiles_n, nsplit), kThreads, Cfg::SmemBytes, stream>>>(
-          ta_hi, ta_lo, tb_hi, tb_lo, num_kb, kb_per_split, tiles_m, tiles_n, ep, status);
+  const int units = tiles_m * tiles_n * nsplit;
+  // Persistent: one CTA per SM (the shared-memory ring admits one) walks the
+  // work units with stride gridDim.x.
+  static int sms[64] = {0};
+  if (sms[dev & 63] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return kErrCuda;
+    sms[dev & 63] = n;
+  }
+  // B200_PERSIST=0: one CTA per unit (the non-persistent schedule), for A/B.
+  static const bool persist = [] {
+    const char* e = getenv("B200_PERSIST");
+    return !(e && e[0] == '0');
+  }();
+  const int grid = persist ? std::min(units, sms[dev & 63]) : units;
+  gemm_tf32x3_kernel<Cfg, kFusedA><<<grid, kThreads, Cfg::SmemBytes, stream>>>(
+      ta_hi, ta_lo, tb_hi, tb_lo, num_kb, kb_per_split, tiles_m, tiles_n, units, ep, status);
   count_launch();
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
