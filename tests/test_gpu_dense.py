@@ -309,3 +309,20 @@ def test_host_api_sharded_over_two_devices(cuda):
     bound = oracle.f32_bound(K, X, W)
     assert max_err(Y1, Y2) <= bound
     assert max_err(Y2[-300:], oracle.dense_f32(X[-300:], W, b, act=1)) <= bound
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (4096, 1, 4096), (8, 8, 16384),
+                                   (65536, 8, 32), (3, 2050, 7), (512, 512, 16384)])
+def test_edge_shapes(cuda, M, N, K):
+    """Single rows / columns, very long K with tiny M and N (split-K at its
+    cap), tall-skinny and wide-short shapes."""
+    import torch
+    X, W, b = _inputs(M, N, K, seed=M + 3 * N + 7 * K)
+    got = dense_device(torch, X, W, b, act=1)
+    rows = np.arange(M) if M <= 2048 else np.random.default_rng(0).choice(M, 2048, replace=False)
+    ref = oracle.dense_f32(X[rows], W, b, act=1)
+    bound = oracle.f32_bound(K, X, W)
+    assert np.isfinite(got).all()
+    assert max_err(got[rows], ref) <= bound
+    exact = np.maximum(X[rows].astype(np.float64) @ W.astype(np.float64) + b, 0)
+    assert float(np.max(np.abs(got[rows] - exact))) <= bound / 10  # f32-level
