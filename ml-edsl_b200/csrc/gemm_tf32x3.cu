@@ -573,6 +573,244 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// 2-SM variant (opt-in, B200_GEMM_2SM=1): a cluster of two CTAs computes a
+// 256 x 256 tile with tcgen05.mma.cta_group::2. Each CTA loads its 128 rows
+// of A and 128 of the 256 B columns (hi and lo) into its own ring: per SM,
+// B traffic is half that of the 1-SM kernel and a stage is 32 KB, so the ring
+// holds 6 stages. The even CTA issues every MMA (both CTAs' TMEM receive
+// their 128 rows x 256 columns); its commits are multicast to the barriers of
+// both CTAs. TMA completions of both CTAs land on the leader's full barrier,
+// whose expected byte count covers both. The peer's epilogue warps release a
+// TMEM chunk with a remote arrive on the leader's tempty barrier.
+struct PairCfg {
+  static constexpr int BK = 16;
+  static constexpr int Stages = 6;
+  static constexpr int ATileBytes = 128 * BK * 4;  // this CTA's 128 rows of A
+  static constexpr int BTileBytes = 128 * BK * 4;  // this CTA's 128 columns of B
+  static constexpr int StageBytes = 2 * ATileBytes + 2 * BTileBytes;  // 32 KB
+  static constexpr int ChunkKB = kChunkK / BK;
+  static constexpr uint32_t UmmaLayout = 4u;  // SWIZZLE_64B
+  static constexpr uint32_t SBO = 8 * BK * 4;
+  static constexpr int BarOffset = Stages * StageBytes;
+  static constexpr int SmemBytes = BarOffset + 256 + 1024;
+  static_assert(SmemBytes <= 232448, "shared memory over the sm_100 limit");
+};
+constexpr int kPairBM = 256;  // rows of a pair tile
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap tmAhi,
+                            const __grid_constant__ CUtensorMap tmAlo,
+                            const __grid_constant__ CUtensorMap tmBhi,
+                            const __grid_constant__ CUtensorMap tmBlo, int num_kb_total,
+                            int kb_per_split, int tiles_m, int tiles_n, int num_units,
+                            Epilogue ep, int* status) {
+  using Cfg = PairCfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::BarOffset);  // (leader) TMA -> MMA
+  uint64_t* empty = full + Cfg::Stages;                                   // MMA -> TMA
+  uint64_t* tfull = empty + Cfg::Stages;  // MMA -> epilogue
+  uint64_t* tempty = tfull + 2;           // (leader) epilogues of both CTAs -> MMA
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+  const int tiles = tiles_m * tiles_n;
+
+  struct Unit {
+    int m0, n0, kb0, nkb, split;
+  };
+  auto unit_of = [&](int u) {
+    Unit w;
+    const int tile = u % tiles;
+    w.split = u / tiles;
+    const int tiles_per_group = kGroupM * tiles_n;
+    const int group = tile / tiles_per_group;
+    const int first_m = group * kGroupM;
+    const int group_rows = min(tiles_m - first_m, kGroupM);
+    const int in_group = tile - group * tiles_per_group;
+    w.m0 = (first_m + in_group % group_rows) * kPairBM;
+    w.n0 = (in_group / group_rows) * kBN;
+    w.kb0 = w.split * kb_per_split;
+    w.nkb = min(num_kb_total - w.kb0, kb_per_split);
+    return w;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::Stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 2 * kEpiWarps);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmAhi);
+    tma_prefetch_desc(&tmAlo);
+    tma_prefetch_desc(&tmBhi);
+    tma_prefetch_desc(&tmBlo);
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int it = 0;
+      for (int u = pair; u < num_units && !*abort_flag; u += npairs) {
+        const Unit w = unit_of(u);
+        const int a_row = w.m0 + (int)rank * 128;
+        const int b_row = w.n0 + (int)rank * 128;
+        for (int kb = 0; kb < w.nkb; ++kb, ++it) {
+          const int s = it % Cfg::Stages;
+          const int round = it / Cfg::Stages;
+          if (round > 0 &&
+              !mbar_wait(&empty[s], (round - 1) & 1, status, kDevTimeoutEmpty, abort_flag))
+            break;
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::StageBytes);
+          uint8_t* st = smem + s * Cfg::StageBytes;
+          const int kx = (w.kb0 + kb) * Cfg::BK;
+          tma_load_2d_pair(st, &tmAhi, &full[s], kx, a_row);
+          tma_load_2d_pair(st + Cfg::ATileBytes, &tmAlo, &full[s], kx, a_row);
+          tma_load_2d_pair(st + 2 * Cfg::ATileBytes, &tmBhi, &full[s], kx, b_row);
+          tma_load_2d_pair(st + 2 * Cfg::ATileBytes + Cfg::BTileBytes, &tmBlo, &full[s], kx,
+                           b_row);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer (leader only)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32_f32(kPairBM, kBN);
+      using D = UmmaDesc<Cfg>;
+      int it = 0, cc = 0;
+      bool ok = true;
+      for (int u = pair; u < num_units && ok; u += npairs) {
+        const Unit w = unit_of(u);
+        for (int kb = 0; kb < w.nkb; ++kb, ++it) {
+          const int s = it % Cfg::Stages;
+          const int round = it / Cfg::Stages;
+          const int buf = cc & 1;
+          const bool chunk_start = (kb % Cfg::ChunkKB) == 0;
+          const bool chunk_end = (kb % Cfg::ChunkKB) == Cfg::ChunkKB - 1 || kb == w.nkb - 1;
+          if (chunk_start && cc >= 2) {
+            if (!mbar_wait(&tempty[buf], ((cc >> 1) - 1) & 1, status, kDevTimeoutAccum,
+                           abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+          }
+          if (!mbar_wait(&full[s], round & 1, status, kDevTimeoutFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + buf * kBN;
+          const uint32_t st = smem_u32(smem + s * Cfg::StageBytes);
+#pragma unroll
+          for (int k = 0; k < Cfg::BK / 8; ++k) {
+            umma_tf32_pair(d_tmem, D::a_lo(st, k), D::b_hi(st, k), idesc,
+                           (chunk_start && k == 0) ? 0u : 1u);
+            umma_tf32_pair(d_tmem, D::a_hi(st, k), D::b_lo(st, k), idesc, 1u);
+            umma_tf32_pair(d_tmem, D::a_hi(st, k), D::b_hi(st, k), idesc, 1u);
+          }
+          umma_commit_pair(&empty[s], 0x3);  // both CTAs may refill stage s
+          if (chunk_end) {
+            umma_commit_pair(&tfull[buf], 0x3);
+            ++cc;
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------ epilogue (8 warps, both CTAs)
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    float acc[128];
+    bool ok = true;
+    int ce = 0;
+#pragma unroll 1
+    for (int u = pair; u < num_units && ok && !*abort_flag; u += npairs) {
+      const Unit w = unit_of(u);
+      const int num_chunks = (w.nkb + Cfg::ChunkKB - 1) / Cfg::ChunkKB;
+#pragma unroll
+      for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
+#pragma unroll 1
+      for (int c = 0; c < num_chunks && ok; ++c, ++ce) {
+        const int buf = ce & 1;
+        if (!mbar_wait(&tfull[buf], (ce >> 1) & 1, status, kDevTimeoutAccum, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + lane_off + buf * kBN + half * 128;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + g * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[g * 32 + j] += __uint_as_float(r[j]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[buf]), 0));
+      }
+      if (!ok || *abort_flag) break;
+      const int64_t row = (int64_t)w.m0 + rank * 128 + quarter * 32 + lane;
+      const int64_t col0 = (int64_t)w.n0 + half * 128;
+      if (row < ep.M) {
+        float* dst = ep.Y + w.split * ep.split_stride + row * ep.ldy + col0;
+#pragma unroll
+        for (int j = 0; j < 128; j += 4) {
+          float bb[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            bb[q] = (ep.bias != nullptr && col0 + j + q < ep.N) ? __ldg(ep.bias + col0 + j + q)
+                                                                : 0.0f;
+          const float v0 = apply_act(acc[j] + bb[0], ep.act, ep.alpha);
+          const float v1 = apply_act(acc[j + 1] + bb[1], ep.act, ep.alpha);
+          const float v2 = apply_act(acc[j + 2] + bb[2], ep.act, ep.alpha);
+          const float v3 = apply_act(acc[j + 3] + bb[3], ep.act, ep.alpha);
+          if (ep.vec_out && col0 + j + 4 <= ep.N) {
+            *reinterpret_cast<float4*>(dst + j) = make_float4(v0, v1, v2, v3);
+          } else {
+            if (col0 + j < ep.N) dst[j] = v0;
+            if (col0 + j + 1 < ep.N) dst[j + 1] = v1;
+            if (col0 + j + 2 < ep.N) dst[j + 2] = v2;
+            if (col0 + j + 3 < ep.N) dst[j + 3] = v3;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the leader's MMAs into this CTA's TMEM are complete
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
 // Failure-detection self-test: one thread waits, with the GEMM's bounded
 // wait, on an mbarrier that nothing ever arrives on. After `limit_ns` the
 // wait gives up and records kDevTimeoutSelfTest in the status word, exactly
@@ -744,9 +982,57 @@ static int run_gemm(const float* xa, const float* xlo, int64_t ldx, bool fused,
   return launch_gemm<Cfg, false>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, ep, splits, status, stream);
 }
 
+// B200_GEMM_2SM=1 selects the 2-SM (CTA pair) kernel for the non-fused path.
+static bool pair_variant() {
+  static const bool on = [] {
+    const char* e = getenv("B200_GEMM_2SM");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
+static int run_gemm_pair(const float* xa, const float* xlo, int64_t ldx, const float* whiT,
+                         const float* wloT, int64_t M, int64_t N, int64_t K, const Epilogue& ep,
+                         int splits, int* status, cudaStream_t stream) {
+  using Cfg = PairCfg;
+  static std::atomic<uint64_t> attr_done{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return kErrCuda;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(attr_done.load() & bit)) {
+    if (cudaFuncSetAttribute(gemm_tf32x3_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cfg::SmemBytes) != cudaSuccess)
+      return kErrCuda;
+    attr_done.fetch_or(bit);
+  }
+  const int64_t Kp = (K + 3) & ~int64_t(3);
+  CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
+  int rc = make_tmap(&ta_hi, xa, K, M, ldx, 128, Cfg::BK);
+  if (rc == kOk) rc = make_tmap(&ta_lo, xlo, K, M, Kp, 128, Cfg::BK);
+  if (rc == kOk) rc = make_tmap(&tb_hi, whiT, K, N, Kp, 128, Cfg::BK);
+  if (rc == kOk) rc = make_tmap(&tb_lo, wloT, K, N, Kp, 128, Cfg::BK);
+  if (rc != kOk) return rc;
+  const int tiles_m = (int)((M + kPairBM - 1) / kPairBM);
+  const int tiles_n = (int)((N + kBN - 1) / kBN);
+  const int num_kb = (int)((K + Cfg::BK - 1) / Cfg::BK);
+  const int kb_per_split = (num_kb + splits - 1) / splits;
+  const int nsplit = (num_kb + kb_per_split - 1) / kb_per_split;
+  const int units = tiles_m * tiles_n * nsplit;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return kErrCuda;
+  const int pairs = std::max(1, std::min(units, sms / 2));
+  gemm_tf32x3_pair_kernel<<<2 * pairs, kThreads, Cfg::SmemBytes, stream>>>(
+      ta_hi, ta_lo, tb_hi, tb_lo, num_kb, kb_per_split, tiles_m, tiles_n, units, ep, status);
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
 static int dispatch_gemm(const float* xa, const float* xlo, int64_t ldx, bool fused,
                          const float* whiT, const float* wloT, int64_t M, int64_t N, int64_t K,
                          const Epilogue& ep, int splits, int* status, cudaStream_t stream) {
+  if (!fused && pair_variant())
+    return run_gemm_pair(xa, xlo, ldx, whiT, wloT, M, N, K, ep, splits, status, stream);
   if (ring_variant() == 0)
     return run_gemm<CfgBK32S2>(xa, xlo, ldx, fused, whiT, wloT, M, N, K, ep, splits, status,
                                stream);
@@ -863,7 +1149,9 @@ static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool
   ep.vec_out = (reinterpret_cast<uintptr_t>(partials) & 15) == 0;
   ep.split_stride = M * ldp;
   // The launcher may use fewer splits so that none is empty; recompute it.
-  const int bk = ring_variant() == 0 ? CfgBK32S2::BK : CfgBK16S4::BK;
+  const int bk = (!fused && pair_variant()) ? PairCfg::BK
+                 : ring_variant() == 0       ? CfgBK32S2::BK
+                                             : CfgBK16S4::BK;
   const int num_kb = (int)((K + bk - 1) / bk);
   const int kbps = (num_kb + splits - 1) / splits;
   const int nsplit = (num_kb + kbps - 1) / kbps;
