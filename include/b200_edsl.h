@@ -172,7 +172,9 @@ int b200_dense_f32_wsplit(const float* X, int64_t ldx, const float* whiT, const 
                           const float* b, float* Y, int64_t ldy, int64_t M, int64_t N, int64_t K,
                           int act, float alpha, void* stream);
 
-/* Device buffers on the current device (synchronous copies). */
+/* Device buffers on the current device, from its stream-ordered memory pool
+ * (allocation and release are ordered on the legacy default stream; freed
+ * blocks stay cached in the pool). Copies are synchronous. */
 int b200_malloc(void** ptr, int64_t bytes);
 int b200_free(void* ptr);
 int b200_memcpy_h2d(void* dst, const void* src, int64_t bytes);
@@ -206,6 +208,12 @@ int b200_dot_i32(const int32_t* a, const int32_t* b, int64_t n, int32_t* out, vo
  * reference: cpp/src/MLIRCompiler.cpp:331-348). */
 int b200_selftest_wait_timeout(int64_t limit_ns, void* stream);
 int b200_debug_fail_alloc(int n);
+
+/* Page-locked host memory from a runtime pool (blocks are cached after
+ * b200_host_free and reused). Results copied back into such buffers move at
+ * full PCIe speed; the Python frontend returns its arrays in them. */
+int b200_host_alloc(void** ptr, int64_t bytes);
+int b200_host_free(void* ptr);
 
 /* --------------------------------------------------- host-pointer entry points */
 

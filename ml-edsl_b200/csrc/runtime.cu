@@ -10,6 +10,8 @@
 #include <cuda_runtime.h>
 #include <algorithm>
 #include <atomic>
+#include <condition_variable>
+#include <functional>
 #include <cstdio>
 #include <cstdlib>
 #include <cmath>
@@ -82,6 +84,120 @@ struct DevBuf {
 
 constexpr int kRing = 3;  // slab buffers in flight per device
 
+// Grow-only page-locked host buffer (staging for pageable user memory).
+struct PinnedBuf {
+  void* p = nullptr;
+  size_t n = 0;
+  cudaError_t reserve(size_t need) {
+    if (need <= n) return cudaSuccess;
+    if (p) cudaFreeHost(p);
+    p = nullptr;
+    n = 0;
+    cudaError_t e = cudaHostAlloc(&p, need, cudaHostAllocPortable);
+    if (e == cudaSuccess) n = need;
+    return e;
+  }
+  void release() {
+    if (p) cudaFreeHost(p);
+    p = nullptr;
+    n = 0;
+  }
+};
+
+// Small persistent pool of host threads for parallel row copies between
+// pageable user memory and the pinned staging buffers.
+class CopyPool {
+ public:
+  static CopyPool& get() {
+    static CopyPool pool;
+    return pool;
+  }
+  // Runs fn(t) for t in [0, nthreads()) and waits for all of them.
+  template <class Fn>
+  void run(Fn fn) {
+    std::unique_lock<std::mutex> lk(mu_);
+    job_ = [&fn](int t) { fn(t); };
+    pending_ = (int)workers_.size();
+    ++gen_;
+    cv_.notify_all();
+    lk.unlock();
+    fn((int)workers_.size());  // the caller is the last participant
+    lk.lock();
+    done_cv_.wait(lk, [&] { return pending_ == 0; });
+  }
+  int nthreads() const { return (int)workers_.size() + 1; }
+
+ private:
+  CopyPool() {
+    // B200_COPY_THREADS overrides the thread count (default: half the
+    // hardware threads, at most 8).
+    unsigned hw = std::thread::hardware_concurrency();
+    int want = (int)std::max(1u, std::min(8u, hw / 2));
+    if (const char* e = getenv("B200_COPY_THREADS")) want = std::max(1, std::min(64, atoi(e)));
+    const int n = want - 1;
+    for (int i = 0; i < n; ++i) workers_.emplace_back([this, i] { loop(i); });
+  }
+  ~CopyPool() {
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      stop_ = true;
+      ++gen_;
+    }
+    cv_.notify_all();
+    for (auto& t : workers_) t.join();
+  }
+  void loop(int id) {
+    uint64_t seen = 0;
+    while (true) {
+      std::function<void(int)> job;
+      {
+        std::unique_lock<std::mutex> lk(mu_);
+        cv_.wait(lk, [&] { return gen_ != seen; });
+        seen = gen_;
+        if (stop_) return;
+        job = job_;
+      }
+      job(id);
+      std::lock_guard<std::mutex> lk(mu_);
+      if (--pending_ == 0) done_cv_.notify_all();
+    }
+  }
+  std::vector<std::thread> workers_;
+  std::mutex mu_;
+  std::condition_variable cv_, done_cv_;
+  std::function<void(int)> job_;
+  int pending_ = 0;
+  uint64_t gen_ = 0;
+  bool stop_ = false;
+};
+
+// rows x row_bytes copy between two pitched host buffers, split over the pool.
+void par_copy_rows(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t row_bytes,
+                   int64_t rows) {
+  CopyPool& pool = CopyPool::get();
+  const int T = pool.nthreads();
+  pool.run([&](int t) {
+    const int64_t r0 = rows * t / T, r1 = rows * (t + 1) / T;
+    char* d = static_cast<char*>(dst) + r0 * dpitch;
+    const char* sp = static_cast<const char*>(src) + r0 * spitch;
+    if (dpitch == row_bytes && spitch == row_bytes) {
+      memcpy(d, sp, (size_t)((r1 - r0) * row_bytes));
+    } else {
+      for (int64_t r = r0; r < r1; ++r, d += dpitch, sp += spitch) memcpy(d, sp, row_bytes);
+    }
+  });
+}
+
+// True for ordinary (not page-locked, not device) host memory.
+bool is_pageable(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return true;
+  }
+  return a.type == cudaMemoryTypeUnregistered;
+}
+
 struct DeviceCtx {
   int dev = -1;
   std::mutex mu;  // one host-pointer call per device at a time
@@ -91,7 +207,9 @@ struct DeviceCtx {
   // host-pointer call buffers
   DevBuf w, whi, wlo, bias;
   DevBuf x[kRing], xhi[kRing], xlo[kRing], y[kRing], part[kRing];
-  cudaEvent_t ev_h2d[kRing], ev_comp[kRing], ev_d2h[kRing];
+  PinnedBuf sx[kRing], sy[kRing];  // staging for pageable X / Y slabs
+  PinnedBuf sc[2];                 // chunk staging for other pageable copies
+  cudaEvent_t ev_h2d[kRing], ev_comp[kRing], ev_d2h[kRing], ev_sc[2];
   // device-pointer call scratch, keyed by stream
   std::map<cudaStream_t, DevBuf> scratch;
 };
@@ -127,6 +245,7 @@ int get_ctx(int dev, DeviceCtx** out) {
       B200_CUDA(cudaEventCreateWithFlags(&c.ev_h2d[i], cudaEventDisableTiming), "event");
       B200_CUDA(cudaEventCreateWithFlags(&c.ev_comp[i], cudaEventDisableTiming), "event");
       B200_CUDA(cudaEventCreateWithFlags(&c.ev_d2h[i], cudaEventDisableTiming), "event");
+      if (i < 2) B200_CUDA(cudaEventCreateWithFlags(&c.ev_sc[i], cudaEventDisableTiming), "event");
     }
     c.dev = dev;
     c.ready = true;
@@ -141,6 +260,100 @@ int current_ctx(DeviceCtx** out) {
   int dev = 0;
   B200_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   return get_ctx(dev, out);
+}
+
+// Pageable copies at least this large go through the pinned staging chunks.
+constexpr int64_t kStageMin = (int64_t)16 << 20;
+constexpr int64_t kStageChunk = (int64_t)32 << 20;
+
+// rows x row_bytes from pitched host memory to pitched device memory on `st`.
+// Pageable sources of kStageMin bytes or more are copied chunk-wise through
+// two pinned buffers: the host copy of chunk j (several threads) overlaps the
+// DMA of chunk j-1. Returns once the source may be reused; the device copy
+// completes in stream order. The caller holds c->mu.
+int h2d_rows(DeviceCtx* c, void* dst, int64_t dpitch, const void* src, int64_t spitch,
+             int64_t row_bytes, int64_t rows, cudaStream_t st) {
+  if (rows <= 0 || row_bytes <= 0) return kOk;
+  if (rows * row_bytes < kStageMin || !is_pageable(src)) {
+    B200_CUDA(cudaMemcpy2DAsync(dst, dpitch, src, spitch, row_bytes, rows,
+                                cudaMemcpyHostToDevice, st),
+              "H2D");
+    return kOk;
+  }
+  const int64_t per = std::max<int64_t>(1, kStageChunk / row_bytes);
+  for (int i = 0; i < 2; ++i) B200_CUDA(c->sc[i].reserve(per * row_bytes), "pinned staging");
+  for (int64_t r0 = 0, j = 0; r0 < rows; r0 += per, ++j) {
+    const int slot = (int)(j & 1);
+    const int64_t n = std::min(per, rows - r0);
+    if (j >= 2) B200_CUDA(cudaEventSynchronize(c->ev_sc[slot]), "staging wait");
+    par_copy_rows(c->sc[slot].p, row_bytes, static_cast<const char*>(src) + r0 * spitch, spitch,
+                  row_bytes, n);
+    B200_CUDA(cudaMemcpy2DAsync(static_cast<char*>(dst) + r0 * dpitch, dpitch, c->sc[slot].p,
+                                row_bytes, row_bytes, n, cudaMemcpyHostToDevice, st),
+              "H2D");
+    B200_CUDA(cudaEventRecord(c->ev_sc[slot], st), "record");
+  }
+  // both staging buffers must be free before the next staged copy reuses them
+  const int64_t nchunk = (rows + per - 1) / per;
+  for (int i = 0; i < 2 && i < nchunk; ++i)
+    B200_CUDA(cudaEventSynchronize(c->ev_sc[i]), "staging wait");
+  return kOk;
+}
+
+// The device-to-host counterpart; returns after the host data is complete.
+int d2h_rows(DeviceCtx* c, void* dst, int64_t dpitch, const void* src, int64_t spitch,
+             int64_t row_bytes, int64_t rows, cudaStream_t st) {
+  if (rows <= 0 || row_bytes <= 0) return kOk;
+  if (rows * row_bytes < kStageMin || !is_pageable(dst)) {
+    B200_CUDA(cudaMemcpy2DAsync(dst, dpitch, src, spitch, row_bytes, rows,
+                                cudaMemcpyDeviceToHost, st),
+              "D2H");
+    B200_CUDA(cudaStreamSynchronize(st), "sync");
+    return kOk;
+  }
+  const int64_t per = std::max<int64_t>(1, kStageChunk / row_bytes);
+  for (int i = 0; i < 2; ++i) B200_CUDA(c->sc[i].reserve(per * row_bytes), "pinned staging");
+  auto unstage = [&](int64_t j) -> int {
+    const int slot = (int)(j & 1);
+    const int64_t r0 = j * per, n = std::min(per, rows - r0);
+    B200_CUDA(cudaEventSynchronize(c->ev_sc[slot]), "staging wait");
+    par_copy_rows(static_cast<char*>(dst) + r0 * dpitch, dpitch, c->sc[slot].p, row_bytes,
+                  row_bytes, n);
+    return kOk;
+  };
+  const int64_t nchunk = (rows + per - 1) / per;
+  for (int64_t j = 0; j < nchunk; ++j) {
+    const int slot = (int)(j & 1);
+    const int64_t r0 = j * per, n = std::min(per, rows - r0);
+    B200_CUDA(cudaMemcpy2DAsync(c->sc[slot].p, row_bytes,
+                                static_cast<const char*>(src) + r0 * spitch, spitch, row_bytes, n,
+                                cudaMemcpyDeviceToHost, st),
+              "D2H");
+    B200_CUDA(cudaEventRecord(c->ev_sc[slot], st), "record");
+    if (j >= 1) {
+      int rc = unstage(j - 1);
+      if (rc) return rc;
+    }
+  }
+  return unstage(nchunk - 1);
+}
+
+// Contiguous copies, viewed as rows of one staging chunk plus a tail row.
+int h2d_flat(DeviceCtx* c, void* dst, const void* src, int64_t bytes, cudaStream_t st) {
+  const int64_t rb = kStageChunk, full = bytes / rb, tail = bytes - full * rb;
+  int rc = full ? h2d_rows(c, dst, rb, src, rb, rb, full, st) : kOk;
+  if (rc == kOk && tail)
+    rc = h2d_rows(c, static_cast<char*>(dst) + full * rb, tail,
+                  static_cast<const char*>(src) + full * rb, tail, tail, 1, st);
+  return rc;
+}
+int d2h_flat(DeviceCtx* c, void* dst, const void* src, int64_t bytes, cudaStream_t st) {
+  const int64_t rb = kStageChunk, full = bytes / rb, tail = bytes - full * rb;
+  int rc = full ? d2h_rows(c, dst, rb, src, rb, rb, full, st) : kOk;
+  if (rc == kOk && tail)
+    rc = d2h_rows(c, static_cast<char*>(dst) + full * rb, tail,
+                  static_cast<const char*>(src) + full * rb, tail, tail, 1, st);
+  return rc;
 }
 
 // Reads and clears the device status word after the stream has drained.
@@ -275,6 +488,11 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
     slab = std::max<int64_t>(512, round_up((M + nslabs_cfg - 1) / nslabs_cfg, 128));
   }
   const int64_t nslab = (M + slab - 1) / slab;
+  // Pageable X / Y (e.g. plain numpy arrays) are staged through pinned slab
+  // buffers with a multi-threaded host copy that overlaps the DMA of other
+  // slabs; the driver's own staging of pageable copies is much slower.
+  const bool stage_x = K > 0 && M * K * 4 >= ((int64_t)16 << 20) && is_pageable(X);
+  const bool stage_y = M * N * 4 >= ((int64_t)16 << 20) && is_pageable(Y);
 
   // Weights (replicated): upload + split once per call on the compute stream.
   B200_CUDA(c->bias.reserve(std::max<int64_t>(N, 1) * 4), "alloc bias");
@@ -288,6 +506,8 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
                                               splitk_partials_bytes(last_rows, N, K))
                                    : 0;
   for (int i = 0; i < kRing && i < nslab; ++i) {
+    if (stage_x) B200_CUDA(c->sx[i].reserve(slab * K * 4), "pinned X staging");
+    if (stage_y) B200_CUDA(c->sy[i].reserve(slab * N * 4), "pinned Y staging");
     B200_CUDA(c->y[i].reserve(slab * N * 4), "alloc Y slab");
     if (part_bytes) B200_CUDA(c->part[i].reserve(part_bytes), "alloc split-K partials");
     if (K > 0) {
@@ -302,9 +522,7 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
   float* db = b ? static_cast<float*>(c->bias.p) : nullptr;
   if (b) B200_CUDA(cudaMemcpyAsync(db, b, N * 4, cudaMemcpyHostToDevice, c->s_comp), "H2D b");
   if (K > 0) {
-    B200_CUDA(cudaMemcpy2DAsync(dW, N * 4, W, ldw * 4, N * 4, K, cudaMemcpyHostToDevice,
-                                c->s_comp),
-              "H2D W");
+    if ((rc = h2d_rows(c, dW, N * 4, W, ldw * 4, N * 4, K, c->s_comp))) return rc;
     // A single-slab call splits W together with X (one launch) below.
     if (nslab > 1 || fuse_a(static_cast<float*>(c->x[0].p), K)) {
       rc = split_w_f32(dW, N, K, N, dWhi, dWlo, c->s_comp);
@@ -321,10 +539,18 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
     // Slot reuse: the copy-in may overwrite X once slab i-kRing's compute has
     // read it; the compute may overwrite Y once slab i-kRing's copy-out is done.
     if (i >= kRing) B200_CUDA(cudaStreamWaitEvent(c->s_h2d, c->ev_comp[slot], 0), "wait");
-    if (K > 0)
+    if (K > 0 && stage_x) {
+      // staging slot free once slab i-kRing's copy from it has finished
+      if (i >= kRing) B200_CUDA(cudaEventSynchronize(c->ev_h2d[slot]), "staging wait");
+      par_copy_rows(c->sx[slot].p, K * 4, X + r0 * ldx, ldx * 4, K * 4, rows);
+      B200_CUDA(cudaMemcpyAsync(dX, c->sx[slot].p, rows * K * 4, cudaMemcpyHostToDevice,
+                                c->s_h2d),
+                "H2D X");
+    } else if (K > 0) {
       B200_CUDA(cudaMemcpy2DAsync(dX, K * 4, X + r0 * ldx, ldx * 4, K * 4, rows,
                                   cudaMemcpyHostToDevice, c->s_h2d),
                 "H2D X");
+    }
     B200_CUDA(cudaEventRecord(c->ev_h2d[slot], c->s_h2d), "record");
     B200_CUDA(cudaStreamWaitEvent(c->s_comp, c->ev_h2d[slot], 0), "wait");
     if (i >= kRing) B200_CUDA(cudaStreamWaitEvent(c->s_comp, c->ev_d2h[slot], 0), "wait");
@@ -356,10 +582,28 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
     if (rc) return fail(rc, "dense kernel launch failed");
     B200_CUDA(cudaEventRecord(c->ev_comp[slot], c->s_comp), "record");
     B200_CUDA(cudaStreamWaitEvent(c->s_d2h, c->ev_comp[slot], 0), "wait");
-    B200_CUDA(cudaMemcpy2DAsync(Y + r0 * ldy, ldy * 4, dY, N * 4, N * 4, rows,
-                                cudaMemcpyDeviceToHost, c->s_d2h),
-              "D2H Y");
+    if (stage_y) {
+      B200_CUDA(cudaMemcpyAsync(c->sy[slot].p, dY, rows * N * 4, cudaMemcpyDeviceToHost,
+                                c->s_d2h),
+                "D2H Y");
+    } else {
+      B200_CUDA(cudaMemcpy2DAsync(Y + r0 * ldy, ldy * 4, dY, N * 4, N * 4, rows,
+                                  cudaMemcpyDeviceToHost, c->s_d2h),
+                "D2H Y");
+    }
     B200_CUDA(cudaEventRecord(c->ev_d2h[slot], c->s_d2h), "record");
+    if (stage_y && i >= 1) {  // unstage the previous slab while this one computes
+      const int ps = (int)((i - 1) % kRing);
+      const int64_t pr0 = (i - 1) * slab;
+      B200_CUDA(cudaEventSynchronize(c->ev_d2h[ps]), "unstage wait");
+      par_copy_rows(Y + pr0 * ldy, ldy * 4, c->sy[ps].p, N * 4, N * 4, std::min(slab, M - pr0));
+    }
+  }
+  if (stage_y) {
+    const int64_t li = nslab - 1;
+    const int ls = (int)(li % kRing);
+    B200_CUDA(cudaEventSynchronize(c->ev_d2h[ls]), "unstage wait");
+    par_copy_rows(Y + li * slab * ldy, ldy * 4, c->sy[ls].p, N * 4, N * 4, M - li * slab);
   }
   B200_CUDA(cudaStreamSynchronize(c->s_d2h), "sync");
   B200_CUDA(cudaStreamSynchronize(c->s_comp), "sync");
@@ -425,17 +669,13 @@ int simple_host_i32_matmul(int dev, const int32_t* A, int64_t lda, const int32_t
   int32_t* db = bias ? static_cast<int32_t*>(c->bias.p) : nullptr;
   cudaStream_t s = c->s_comp;
   if (K > 0) {
-    B200_CUDA(cudaMemcpy2DAsync(dA, K * 4, A, lda * 4, K * 4, M, cudaMemcpyHostToDevice, s),
-              "H2D A");
-    B200_CUDA(cudaMemcpy2DAsync(dB, N * 4, B, ldb * 4, N * 4, K, cudaMemcpyHostToDevice, s),
-              "H2D B");
+    if ((rc = h2d_rows(c, dA, K * 4, A, lda * 4, K * 4, M, s))) return rc;
+    if ((rc = h2d_rows(c, dB, N * 4, B, ldb * 4, N * 4, K, s))) return rc;
   }
   if (bias) B200_CUDA(cudaMemcpyAsync(db, bias, N * 4, cudaMemcpyHostToDevice, s), "H2D bias");
   rc = gemm_i32(dA, K, dB, N, dC, N, M, N, K, db, s);
   if (rc) return fail(rc, "i32 matmul launch failed");
-  B200_CUDA(cudaMemcpy2DAsync(C, ldc * 4, dC, N * 4, N * 4, M, cudaMemcpyDeviceToHost, s),
-            "D2H C");
-  B200_CUDA(cudaStreamSynchronize(s), "sync");
+  if ((rc = d2h_rows(c, C, ldc * 4, dC, N * 4, N * 4, M, s))) return rc;
   return kOk;
 }
 
@@ -452,13 +692,11 @@ int elementwise_host(size_t in_bytes_x, const void* X, size_t in_bytes_b, const 
   B200_CUDA(c->bias.reserve(std::max<size_t>(in_bytes_b, 4)), "alloc b");
   B200_CUDA(c->y[0].reserve(out_bytes), "alloc Y");
   cudaStream_t s = c->s_comp;
-  B200_CUDA(cudaMemcpyAsync(c->x[0].p, X, in_bytes_x, cudaMemcpyHostToDevice, s), "H2D X");
+  if ((rc = h2d_flat(c, c->x[0].p, X, (int64_t)in_bytes_x, s))) return rc;
   if (b) B200_CUDA(cudaMemcpyAsync(c->bias.p, b, in_bytes_b, cudaMemcpyHostToDevice, s), "H2D b");
   rc = launch(c->x[0].p, b ? c->bias.p : nullptr, c->y[0].p, s);
   if (rc) return fail(rc, "elementwise launch failed");
-  B200_CUDA(cudaMemcpyAsync(Y, c->y[0].p, out_bytes, cudaMemcpyDeviceToHost, s), "D2H Y");
-  B200_CUDA(cudaStreamSynchronize(s), "sync");
-  return kOk;
+  return d2h_flat(c, Y, c->y[0].p, (int64_t)out_bytes, s);
 }
 
 
@@ -475,9 +713,8 @@ int reduce_host_impl(const T* x, const T* y, int64_t n, int op, T init, T* resul
   if (y) B200_CUDA(c->w.reserve(bytes), "alloc y");
   B200_CUDA(c->y[0].reserve((size_t)reduce_scratch_bytes() + 256), "alloc partials");
   cudaStream_t s = c->s_comp;
-  if (n) B200_CUDA(cudaMemcpyAsync(c->x[0].p, x, n * sizeof(T), cudaMemcpyHostToDevice, s), "H2D x");
-  if (y && n)
-    B200_CUDA(cudaMemcpyAsync(c->w.p, y, n * sizeof(T), cudaMemcpyHostToDevice, s), "H2D y");
+  if (n && (rc = h2d_flat(c, c->x[0].p, x, n * (int64_t)sizeof(T), s))) return rc;
+  if (y && n && (rc = h2d_flat(c, c->w.p, y, n * (int64_t)sizeof(T), s))) return rc;
   char* scratch = static_cast<char*>(c->y[0].p);
   T* dout = reinterpret_cast<T*>(scratch + reduce_scratch_bytes());
   if constexpr (std::is_same<T, float>::value)
@@ -565,6 +802,9 @@ int b200_release(void) {
     for (int i = 0; i < kRing; ++i) {
       c.x[i].release(); c.xhi[i].release(); c.xlo[i].release(); c.y[i].release();
       c.part[i].release();
+      if (i < 2) c.sc[i].release();
+      c.sx[i].release();
+      c.sy[i].release();
     }
     for (auto& kv : c.scratch) kv.second.release();
     c.scratch.clear();
@@ -764,29 +1004,74 @@ int b200_dense_f32_wsplit(const float* X, int64_t ldx, const float* whiT, const 
 }
 
 // ---------------------------------------------------------------- device buffers
+// Device buffers come from the device's stream-ordered memory pool with its
+// release threshold raised, so freed blocks stay cached for the next call
+// instead of returning to the driver (cudaFree would synchronise the device).
+static int pool_ready(int dev) {
+  static std::atomic<uint64_t> done{0};
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done.load() & bit) return kOk;
+  cudaMemPool_t pool;
+  B200_CUDA(cudaDeviceGetDefaultMemPool(&pool, dev), "cudaDeviceGetDefaultMemPool");
+  uint64_t threshold = UINT64_MAX;
+  B200_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold),
+            "cudaMemPoolSetAttribute");
+  done.fetch_or(bit);
+  return kOk;
+}
+
 int b200_malloc(void** ptr, int64_t bytes) {
   if (!ptr || bytes < 0) return fail(kErrInvalidArg, "bad malloc arguments");
   *ptr = nullptr;
   if (bytes == 0) return succeed();
   if (device_count() == 0) return fail(kErrNoDevice, "no CUDA device available");
-  B200_CUDA(cudaMalloc(ptr, (size_t)bytes), "cudaMalloc");
+  int dev = 0;
+  B200_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  int rc = pool_ready(dev);
+  if (rc) return rc;
+  B200_CUDA(cudaMallocAsync(ptr, (size_t)bytes, nullptr), "cudaMallocAsync");
   return succeed();
 }
 
 int b200_free(void* ptr) {
-  if (ptr) B200_CUDA(cudaFree(ptr), "cudaFree");
+  if (ptr) B200_CUDA(cudaFreeAsync(ptr, nullptr), "cudaFreeAsync");
   return succeed();
 }
 
+// Large pageable host buffers are staged through the runtime's pinned chunks
+// (parallel host copies overlapping the DMA); everything else is one copy.
+// Both calls are synchronous with respect to the host buffer.
 int b200_memcpy_h2d(void* dst, const void* src, int64_t bytes) {
   if (bytes < 0) return fail(kErrInvalidArg, "negative size");
-  if (bytes) B200_CUDA(cudaMemcpy(dst, src, (size_t)bytes, cudaMemcpyHostToDevice), "H2D");
+  if (!bytes) return succeed();
+  if (bytes < kStageMin) {
+    B200_CUDA(cudaMemcpy(dst, src, (size_t)bytes, cudaMemcpyHostToDevice), "H2D");
+    return succeed();
+  }
+  DeviceCtx* c = nullptr;
+  int rc = current_ctx(&c);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(c->mu);
+  // cudaMemcpy's ordering: after the work queued on the legacy default stream
+  B200_CUDA(cudaStreamSynchronize(nullptr), "sync");
+  if ((rc = h2d_flat(c, dst, src, bytes, c->s_h2d))) return rc;
+  B200_CUDA(cudaStreamSynchronize(c->s_h2d), "sync");
   return succeed();
 }
 
 int b200_memcpy_d2h(void* dst, const void* src, int64_t bytes) {
   if (bytes < 0) return fail(kErrInvalidArg, "negative size");
-  if (bytes) B200_CUDA(cudaMemcpy(dst, src, (size_t)bytes, cudaMemcpyDeviceToHost), "D2H");
+  if (!bytes) return succeed();
+  if (bytes < kStageMin) {
+    B200_CUDA(cudaMemcpy(dst, src, (size_t)bytes, cudaMemcpyDeviceToHost), "D2H");
+    return succeed();
+  }
+  DeviceCtx* c = nullptr;
+  int rc = current_ctx(&c);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(c->mu);
+  B200_CUDA(cudaStreamSynchronize(nullptr), "sync");
+  if ((rc = d2h_flat(c, dst, src, bytes, c->s_d2h))) return rc;
   return succeed();
 }
 
@@ -832,6 +1117,58 @@ int b200_dot_i32_host(const int32_t* a, const int32_t* b, int64_t n, int32_t* re
   if (n < 0 || !result || (n > 0 && (!a || !b))) return fail(kErrInvalidArg, "bad dot arguments");
   int rc = reduce_host_impl<int32_t>(a, b, n, kRedSum, 0, result);
   return rc ? rc : succeed();
+}
+
+// ---------------------------------------------------------------- pinned host pool
+// Page-locked host blocks for results returned to Python: device-to-host
+// copies into them run at full PCIe speed and never fault pages in. Freed
+// blocks are kept (bucketed by size rounded up to 2 MiB, at most
+// kPinnedCacheBytes in total) and handed out again.
+namespace {
+constexpr size_t kPinnedBucket = (size_t)2 << 20;
+constexpr size_t kPinnedCacheBytes = (size_t)16 << 30;
+std::mutex g_pin_mu;
+std::multimap<size_t, void*> g_pin_free;   // bucketed size -> block
+std::map<void*, size_t> g_pin_size;        // live and cached blocks
+size_t g_pin_cached = 0;
+}  // namespace
+
+int b200_host_alloc(void** ptr, int64_t bytes) {
+  if (!ptr || bytes < 0) return fail(kErrInvalidArg, "bad host_alloc arguments");
+  *ptr = nullptr;
+  if (bytes == 0) return succeed();
+  if (device_count() == 0) return fail(kErrNoDevice, "no CUDA device available");
+  const size_t sz = ((size_t)bytes + kPinnedBucket - 1) / kPinnedBucket * kPinnedBucket;
+  {
+    std::lock_guard<std::mutex> lk(g_pin_mu);
+    auto it = g_pin_free.find(sz);
+    if (it != g_pin_free.end()) {
+      *ptr = it->second;
+      g_pin_free.erase(it);
+      g_pin_cached -= sz;
+      return succeed();
+    }
+  }
+  B200_CUDA(cudaHostAlloc(ptr, sz, cudaHostAllocPortable), "cudaHostAlloc");
+  std::lock_guard<std::mutex> lk(g_pin_mu);
+  g_pin_size[*ptr] = sz;
+  return succeed();
+}
+
+int b200_host_free(void* ptr) {
+  if (!ptr) return succeed();
+  std::lock_guard<std::mutex> lk(g_pin_mu);
+  auto it = g_pin_size.find(ptr);
+  if (it == g_pin_size.end()) return fail(kErrInvalidArg, "pointer not from b200_host_alloc");
+  const size_t sz = it->second;
+  if (g_pin_cached + sz <= kPinnedCacheBytes) {
+    g_pin_free.emplace(sz, ptr);
+    g_pin_cached += sz;
+  } else {
+    g_pin_size.erase(it);
+    cudaFreeHost(ptr);
+  }
+  return succeed();
 }
 
 // ---------------------------------------------------------------- failure detection

@@ -33,7 +33,7 @@ EXPORTED_SYMBOLS = [
     "b200_tf32_split_rows", "b200_tf32_split_transpose", "b200_gemm_tf32x3_presplit",
     "b200_dense_f32_wsplit",
     "b200_malloc", "b200_free", "b200_memcpy_h2d", "b200_memcpy_d2h",
-    "b200_selftest_wait_timeout", "b200_debug_fail_alloc",
+    "b200_selftest_wait_timeout", "b200_debug_fail_alloc", "b200_host_alloc", "b200_host_free",
     "b200_dense_f32_host", "b200_matmul_i32_host", "b200_bias_act_f32_host",
     "b200_bias_add_i32_host", "b200_act_f32_host",
     "b200_reduce_f32", "b200_reduce_i32", "b200_dot_f32", "b200_dot_i32",
@@ -88,6 +88,8 @@ def _declare(lib):
                                   i32),
         "b200_malloc": ([c.POINTER(vp), i64], i32),
         "b200_selftest_wait_timeout": ([i64, vp], i32),
+        "b200_host_alloc": ([c.POINTER(vp), i64], i32),
+        "b200_host_free": ([vp], i32),
         "b200_debug_fail_alloc": ([i32], i32),
         "b200_free": ([vp], i32),
         "b200_memcpy_h2d": ([vp, vp, i64], i32),
@@ -157,3 +159,21 @@ def dense_launches(M, N, K):
 
 def device_count():
     return int(lib().b200_device_count())
+
+
+def pinned_empty(shape, dtype):
+    """An uninitialised numpy array in page-locked memory from the runtime's
+    pool; the block returns to the pool when the array (and every view of it)
+    is garbage-collected."""
+    import weakref
+    import numpy as np
+    dtype = np.dtype(dtype)
+    nbytes = int(np.prod(shape)) * dtype.itemsize
+    if nbytes == 0:
+        return np.empty(shape, dtype)
+    L = lib()
+    p = ctypes.c_void_p()
+    check(L.b200_host_alloc(ctypes.byref(p), nbytes))
+    buf = (ctypes.c_byte * nbytes).from_address(p.value)
+    weakref.finalize(buf, L.b200_host_free, ctypes.c_void_p(p.value))
+    return np.frombuffer(buf, dtype=dtype, count=int(np.prod(shape))).reshape(shape)

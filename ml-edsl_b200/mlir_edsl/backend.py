@@ -54,8 +54,19 @@ def _memref_descriptor(data: np.ndarray, array_type: TensorType):
     return c_types, c_vals, data
 
 
+# Results of at least this many bytes are returned in page-locked memory.
+PINNED_OUTPUT_BYTES = 1 << 20
+
+
+def _new_output(shape, dtype):
+    nbytes = int(np.prod(shape)) * np.dtype(dtype).itemsize
+    if nbytes >= PINNED_OUTPUT_BYTES:
+        return _native.pinned_empty(shape, dtype)
+    return np.empty(shape, dtype=dtype)
+
+
 def _output_descriptor(shape, dtype):
-    buf = np.empty(shape, dtype=dtype)
+    buf = _new_output(shape, dtype)
     ptr = buf.ctypes.data_as(ctypes.c_void_p)
     nd = len(shape)
     strides = [1] * nd
@@ -309,7 +320,7 @@ class B200Backend:
             final = plan.steps[plan.output.index]
             if final.shape == ():
                 return _to_python(scalar(plan.output))
-            res = np.empty(final.shape, np.float32 if final.dtype == "f32" else np.int32)
+            res = _new_output(final.shape, np.float32 if final.dtype == "f32" else np.int32)
             _native.check(L.b200_memcpy_d2h(res.ctypes.data_as(ctypes.c_void_p),
                                             douts[plan.output.index], res.nbytes))
             return res

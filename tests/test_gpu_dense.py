@@ -158,6 +158,25 @@ def test_host_api_pipelined_slabs(cuda):
     assert max_err(Y, ref) <= oracle.f32_bound(K, X, W)
 
 
+def test_host_api_staged_pageable_strided(cuda):
+    """Pageable X and Y above the staging threshold with row pitches larger
+    than the rows: both go through the pinned staging ring (parallel host
+    copies), and the padding columns of Y stay untouched."""
+    M, N, K, ldx, ldy = 8192, 1024, 640, 700, 1100
+    X, W, b = _inputs(M, N, K, seed=37)
+    Xs = np.full((M, ldx), 7.0, np.float32)
+    Xs[:, :K] = X
+    Y = np.full((M, ldy), np.nan, np.float32)
+    L = _native.lib()
+    c = ctypes.c_void_p
+    _native.check(L.b200_dense_f32_host(c(Xs.ctypes.data), ldx, c(W.ctypes.data), N,
+                                        c(b.ctypes.data), c(Y.ctypes.data), ldy, M, N, K, 2,
+                                        0.05, 1))
+    ref = oracle.dense_f32(X, W, b, act=2, alpha=0.05)
+    assert max_err(Y[:, :N], ref) <= oracle.f32_bound(K, X, W)
+    assert np.isnan(Y[:, N:]).all()
+
+
 def test_workspace_entry_point(cuda):
     import torch
     dev = torch.device("cuda:0")

@@ -101,3 +101,31 @@ def test_bias_add_i32_host(cuda):
                                            c(Y.ctypes.data), 30, 20, 30))
     np.testing.assert_array_equal(Y, (X.astype(np.int64) + b).astype(np.uint32).astype(np.int32)
                                   if False else (X.view(np.uint32) + b.view(np.uint32)).view(np.int32))
+
+
+def test_staged_copies_round_trip(cuda):
+    """b200_memcpy_h2d / _d2h with pageable buffers above the staging
+    threshold (several 32 MiB chunks plus a ragged tail) and below it."""
+    L = _native.lib()
+    c = ctypes.c_void_p
+    for nbytes in (100 * (1 << 20) + 12345, 1000):
+        src = np.random.default_rng(nbytes).integers(0, 256, nbytes, dtype=np.uint8)
+        dst = np.zeros(nbytes, np.uint8)
+        d = c()
+        _native.check(L.b200_malloc(ctypes.byref(d), nbytes))
+        try:
+            _native.check(L.b200_memcpy_h2d(d, c(src.ctypes.data), nbytes))
+            _native.check(L.b200_memcpy_d2h(c(dst.ctypes.data), d, nbytes))
+        finally:
+            _native.check(L.b200_free(d))
+        np.testing.assert_array_equal(dst, src)
+
+
+def test_act_f32_host_staged(cuda):
+    """A pageable 64 MiB tensor through the host elementwise entry point."""
+    L = _native.lib()
+    x = np.random.default_rng(5).standard_normal(1 << 24).astype(np.float32)
+    y = np.full_like(x, np.nan)
+    _native.check(L.b200_act_f32_host(ctypes.c_void_p(x.ctypes.data),
+                                      ctypes.c_void_p(y.ctypes.data), x.size, 1, 0.0))
+    np.testing.assert_array_equal(y, np.maximum(x, 0) + 0.0)
