@@ -43,6 +43,7 @@
 #include <cuda_runtime.h>
 #include <algorithm>
 #include <atomic>
+#include <type_traits>
 #include <cstdlib>
 #include <cstring>
 #include <cstdint>
@@ -242,6 +243,54 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Rows of a row-major [rows, cols] matrix (pitch ld) -> lo (and hi when
+// non-null) with pitch pc = roundup(cols, 4); pad columns zero. Quads
+// i0, i0 + step, ... of the rows * pc / 4 output quads.
+__device__ __forceinline__ void split_quads(const float* __restrict__ src, int64_t ld,
+                                            int64_t rows, int64_t cols, int64_t pc,
+                                            float* __restrict__ hi, float* __restrict__ lo,
+                                            int64_t i0, int64_t step) {
+  const int64_t q_per_row = pc >> 2;
+  const int64_t total = rows * q_per_row;
+  const int vec_in = ((ld & 3) == 0) && ((reinterpret_cast<uintptr_t>(src) & 15) == 0);
+  for (int64_t i = i0; i < total; i += step) {
+    const int64_t r = i / q_per_row;
+    const int64_t c = (i - r * q_per_row) << 2;
+    float v[4];
+    if (vec_in && c + 4 <= cols) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(src + r * ld + c));
+      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = (c + j < cols) ? __ldg(src + r * ld + c + j) : 0.0f;
+    }
+    float4 h, l;
+    tf32_split(v[0], h.x, l.x);
+    tf32_split(v[1], h.y, l.y);
+    tf32_split(v[2], h.z, l.z);
+    tf32_split(v[3], h.w, l.w);
+    if (hi) *reinterpret_cast<float4*>(hi + r * pc + c) = h;
+    *reinterpret_cast<float4*>(lo + r * pc + c) = l;
+  }
+}
+
+// Pre-pass 4, for the MN-major B operand: X -> X_lo [M, Kp] (and X_hi when
+// xhi is non-null) and W [K, N] -> W_lo [K, Np] (row-major, not transposed)
+// in one launch; the GEMM reads the raw W as B_hi. Blocks [0, x_blocks)
+// take X, the rest W. 256 threads.
+__global__ void __launch_bounds__(256)
+    split_lo_xw_kernel(const float* __restrict__ X, int64_t ldx, int64_t M, int64_t K,
+                       int64_t Kp, int x_blocks, float* __restrict__ xhi,
+                       float* __restrict__ xlo, const float* __restrict__ W, int64_t ldw,
+                       int64_t N, int64_t Np, float* __restrict__ wlo) {
+  if ((int)blockIdx.x < x_blocks)
+    split_quads(X, ldx, M, K, Kp, xhi, xlo, blockIdx.x * 256ll + threadIdx.x,
+                (int64_t)x_blocks * 256);
+  else
+    split_quads(W, ldw, K, N, Np, nullptr, wlo, (blockIdx.x - x_blocks) * 256ll + threadIdx.x,
+                (int64_t)(gridDim.x - x_blocks) * 256);
+}
+
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float apply_act(float x, int act, float alpha) {
   if (act == kActRelu) {
@@ -287,13 +336,35 @@ struct UmmaDesc {
   }
 };
 
+// B tiles stored MN-major (the raw row-major W[K, N] and its lo part): each
+// B tile is 8 blocks of BK K-rows x 128 bytes (32 columns), one TMA box
+// each, in the 32-byte-atom 128-byte swizzle; k-step k (8 rows) starts
+// 1 KB into every block, and its two 4-row groups are 512 bytes apart.
+template <class Cfg>
+struct UmmaDescBMn {
+  static constexpr uint32_t kAtomBytes = Cfg::BK * 128;
+  static __device__ __forceinline__ uint64_t b_hi(uint32_t st, int k) {
+    return umma_desc_mn_sw128_32b<kAtomBytes, 512>(st + 2 * Cfg::ATileBytes + k * 1024);
+  }
+  static __device__ __forceinline__ uint64_t b_lo(uint32_t st, int k) {
+    return umma_desc_mn_sw128_32b<kAtomBytes, 512>(st + 2 * Cfg::ATileBytes +
+                                                     Cfg::BTileBytes + k * 1024);
+  }
+};
+
 // kFusedA: the A operand arrives as raw f32 X tiles (one TMA load into the
 // A_hi slot). The tensor core reads a tf32 operand from f32 bits by ignoring
 // the low 13 mantissa bits, so the raw tile serves as A_hi unchanged; the
 // epilogue warps derive A_lo = x - hi into the A_lo slot and release it to
 // the MMA through conv[s]. The MMA issues the two products that use A_hi as
 // soon as the tile lands and the lo * B_hi product after conv[s].
-template <class Cfg, bool kFusedA>
+//
+// kBMn: B_hi is the raw f32 W (row-major [K, N], read as an MN-major tf32
+// operand: the tensor core drops the low 13 mantissa bits, which is the hi
+// part) and B_lo the row-major lo part, so W needs neither a transpose nor a
+// hi copy. The producer warp's lanes issue the two B tiles and two A tiles of a
+// stage from separate lanes.
+template <class Cfg, bool kFusedA, bool kBMn>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAhi,
                        const __grid_constant__ CUtensorMap tmAlo,
@@ -364,7 +435,46 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // Ring stages and TMEM chunk buffers are counted across all units of the
   // CTA, so their mbarrier phases run on from one tile to the next.
-  if (warp == 0) {
+  static_assert(!(kFusedA && kBMn), "fused A split uses K-major B");
+  if (warp == 0 && kBMn) {
+    // ------------------------------------------------ TMA producer (MN-major B)
+    // Lane 0 waits for the stage and posts the byte count; the decision is
+    // broadcast so that the whole warp leaves the loop together.
+    int it = 0;
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+      int go = lane == 0 ? !*abort_flag : 0;
+      if (!__shfl_sync(0xffffffffu, go, 0)) break;
+      const Unit w = unit_of(u);
+      bool ok = true;
+      for (int kb = 0; kb < w.nkb; ++kb, ++it) {
+        const int s = it % Cfg::Stages;
+        const int round = it / Cfg::Stages;
+        go = 1;
+        if (lane == 0) {
+          if (round > 0 &&
+              !mbar_wait(&empty[s], (round - 1) & 1, status, kDevTimeoutEmpty, abort_flag))
+            go = 0;
+          else
+            mbar_arrive_expect_tx(&full[s], Cfg::StageBytes);
+        }
+        if (!__shfl_sync(0xffffffffu, go, 0)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + s * Cfg::StageBytes;
+        const int kx = (w.kb0 + kb) * Cfg::BK;
+        if (lane < 2) {  // whole 256-column B tile: {0, kx, n0 / 32}
+          tma_load_3d(st + 2 * Cfg::ATileBytes + lane * Cfg::BTileBytes,
+                      lane == 0 ? &tmBhi : &tmBlo, &full[s], 0, kx, w.n0 / 32);
+        } else if (lane == 2) {
+          tma_load_2d(st, &tmAhi, &full[s], kx, w.m0);
+        } else if (lane == 3) {
+          tma_load_2d(st + Cfg::ATileBytes, &tmAlo, &full[s], kx, w.m0);
+        }
+      }
+      if (!ok) break;
+    }
+  } else if (warp == 0) {
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
       int it = 0;
@@ -394,8 +504,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32_f32(kBM, kBN);
+      constexpr uint32_t idesc = kBMn ? idesc_tf32_f32_bmn(kBM, kBN) : idesc_tf32_f32(kBM, kBN);
       using D = UmmaDesc<Cfg>;
+      using DB = typename std::conditional<kBMn, UmmaDescBMn<Cfg>, UmmaDesc<Cfg>>::type;
       int it = 0, cc = 0;  // k-blocks and TMEM chunks issued by this CTA
       bool ok = true;
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
@@ -438,11 +549,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               umma_tf32(d_tmem, D::a_lo(st, k), D::b_hi(st, k), idesc, 1u);
           } else {
 #pragma unroll
-            for (int k = 0; k < Cfg::BK / 8; ++k) {  // tf32 UMMA consumes K = 8 (32 B)
-              umma_tf32(d_tmem, D::a_lo(st, k), D::b_hi(st, k), idesc,
+            for (int k = 0; k < Cfg::BK / 8; ++k) {  // tf32 UMMA consumes K = 8
+              umma_tf32(d_tmem, D::a_lo(st, k), DB::b_hi(st, k), idesc,
                         (chunk_start && k == 0) ? 0u : 1u);
-              umma_tf32(d_tmem, D::a_hi(st, k), D::b_lo(st, k), idesc, 1u);
-              umma_tf32(d_tmem, D::a_hi(st, k), D::b_hi(st, k), idesc, 1u);
+              umma_tf32(d_tmem, D::a_hi(st, k), DB::b_lo(st, k), idesc, 1u);
+              umma_tf32(d_tmem, D::a_hi(st, k), DB::b_hi(st, k), idesc, 1u);
             }
           }
           umma_commit(&empty[s]);  // stage s may be refilled once these MMAs finish
@@ -873,6 +984,41 @@ static int make_tmap(CUtensorMap* map, const float* base, int64_t cols, int64_t 
   return r == CUDA_SUCCESS ? kOk : kErrDriver;
 }
 
+// Tensor map of a row-major [rows = K, cols = N] operand read MN-major, N a
+// multiple of 32: viewed as 3-D {32 columns, K rows, N/32 column blocks} so
+// that one box {32, bk, 8} brings a whole 256-column B tile, stored
+// block-major ([8][bk][32]), in the 128-byte swizzle with 32-byte atomicity
+// (the only MN-major layout the tensor core takes for 32-bit operands).
+// Column blocks past N/32 read as zero.
+static int make_tmap_mn(CUtensorMap* map, const float* base, int64_t cols, int64_t rows,
+                        int64_t pitch, int bk) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return kErrDriver;
+  if (cols % 32) return kErrInvalidArg;
+  cuuint64_t dims[3] = {32, (cuuint64_t)rows, (cuuint64_t)(cols / 32)};
+  cuuint64_t strides[2] = {(cuuint64_t)pitch * 4, 128};
+  cuuint32_t box[3] = {32, (cuuint32_t)bk, kBN / 32};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? kOk : kErrDriver;
+}
+
+// The B operand of one GEMM: K-major split W^T (hi, lo with pitch Kp), or
+// MN-major raw W (hi, pitch ldw) with its row-major lo part (pitch ld_lo).
+struct BOp {
+  const float* hi;
+  const float* lo;
+  int64_t ld_hi, ld_lo;
+  bool mn;
+};
+static BOp bop_k(const float* whiT, const float* wloT, int64_t K) {
+  const int64_t Kp = (K + 3) & ~int64_t(3);
+  return BOp{whiT, wloT, Kp, Kp, false};
+}
+
 int64_t dense_f32_workspace_bytes(int64_t M, int64_t N, int64_t K) {
   const int64_t Kp = (K + 3) & ~int64_t(3);
   // hi + lo of X (M x Kp) and of W^T (N x Kp), each region 256-byte aligned
@@ -921,7 +1067,7 @@ static int ring_variant() {
   return v;
 }
 
-template <class Cfg, bool kFusedA>
+template <class Cfg, bool kFusedA, bool kBMn>
 static int launch_gemm(const CUtensorMap& ta_hi, const CUtensorMap& ta_lo,
                        const CUtensorMap& tb_hi, const CUtensorMap& tb_lo, int64_t M, int64_t N,
                        int64_t K, const Epilogue& ep, int splits, int* status,
@@ -932,7 +1078,7 @@ static int launch_gemm(const CUtensorMap& ta_hi, const CUtensorMap& ta_lo,
   if (cudaGetDevice(&dev) != cudaSuccess) return kErrCuda;
   const uint64_t bit = 1ull << (dev & 63);
   if (!(attr_done.load() & bit)) {
-    if (cudaFuncSetAttribute(gemm_tf32x3_kernel<Cfg, kFusedA>,
+    if (cudaFuncSetAttribute(gemm_tf32x3_kernel<Cfg, kFusedA, kBMn>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Cfg::SmemBytes) != cudaSuccess)
       return kErrCuda;
@@ -958,7 +1104,7 @@ static int launch_gemm(const CUtensorMap& ta_hi, const CUtensorMap& ta_lo,
     return !(e && e[0] == '0');
   }();
   const int grid = persist ? std::min(units, sms[dev & 63]) : units;
-  gemm_tf32x3_kernel<Cfg, kFusedA><<<grid, kThreads, Cfg::SmemBytes, stream>>>(
+  gemm_tf32x3_kernel<Cfg, kFusedA, kBMn><<<grid, kThreads, Cfg::SmemBytes, stream>>>(
       ta_hi, ta_lo, tb_hi, tb_lo, num_kb, kb_per_split, tiles_m, tiles_n, units, ep, status);
   count_launch();
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
@@ -967,19 +1113,29 @@ static int launch_gemm(const CUtensorMap& ta_hi, const CUtensorMap& ta_lo,
 // A operand: hi from `xa` with row pitch ldx (the pre-split xhi with pitch
 // Kp, or raw X), lo from xlo (pitch Kp); fused: lo derived in the kernel.
 template <class Cfg>
-static int run_gemm(const float* xa, const float* xlo, int64_t ldx, bool fused,
-                    const float* whiT, const float* wloT, int64_t M, int64_t N, int64_t K,
-                    const Epilogue& ep, int splits, int* status, cudaStream_t stream) {
+static int run_gemm(const float* xa, const float* xlo, int64_t ldx, bool fused, const BOp& b,
+                    int64_t M, int64_t N, int64_t K, const Epilogue& ep, int splits, int* status,
+                    cudaStream_t stream) {
   const int64_t Kp = (K + 3) & ~int64_t(3);
   CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
   int rc = make_tmap(&ta_hi, xa, K, M, ldx, kBM, Cfg::BK);
   if (rc == kOk) rc = make_tmap(&ta_lo, fused ? xa : xlo, K, M, fused ? ldx : Kp, kBM, Cfg::BK);
-  if (rc == kOk) rc = make_tmap(&tb_hi, whiT, K, N, Kp, kBN, Cfg::BK);
-  if (rc == kOk) rc = make_tmap(&tb_lo, wloT, K, N, Kp, kBN, Cfg::BK);
+  if (b.mn) {
+    if (fused) return kErrInvalidArg;
+    if (rc == kOk) rc = make_tmap_mn(&tb_hi, b.hi, N, K, b.ld_hi, Cfg::BK);
+    if (rc == kOk) rc = make_tmap_mn(&tb_lo, b.lo, N, K, b.ld_lo, Cfg::BK);
+    if (rc != kOk) return rc;
+    return launch_gemm<Cfg, false, true>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, ep, splits, status,
+                                         stream);
+  }
+  if (rc == kOk) rc = make_tmap(&tb_hi, b.hi, K, N, b.ld_hi, kBN, Cfg::BK);
+  if (rc == kOk) rc = make_tmap(&tb_lo, b.lo, K, N, b.ld_lo, kBN, Cfg::BK);
   if (rc != kOk) return rc;
   if (fused)
-    return launch_gemm<Cfg, true>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, ep, splits, status, stream);
-  return launch_gemm<Cfg, false>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, ep, splits, status, stream);
+    return launch_gemm<Cfg, true, false>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, ep, splits, status,
+                                         stream);
+  return launch_gemm<Cfg, false, false>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, ep, splits, status,
+                                        stream);
 }
 
 // B200_GEMM_2SM=1 selects the 2-SM (CTA pair) kernel for the non-fused path.
@@ -1028,16 +1184,16 @@ static int run_gemm_pair(const float* xa, const float* xlo, int64_t ldx, const f
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
-static int dispatch_gemm(const float* xa, const float* xlo, int64_t ldx, bool fused,
-                         const float* whiT, const float* wloT, int64_t M, int64_t N, int64_t K,
-                         const Epilogue& ep, int splits, int* status, cudaStream_t stream) {
-  if (!fused && pair_variant())
-    return run_gemm_pair(xa, xlo, ldx, whiT, wloT, M, N, K, ep, splits, status, stream);
+static bool use_pair(bool fused, const BOp& b) { return !fused && !b.mn && pair_variant(); }
+
+static int dispatch_gemm(const float* xa, const float* xlo, int64_t ldx, bool fused, const BOp& b,
+                         int64_t M, int64_t N, int64_t K, const Epilogue& ep, int splits,
+                         int* status, cudaStream_t stream) {
+  if (use_pair(fused, b))
+    return run_gemm_pair(xa, xlo, ldx, b.hi, b.lo, M, N, K, ep, splits, status, stream);
   if (ring_variant() == 0)
-    return run_gemm<CfgBK32S2>(xa, xlo, ldx, fused, whiT, wloT, M, N, K, ep, splits, status,
-                               stream);
-  return run_gemm<CfgBK16S4>(xa, xlo, ldx, fused, whiT, wloT, M, N, K, ep, splits, status,
-                             stream);
+    return run_gemm<CfgBK32S2>(xa, xlo, ldx, fused, b, M, N, K, ep, splits, status, stream);
+  return run_gemm<CfgBK16S4>(xa, xlo, ldx, fused, b, M, N, K, ep, splits, status, stream);
 }
 
 int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
@@ -1054,8 +1210,8 @@ int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
   ep.alpha = alpha;
   ep.vec_out = ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(Y) & 15) == 0);
   ep.split_stride = 0;
-  return dispatch_gemm(xhi, xlo, (K + 3) & ~int64_t(3), false, whiT, wloT, M, N, K, ep, 1, status,
-                       stream);
+  return dispatch_gemm(xhi, xlo, (K + 3) & ~int64_t(3), false, bop_k(whiT, wloT, K), M, N, K, ep, 1,
+                       status, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -1123,9 +1279,8 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ P, int splits, in
 
 // Shared launcher of the split-K and fused paths: GEMM (+ reduce when split).
 static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool fused,
-                            const float* whiT, const float* wloT, int64_t M, int64_t N, int64_t K,
-                            const float* bias, float* Y, int64_t ldy, int act, float alpha,
-                            int splits, float* partials, int* status, cudaStream_t stream) {
+                            const BOp& bop, int64_t M, int64_t N, int64_t K, const float* bias,
+                            float* Y, int64_t ldy, int act, float alpha, int splits, float* partials, int* status, cudaStream_t stream) {
   Epilogue ep;
   ep.M = M;
   ep.N = N;
@@ -1137,7 +1292,7 @@ static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool
     ep.alpha = alpha;
     ep.vec_out = ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(Y) & 15) == 0);
     ep.split_stride = 0;
-    return dispatch_gemm(xa, xlo, ldx, fused, whiT, wloT, M, N, K, ep, 1, status, stream);
+    return dispatch_gemm(xa, xlo, ldx, fused, bop, M, N, K, ep, 1, status, stream);
   }
   // Partials: [splits][M][ldp] raw sums (no bias, no activation).
   const int64_t ldp = partials_pitch(N);
@@ -1149,13 +1304,13 @@ static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool
   ep.vec_out = (reinterpret_cast<uintptr_t>(partials) & 15) == 0;
   ep.split_stride = M * ldp;
   // The launcher may use fewer splits so that none is empty; recompute it.
-  const int bk = (!fused && pair_variant()) ? PairCfg::BK
+  const int bk = use_pair(fused, bop) ? PairCfg::BK
                  : ring_variant() == 0       ? CfgBK32S2::BK
                                              : CfgBK16S4::BK;
   const int num_kb = (int)((K + bk - 1) / bk);
   const int kbps = (num_kb + splits - 1) / splits;
   const int nsplit = (num_kb + kbps - 1) / kbps;
-  int rc = dispatch_gemm(xa, xlo, ldx, fused, whiT, wloT, M, N, K, ep, splits, status, stream);
+  int rc = dispatch_gemm(xa, xlo, ldx, fused, bop, M, N, K, ep, splits, status, stream);
   if (rc != kOk) return rc;
   const int vec = ((N & 3) == 0) && ((ldy & 3) == 0) &&
                   ((reinterpret_cast<uintptr_t>(Y) & 15) == 0) && ep.vec_out;
@@ -1171,8 +1326,8 @@ int gemm_tf32x3_splitk(const float* xhi, const float* xlo, const float* whiT, co
                        int64_t M, int64_t N, int64_t K, const float* bias, float* Y, int64_t ldy,
                        int act, float alpha, int splits, float* partials, int* status,
                        cudaStream_t stream) {
-  return gemm_with_splits(xhi, xlo, (K + 3) & ~int64_t(3), false, whiT, wloT, M, N, K, bias, Y,
-                          ldy, act, alpha, splits, partials, status, stream);
+  return gemm_with_splits(xhi, xlo, (K + 3) & ~int64_t(3), false, bop_k(whiT, wloT, K), M, N, K,
+                          bias, Y, ldy, act, alpha, splits, partials, status, stream);
 }
 
 int split_xw_f32(const float* X, int64_t ldx, int64_t M, const float* W, int64_t ldw,
@@ -1205,8 +1360,8 @@ int gemm_tf32x3_xraw(const float* X, int64_t ldx, const float* xlo, const float*
                      float* Y, int64_t ldy, int act, float alpha, int splits, float* partials,
                      int* status, cudaStream_t stream) {
   if (!fused_a_ok(X, ldx)) return kErrInvalidArg;
-  return gemm_with_splits(X, xlo, ldx, false, whiT, wloT, M, N, K, bias, Y, ldy, act, alpha,
-                          splits, partials, status, stream);
+  return gemm_with_splits(X, xlo, ldx, false, bop_k(whiT, wloT, K), M, N, K, bias, Y, ldy, act,
+                          alpha, splits, partials, status, stream);
 }
 
 bool fused_a_ok(const float* X, int64_t ldx) {
@@ -1218,8 +1373,52 @@ int gemm_tf32x3_fused(const float* X, int64_t ldx, const float* whiT, const floa
                       int act, float alpha, int splits, float* partials, int* status,
                       cudaStream_t stream) {
   if (!fused_a_ok(X, ldx)) return kErrInvalidArg;
-  return gemm_with_splits(X, nullptr, ldx, true, whiT, wloT, M, N, K, bias, Y, ldy, act, alpha,
-                          splits, partials, status, stream);
+  return gemm_with_splits(X, nullptr, ldx, true, bop_k(whiT, wloT, K), M, N, K, bias, Y, ldy, act,
+                          alpha, splits, partials, status, stream);
+}
+
+// ---------------------------------------------------------------------------
+// MN-major B: the GEMM reads W itself as B_hi and W_lo [K, Np] as B_lo.
+// Selected for M <= 4096 rows: there the transposing W split costs up to
+// ~35% of a call (512-row MLP layers: 115 us of split per 200 us of GEMM),
+// while the MN-major GEMM itself measured ~2-3% slower than the K-major one
+// at M >= 8192 (same-box A/B at 8192^3 and 65536 x 4096 x 4096).
+bool w_mn_ok(const float* W, int64_t ldw, int64_t M, int64_t N) {
+  static const bool enabled = [] {
+    const char* e = getenv("B200_W_MN");
+    return !(e && e[0] == '0');
+  }();
+  return enabled && !pair_variant() && M <= 4096 && (N % 32) == 0 && ((ldw & 3) == 0) &&
+         ((reinterpret_cast<uintptr_t>(W) & 15) == 0);
+}
+
+int64_t w_lo_mn_bytes(int64_t K, int64_t N) { return K * ((N + 3) & ~int64_t(3)) * 4; }
+
+int split_lo_xw_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xhi, float* xlo,
+                    const float* W, int64_t ldw, int64_t N, float* wlo, cudaStream_t stream) {
+  const int64_t Kp = (K + 3) & ~int64_t(3), Np = (N + 3) & ~int64_t(3);
+  const int64_t xq = X ? M * (Kp / 4) : 0, wq = K * (Np / 4);
+  // blocks in proportion to each part's quads, together about 16 per SM
+  const int64_t cap = 148 * 16;
+  const int x_blocks = xq ? (int)std::max<int64_t>(
+                                1, std::min<int64_t>((xq + 255) / 256, cap * xq / (xq + wq) + 1))
+                          : 0;
+  const int w_blocks =
+      (int)std::max<int64_t>(1, std::min<int64_t>((wq + 255) / 256, cap * wq / (xq + wq) + 1));
+  split_lo_xw_kernel<<<(unsigned)(x_blocks + w_blocks), 256, 0, stream>>>(
+      X, ldx, M, K, Kp, x_blocks, xhi, xlo, W, ldw, N, Np, wlo);
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int gemm_tf32x3_wmn(const float* xa, const float* xlo, int64_t ldx, const float* W, int64_t ldw,
+                    const float* wlo, int64_t M, int64_t N, int64_t K, const float* bias,
+                    float* Y, int64_t ldy, int act, float alpha, int splits, float* partials,
+                    int* status, cudaStream_t stream) {
+  if (!fused_a_ok(xa, ldx) || !w_mn_ok(W, ldw, M, N)) return kErrInvalidArg;
+  const BOp b{W, wlo, ldw, (N + 3) & ~int64_t(3), true};
+  return gemm_with_splits(xa, xlo, ldx, false, b, M, N, K, bias, Y, ldy, act, alpha, splits,
+                          partials, status, stream);
 }
 
 }  // namespace b200

@@ -57,6 +57,21 @@ int gemm_tf32x3_xraw(const float* X, int64_t ldx, const float* xlo, const float*
                      float* Y, int64_t ldy, int act, float alpha, int splits, float* partials,
                      int* status, cudaStream_t stream);
 
+// MN-major B operand: the GEMM reads the row-major W itself as B_hi and a
+// row-major lo part W_lo [K, Np] (Np = roundup(N, 4)) as B_lo. w_mn_ok:
+// W rows 16-byte aligned, N % 32 == 0, M <= 4096, the 2-SM kernel not
+// selected and B200_W_MN not 0. split_lo_xw_f32 writes X's lo (and hi when
+// xhi != nullptr; X may be null for W alone) and W_lo in one launch.
+bool w_mn_ok(const float* W, int64_t ldw, int64_t M, int64_t N);
+int64_t w_lo_mn_bytes(int64_t K, int64_t N);
+int split_lo_xw_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xhi, float* xlo,
+                    const float* W, int64_t ldw, int64_t N, float* wlo, cudaStream_t stream);
+// xa: raw X (pitch ldx) or its pre-split hi part (pitch Kp); xlo pitch Kp.
+int gemm_tf32x3_wmn(const float* xa, const float* xlo, int64_t ldx, const float* W, int64_t ldw,
+                    const float* wlo, int64_t M, int64_t N, int64_t K, const float* bias,
+                    float* Y, int64_t ldy, int act, float alpha, int splits, float* partials,
+                    int* status, cudaStream_t stream);
+
 // Fused A split: raw X (pitch ldx, 16-byte aligned rows: fused_a_ok) is
 // split to tf32 hi/lo inside the GEMM; W pre-split as whiT/wloT.
 bool fused_a_ok(const float* X, int64_t ldx);

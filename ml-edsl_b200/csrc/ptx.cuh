@@ -98,6 +98,15 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, ui
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, uint64_t* bar,
+                                            int32_t x, int32_t y, int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
@@ -149,6 +158,24 @@ __device__ __forceinline__ uint64_t umma_desc_k(uint32_t smem_addr) {
   return d;
 }
 
+// Shared-memory descriptor of an MN-major tf32 operand. For 32-bit MN-major
+// operands the only layout is the 128-byte swizzle with 32-byte atomicity
+// (layout type 1): K-rows of 128 bytes (32 elements along M/N), grouped by
+// four, with the 32-byte chunks of a row XOR-ed by the row index mod 4 (what
+// TMA writes with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B). kLBO is the byte
+// stride between 32-element blocks along M/N, kSBO between 4-row groups
+// along K.
+template <uint32_t kLBO, uint32_t kSBO>
+__device__ __forceinline__ uint64_t umma_desc_mn_sw128_32b(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((kLBO >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((kSBO >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+  d |= (uint64_t)1 << 61;  // SWIZZLE_128B_BASE32B
+  return d;
+}
+
 // Instruction descriptor for kind::tf32 with f32 accumulation, both operands
 // K-major, tile M x N.  Fields: [4,6) D format (1=f32), [7,10) A format
 // (2=tf32), [10,13) B format, [15] A major, [16] B major, [17,23) N>>3,
@@ -156,6 +183,11 @@ __device__ __forceinline__ uint64_t umma_desc_k(uint32_t smem_addr) {
 __host__ __device__ constexpr uint32_t idesc_tf32_f32(int M, int N) {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) |
          ((uint32_t)(M >> 4) << 24);
+}
+
+// The same with B MN-major (bit 16), A K-major.
+__host__ __device__ constexpr uint32_t idesc_tf32_f32_bmn(int M, int N) {
+  return idesc_tf32_f32(M, N) | (1u << 16);
 }
 
 // D[tmem] (+)= A[smem] * B[smem]; issued by a single thread.

@@ -427,6 +427,18 @@ int dense_device(DeviceCtx* c, const float* X, int64_t ldx, const float* W, int6
     if (rc == kOk)
       rc = gemm_tf32x3_fused(X, ldx, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha, splits,
                              s.partials, c->status, st);
+  } else if (w_mn_ok(W, ldw, M, N) &&
+             w_lo_mn_bytes(K, N) <= reinterpret_cast<char*>(s.partials) -
+                                        reinterpret_cast<char*>(s.whi)) {
+    // W is read as-is (MN-major B_hi); its row-major lo part goes into the
+    // W split region. X likewise when its rows are 16-byte aligned.
+    const bool xraw = fused_a_ok(X, ldx);
+    float* wlo = s.whi;
+    rc = split_lo_xw_f32(X, ldx, M, K, xraw ? nullptr : s.xhi, s.xlo, W, ldw, N, wlo, st);
+    if (rc == kOk)
+      rc = gemm_tf32x3_wmn(xraw ? X : s.xhi, s.xlo, xraw ? ldx : (K + 3) & ~int64_t(3), W, ldw,
+                           wlo, M, N, K, b, Y, ldy, act, alpha, splits, s.partials, c->status,
+                           st);
   } else if (fused_a_ok(X, ldx)) {  // X is the hi part; only lo is written
     rc = split_xw_f32(X, ldx, M, W, ldw, K, N, nullptr, s.xlo, s.whi, s.wlo, st);
     if (rc == kOk)
@@ -498,7 +510,7 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
   B200_CUDA(c->bias.reserve(std::max<int64_t>(N, 1) * 4), "alloc bias");
   if (K > 0) {
     B200_CUDA(c->w.reserve(K * N * 4), "alloc W");
-    B200_CUDA(c->whi.reserve(N * Kp * 4), "alloc W split");
+    B200_CUDA(c->whi.reserve(std::max(N * Kp * 4, w_lo_mn_bytes(K, N))), "alloc W split");
     B200_CUDA(c->wlo.reserve(N * Kp * 4), "alloc W split");
   }
   const int64_t last_rows = M - (nslab - 1) * slab;
@@ -520,11 +532,17 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
   float* dWhi = static_cast<float*>(c->whi.p);
   float* dWlo = static_cast<float*>(c->wlo.p);
   float* db = b ? static_cast<float*>(c->bias.p) : nullptr;
+  // MN-major B (W read as-is, row-major lo part in dWhi) unless the fused A
+  // split is selected.
+  const bool wmn = K > 0 && !fuse_a(static_cast<float*>(c->x[0].p), K) && w_mn_ok(dW, N, M, N);
   if (b) B200_CUDA(cudaMemcpyAsync(db, b, N * 4, cudaMemcpyHostToDevice, c->s_comp), "H2D b");
   if (K > 0) {
     if ((rc = h2d_rows(c, dW, N * 4, W, ldw * 4, N * 4, K, c->s_comp))) return rc;
     // A single-slab call splits W together with X (one launch) below.
-    if (nslab > 1 || fuse_a(static_cast<float*>(c->x[0].p), K)) {
+    if (nslab > 1 && wmn) {
+      rc = split_lo_xw_f32(nullptr, 0, 0, K, nullptr, nullptr, dW, N, N, dWhi, c->s_comp);
+      if (rc) return fail(rc, "split W launch failed");
+    } else if (!wmn && (nslab > 1 || fuse_a(static_cast<float*>(c->x[0].p), K))) {
       rc = split_w_f32(dW, N, K, N, dWhi, dWlo, c->s_comp);
       if (rc) return fail(rc, "split W launch failed");
     }
@@ -562,6 +580,19 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
       if (fuse_a(dX, K)) {
         rc = gemm_tf32x3_fused(dX, K, dWhi, dWlo, rows, N, K, db, dY, N, act, alpha, splits,
                                part, c->status, c->s_comp);
+      } else if (wmn) {
+        float* xhi = static_cast<float*>(c->xhi[slot].p);
+        float* xlo = static_cast<float*>(c->xlo[slot].p);
+        const bool xraw = fused_a_ok(dX, K);
+        if (nslab == 1)
+          rc = split_lo_xw_f32(dX, K, rows, K, xraw ? nullptr : xhi, xlo, dW, N, N, dWhi,
+                               c->s_comp);
+        else
+          rc = xraw ? split_x_lo_f32(dX, K, rows, K, xlo, c->s_comp)
+                    : split_x_f32(dX, K, rows, K, xhi, xlo, c->s_comp);
+        if (rc == kOk)
+          rc = gemm_tf32x3_wmn(xraw ? dX : xhi, xlo, xraw ? K : Kp, dW, N, dWhi, rows, N, K, db,
+                               dY, N, act, alpha, splits, part, c->status, c->s_comp);
       } else if (fused_a_ok(dX, K)) {
         float* xlo = static_cast<float*>(c->xlo[slot].p);
         rc = nslab == 1 ? split_xw_f32(dX, K, rows, dW, N, K, N, nullptr, xlo, dWhi, dWlo, c->s_comp)

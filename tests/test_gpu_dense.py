@@ -375,3 +375,50 @@ print("ok")
     r = subprocess.run([sys.executable, "-c", script, ROOT, PKG_PARENT, tests_dir], env=env,
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
+
+
+# N % 32 == 0 (the MN-major path's condition) with M and K tails, fewer than
+# 256 columns, unaligned X rows (K odd: X split path) and split-K.
+_WMN_SHAPES = [(512, 512, 4096), (300, 1024, 1001), (1000, 992, 999), (517, 32, 64),
+               (512, 11008, 4096), (129, 288, 16), (77, 4096, 37)]
+
+
+def _wmn_outputs(torch):
+    outs = []
+    for (M, N, K) in _WMN_SHAPES:
+        X, W, b = _inputs(M, N, K, seed=N + K)
+        outs.append(dense_device(torch, X, W, b, act=1))
+    return outs
+
+
+def test_w_mn_major_matches_k_major(cuda, tmp_path):
+    """The default B operand is the raw row-major W read MN-major (plus a
+    row-major lo part); B200_W_MN=0 (child process) selects the transposed
+    K-major split. Same tf32 operands, same MMA order: bit-identical output,
+    across column-block tails, K tails, unaligned X rows (X split path)
+    and split-K."""
+    import os
+    import subprocess
+    import sys
+    import torch
+    from conftest import PKG_PARENT, ROOT
+    out = str(tmp_path / "kmajor.npz")
+    script = r"""
+import sys, numpy as np, torch
+sys.path[:0] = sys.argv[1:4]
+import test_gpu_dense as t
+np.savez(sys.argv[4], *t._wmn_outputs(torch))
+print("ok")
+"""
+    tests_dir = os.path.dirname(os.path.abspath(__file__))
+    env = dict(os.environ, B200_W_MN="0")
+    r = subprocess.run([sys.executable, "-c", script, ROOT, PKG_PARENT, tests_dir, out], env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
+    ref = np.load(out)
+    for i, (got, shape) in enumerate(zip(_wmn_outputs(torch), _WMN_SHAPES)):
+        np.testing.assert_array_equal(got, ref[f"arr_{i}"], err_msg=str(shape))
+    M, N, K = _WMN_SHAPES[1]
+    X, W, b = _inputs(M, N, K, seed=N + K)
+    assert max_err(_wmn_outputs(torch)[1], oracle.dense_f32(X, W, b, act=1)) <= \
+        oracle.f32_bound(K, X, W)
