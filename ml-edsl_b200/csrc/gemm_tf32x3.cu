@@ -44,6 +44,7 @@
 #include <algorithm>
 #include <atomic>
 #include <type_traits>
+#include <utility>
 #include <cstdlib>
 #include <cstring>
 #include <cstdint>
@@ -101,6 +102,8 @@ __device__ __forceinline__ void tf32_split(float x, float& h, float& l) {
 __global__ void split_rows_kernel(const float* __restrict__ X, int64_t ldx, int64_t M, int64_t K,
                                   int64_t Kp, float* __restrict__ hi, float* __restrict__ lo,
                                   int vec_in) {
+  // The GEMM that follows may start its prologue once every CTA is done.
+  const PdlTriggerOnExit pdl_trigger_on_exit;
   const int64_t q_per_row = Kp >> 2;
   const int64_t total = M * q_per_row;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -131,6 +134,8 @@ __global__ void split_rows_kernel(const float* __restrict__ X, int64_t ldx, int6
 // and NaN too), so the products are bit-identical to the full split's.
 __global__ void split_rows_lo_kernel(const float* __restrict__ X, int64_t ldx, int64_t M,
                                      int64_t K, int64_t Kp, float* __restrict__ lo) {
+  // The GEMM that follows may start its prologue once every CTA is done.
+  const PdlTriggerOnExit pdl_trigger_on_exit;
   const int64_t q_per_row = Kp >> 2;
   const int64_t total = M * q_per_row;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -159,6 +164,8 @@ __global__ void split_rows_lo_kernel(const float* __restrict__ X, int64_t ldx, i
 __global__ void split_transpose_kernel(const float* __restrict__ W, int64_t ldw, int64_t K,
                                        int64_t N, int64_t Kp, float* __restrict__ hiT,
                                        float* __restrict__ loT) {
+  // The GEMM that follows may start its prologue once every CTA is done.
+  const PdlTriggerOnExit pdl_trigger_on_exit;
   __shared__ float th[32][33];
   __shared__ float tl[32][33];
   const int64_t n0 = (int64_t)blockIdx.x * 32;
@@ -192,6 +199,8 @@ __global__ void __launch_bounds__(256)
                     float* __restrict__ xhi, float* __restrict__ xlo,
                     const float* __restrict__ W, int64_t ldw, int64_t K, int64_t N, int64_t Kp,
                     int tiles_n, float* __restrict__ whiT, float* __restrict__ wloT) {
+  // The GEMM that follows may start its prologue once every CTA is done.
+  const PdlTriggerOnExit pdl_trigger_on_exit;
   if ((int)blockIdx.x < x_blocks) {
     const int64_t q_per_row = Kp >> 2;
     const int64_t total = M * q_per_row;
@@ -283,6 +292,8 @@ __global__ void __launch_bounds__(256)
                        int64_t Kp, int x_blocks, float* __restrict__ xhi,
                        float* __restrict__ xlo, const float* __restrict__ W, int64_t ldw,
                        int64_t N, int64_t Np, float* __restrict__ wlo) {
+  // The GEMM that follows may start its prologue once every CTA is done.
+  const PdlTriggerOnExit pdl_trigger_on_exit;
   if ((int)blockIdx.x < x_blocks)
     split_quads(X, ldx, M, K, Kp, xhi, xlo, blockIdx.x * 256ll + threadIdx.x,
                 (int64_t)x_blocks * 256);
@@ -432,6 +443,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Launched as a programmatic dependent of the split pass: everything above
+  // overlaps its tail; operands are read only after it has completed.
+  pdl_wait();
 
   // Ring stages and TMEM chunk buffers are counted across all units of the
   // CTA, so their mbarrier phases run on from one tile to the next.
@@ -676,6 +690,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  pdl_trigger();  // a following split-K reduction may launch (it waits for completion)
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -1067,6 +1082,35 @@ static int ring_variant() {
   return v;
 }
 
+// Programmatic dependent launch (see pdl_wait) for problems of at most 2^33
+// multiply-adds (2048^3): there the launch and prologue latency it hides is
+// 10-20% of a call (dense 1024^3: 31.0 -> 26.9 us; 256^3: 22.7 -> 18.6 us);
+// for long GEMMs it gained nothing measurable. B200_PDL=0 turns it off.
+static bool pdl_enabled(int64_t M, int64_t N, int64_t K) {
+  static const bool on = [] {
+    const char* e = getenv("B200_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on && (double)M * (double)N * (double)K <= 8589934592.0;
+}
+
+template <class... KArgs, class... Args>
+static cudaError_t launch_dependent(bool pdl, void (*kernel)(KArgs...), unsigned grid,
+                                    unsigned block, size_t smem, cudaStream_t stream,
+                                    Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 template <class Cfg, bool kFusedA, bool kBMn>
 static int launch_gemm(const CUtensorMap& ta_hi, const CUtensorMap& ta_lo,
                        const CUtensorMap& tb_hi, const CUtensorMap& tb_lo, int64_t M, int64_t N,
@@ -1104,10 +1148,12 @@ static int launch_gemm(const CUtensorMap& ta_hi, const CUtensorMap& ta_lo,
     return !(e && e[0] == '0');
   }();
   const int grid = persist ? std::min(units, sms[dev & 63]) : units;
-  gemm_tf32x3_kernel<Cfg, kFusedA, kBMn><<<grid, kThreads, Cfg::SmemBytes, stream>>>(
-      ta_hi, ta_lo, tb_hi, tb_lo, num_kb, kb_per_split, tiles_m, tiles_n, units, ep, status);
+  const cudaError_t e =
+      launch_dependent(pdl_enabled(M, N, K), gemm_tf32x3_kernel<Cfg, kFusedA, kBMn>,
+                       (unsigned)grid, kThreads, Cfg::SmemBytes, stream, ta_hi, ta_lo, tb_hi,
+                       tb_lo, num_kb, kb_per_split, tiles_m, tiles_n, units, ep, status);
   count_launch();
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return e == cudaSuccess ? kOk : kErrCuda;
 }
 
 // A operand: hi from `xa` with row pitch ldx (the pre-split xhi with pitch
@@ -1245,6 +1291,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ P, int splits, in
                                      int64_t ldp, int64_t M, int64_t N,
                                      const float* __restrict__ bias, int act, float alpha,
                                      float* __restrict__ Y, int64_t ldy, int vec) {
+  pdl_wait();  // launched as a programmatic dependent of the GEMM
   if (vec) {  // N % 4 == 0, Y 16-byte aligned, ldy % 4 == 0
     const int64_t q = N >> 2, total = M * q;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -1316,10 +1363,12 @@ static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool
                   ((reinterpret_cast<uintptr_t>(Y) & 15) == 0) && ep.vec_out;
   const int64_t work = vec ? M * N / 4 : M * N;
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, 148 * 16));
-  splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(partials, nsplit, M * ldp, ldp, M, N, bias,
-                                                   act, alpha, Y, ldy, vec);
+  const cudaError_t e =
+      launch_dependent(pdl_enabled(M, N, K), splitk_reduce_kernel, (unsigned)blocks, 256, 0,
+                       stream, static_cast<const float*>(partials), nsplit, M * ldp, ldp, M, N,
+                       bias, act, alpha, Y, ldy, vec);
   count_launch();
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return e == cudaSuccess ? kOk : kErrCuda;
 }
 
 int gemm_tf32x3_splitk(const float* xhi, const float* xlo, const float* whiT, const float* wloT,

@@ -107,6 +107,20 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, ui
       : "memory");
 }
 
+// Programmatic dependent launch. A kernel launched with the programmatic
+// stream-serialization attribute may begin once every CTA of its predecessor
+// in the stream has executed pdl_trigger() or exited; pdl_wait() then blocks
+// until the predecessor has completed and its memory writes are visible (it
+// returns at once when there is no such predecessor).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// Triggers when the CTA's thread leaves the kernel, whatever the exit path.
+struct PdlTriggerOnExit {
+  __device__ ~PdlTriggerOnExit() { pdl_trigger(); }
+};
+
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }

@@ -422,3 +422,42 @@ print("ok")
     X, W, b = _inputs(M, N, K, seed=N + K)
     assert max_err(_wmn_outputs(torch)[1], oracle.dense_f32(X, W, b, act=1)) <= \
         oracle.f32_bound(K, X, W)
+
+
+def test_back_to_back_small_layers_match_synchronised(cuda):
+    """Small layers run with programmatic dependent launch (the GEMM's
+    prologue overlaps the split pass, the split-K reduction overlaps the GEMM's
+    teardown). A chain of dependent layers issued back to back must equal,
+    bit for bit, the same chain with a device synchronisation after each
+    layer, and stay within the f32 bound of the oracle's chain."""
+    import torch
+    dev = torch.device("cuda:0")
+    L = _native.lib()
+    s = stream_ptr(torch)
+    rng = np.random.default_rng(77)
+    shapes = [(256, 256, 256), (256, 512, 256), (256, 256, 512), (256, 1024, 256),
+              (256, 256, 1024)] * 2 + [(256, 288, 256), (256, 256, 288)]
+    Ws = [(rng.uniform(-1, 1, (K, N)) / np.sqrt(K)).astype(np.float32) for (_, N, K) in shapes]
+    bs = [rng.uniform(-0.1, 0.1, (N,)).astype(np.float32) for (_, N, _) in shapes]
+    X0 = rng.uniform(-1, 1, (256, 256)).astype(np.float32)
+    tW = [torch.from_numpy(w).to(dev) for w in Ws]
+    tb = [torch.from_numpy(b).to(dev) for b in bs]
+
+    def chain(sync):
+        h = torch.from_numpy(X0).to(dev)
+        for (M, N, K), w, b in zip(shapes, tW, tb):
+            y = torch.empty((M, N), device=dev)
+            _native.check(L.b200_dense_f32(ptr(h), K, ptr(w), N, ptr(b), ptr(y), N, M, N, K, 1,
+                                           0.0, s))
+            if sync:
+                _native.check(L.b200_stream_sync(s))
+            h = y
+        _native.check(L.b200_stream_sync(s))
+        return h.cpu().numpy()
+
+    a, b = chain(False), chain(True)
+    np.testing.assert_array_equal(a, b)
+    h = X0
+    for w, bb in zip(Ws, bs):
+        h = oracle.dense_f32(h, w, bb, act=1)
+    assert max_err(a, h) <= 1e-4 * len(shapes)
