@@ -1,0 +1,492 @@
+// i32 GEMM on the tensor cores, exact modulo 2^32.
+//
+// Reference semantics: linalg.fill(0) + linalg.matmul on i32 tensors lower to
+// arith.muli / arith.addi, which wrap modulo 2^32
+// (cpp/src/builders/LinalgBuilder.cpp:106-139; tested exactly at
+// tests/linalg/test_matmul_execution.py:93-103); the dense form adds an i32
+// bias with arith.addi (cpp/src/builders/LinalgBuilder.cpp:301-339).
+//
+// Byte-sliced products. Each i32 is read as its 32-bit two's-complement
+// pattern u = sum_p u_p 256^p with unsigned bytes u_p (p = 0..3). Then
+//   (A B)[m][n] mod 2^32 = sum_{s=0..3} 256^s S_s[m][n] mod 2^32,
+//   S_s = sum_{i+j=s} sum_k A_i[m][k] B_j[k][n],
+// because every byte product with i + j >= 4 is a multiple of 2^32. The ten
+// products A_i B_j (i + j <= 3) run as tcgen05.mma.kind::i8 (u8 x u8 -> s32)
+// into four TMEM accumulators, one per shift s; the epilogue forms
+// sum_s S_s << 8s with wrapping 32-bit adds and adds the bias the same way.
+// An accumulator sums at most 4 * Kr * 255^2 with Kr <= 8192 (the K range of
+// one work unit; longer K is split and the partial sums added modulo 2^32), which
+// is below 2^31: the s32 accumulators never overflow.
+//
+// Layout: A's bytes as four planes [4][M][Kp] and B's as four transposed
+// planes [4][N][Kp] (K-major, Kp = roundup(K, 16), pad bytes zero), written by
+// one HBM pass. Per stage the producer loads all four planes of a 128 x 64-byte
+// A tile and of a 128 x 64-byte B tile with one 3-D TMA each (64-byte swizzle).
+// Roles as in the f32 kernel: warp 0 TMA, warp 1 TMEM allocation + MMA issue,
+// warps 2-9 epilogue; persistent over (tile, K-split) units.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <algorithm>
+#include <atomic>
+#include <cstdint>
+#include <cstdlib>
+#include "ptx.cuh"
+#include "kernels.h"
+
+namespace b200 {
+
+namespace {
+
+constexpr int kQBM = 128, kQBN = 128;  // output tile
+constexpr int kQBK = 64;               // K bytes per stage: 64-byte rows, 64-byte swizzle
+constexpr int kQStages = 3;
+constexpr int kQPlaneA = kQBM * kQBK;  // 8 KB
+constexpr int kQPlaneB = kQBN * kQBK;  // 8 KB
+constexpr int kQStageBytes = 4 * kQPlaneA + 4 * kQPlaneB;  // 64 KB
+constexpr int kQBarOffset = kQStages * kQStageBytes;
+constexpr int kQSmemBytes = kQBarOffset + 256 + 1024;  // barriers + alignment slack
+constexpr int kQEpiWarps = 8;
+constexpr int kQThreads = 64 + 32 * kQEpiWarps;
+constexpr int kQTmemCols = 4 * kQBN;  // one 128 x 128 s32 accumulator per shift
+constexpr int kQMaxKr = 8192;         // K per unit: 4 * 8192 * 255^2 < 2^31
+constexpr int kQGroupM = 16;
+static_assert(kQSmemBytes <= 232448, "shared memory over the sm_100 limit");
+
+struct QEpilogue {
+  int32_t* C;
+  int64_t ldc;
+  const int32_t* bias;  // may be null
+  int64_t M, N;
+  int vec_out;           // C 16-byte aligned and ldc % 4 == 0
+  int64_t split_stride;  // split-K: split s writes raw sums at C + s * split_stride
+};
+
+// K-major operand tile with 64-byte rows (64 bytes of K), 8-row groups 512 B
+// apart; k-step kk (32 bytes of K) starts 32 * kk bytes into the row.
+__device__ __forceinline__ uint64_t qdesc(uint32_t addr) { return umma_desc_k<4, 512>(addr); }
+
+}  // namespace
+
+__global__ void __launch_bounds__(kQThreads, 1)
+    gemm_i32_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+                       const __grid_constant__ CUtensorMap tmB, int num_kb_total,
+                       int kb_per_split, int tiles_m, int tiles_n, int num_units, QEpilogue ep,
+                       int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kQBarOffset);  // TMA -> MMA
+  uint64_t* empty = full + kQStages;                                  // MMA -> TMA
+  uint64_t* tfull = empty + kQStages;  // MMA -> epilogue: accumulators complete
+  uint64_t* tempty = tfull + 1;        // epilogue -> MMA: accumulators read out
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tiles = tiles_m * tiles_n;
+
+  struct Unit {
+    int m0, n0, kb0, nkb, split;
+  };
+  auto unit_of = [&](int u) {
+    Unit w;
+    const int tile = u % tiles;
+    w.split = u / tiles;
+    const int tiles_per_group = kQGroupM * tiles_n;
+    const int group = tile / tiles_per_group;
+    const int first_m = group * kQGroupM;
+    const int group_rows = min(tiles_m - first_m, kQGroupM);
+    const int in_group = tile - group * tiles_per_group;
+    w.m0 = (first_m + in_group % group_rows) * kQBM;
+    w.n0 = (in_group / group_rows) * kQBN;
+    w.kb0 = w.split * kb_per_split;
+    w.nkb = min(num_kb_total - w.kb0, kb_per_split);
+    return w;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kQStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(tempty, kQEpiWarps);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kQTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int it = 0;
+      for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
+        const Unit w = unit_of(u);
+        bool ok = true;
+        for (int kb = 0; kb < w.nkb; ++kb, ++it) {
+          const int s = it % kQStages;
+          const int round = it / kQStages;
+          if (round > 0 &&
+              !mbar_wait(&empty[s], (round - 1) & 1, status, kDevTimeoutEmpty, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * kQStageBytes;
+          const int kx = (w.kb0 + kb) * kQBK;
+          mbar_arrive_expect_tx(&full[s], kQStageBytes);
+          tma_load_3d(st, &tmA, &full[s], kx, w.m0, 0);                 // 4 planes of A
+          tma_load_3d(st + 4 * kQPlaneA, &tmB, &full[s], kx, w.n0, 0);  // 4 planes of B^T
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_u8_s32(kQBM, kQBN);
+      int it = 0, tu = 0;  // k-blocks and units issued by this CTA
+      bool ok = true;
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const Unit w = unit_of(u);
+        if (tu > 0) {  // the previous unit's accumulators must have been read out
+          if (!mbar_wait(tempty, (tu - 1) & 1, status, kDevTimeoutAccum, abort_flag)) break;
+          tc_fence_after();
+        }
+        for (int kb = 0; kb < w.nkb; ++kb, ++it) {
+          const int s = it % kQStages;
+          if (!mbar_wait(&full[s], (it / kQStages) & 1, status, kDevTimeoutFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = smem_u32(smem + s * kQStageBytes);
+#pragma unroll
+          for (int kk = 0; kk < kQBK / 32; ++kk) {
+#pragma unroll
+            for (int sh = 0; sh < 4; ++sh) {
+#pragma unroll
+              for (int i = 0; i <= sh; ++i) {
+                const int j = sh - i;
+                const uint32_t first = (kb == 0 && kk == 0 && i == 0) ? 0u : 1u;
+                umma_i8(tmem_base + sh * kQBN, qdesc(st + i * kQPlaneA + kk * 32),
+                        qdesc(st + 4 * kQPlaneA + j * kQPlaneB + kk * 32), idesc, first);
+              }
+            }
+          }
+          umma_commit(&empty[s]);  // stage s may be refilled once these MMAs finish
+        }
+        if (!ok) break;
+        umma_commit(tfull);
+        ++tu;
+      }
+    }
+  } else {
+    // ------------------------------------------------ epilogue (8 warps)
+    // Warp w reads TMEM lane quarter w % 4 and column half (w - 2) / 4.
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    int tu = 0;
+#pragma unroll 1
+    for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
+      const Unit w = unit_of(u);
+      if (!mbar_wait(tfull, tu & 1, status, kDevTimeoutAccum, abort_flag)) break;
+      tc_fence_after();
+      uint32_t acc[64];
+#pragma unroll
+      for (int j = 0; j < 64; ++j) acc[j] = 0u;
+#pragma unroll
+      for (int sh = 0; sh < 4; ++sh) {
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + lane_off + sh * kQBN + half * 64 + g * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[g * 32 + j] += r[j] << (8 * sh);  // mod 2^32
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty);  // the next unit's MMAs may start
+      ++tu;
+      const int64_t row = (int64_t)w.m0 + quarter * 32 + lane;
+      const int64_t col0 = (int64_t)w.n0 + half * 64;
+      if (row < ep.M) {
+        int32_t* dst = ep.C + w.split * ep.split_stride + row * ep.ldc + col0;
+#pragma unroll
+        for (int j = 0; j < 64; j += 4) {
+          uint32_t v[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int64_t c = col0 + j + q;
+            v[q] = acc[j + q] +
+                   ((ep.bias != nullptr && c < ep.N) ? (uint32_t)__ldg(ep.bias + c) : 0u);
+          }
+          if (ep.vec_out && col0 + j + 4 <= ep.N) {
+            *reinterpret_cast<int4*>(dst + j) =
+                make_int4((int)v[0], (int)v[1], (int)v[2], (int)v[3]);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              if (col0 + j + q < ep.N) dst[j + q] = (int32_t)v[q];
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kQTmemCols);
+  }
+}
+
+// One HBM pass: A [M, K] -> byte planes Ap [4][M][Kp]; B [K, N] -> transposed
+// byte planes Bp [4][N][Kp]; pad bytes (k >= K) zero. Blocks [0, a_blocks)
+// take A (4 consecutive k per thread, grid-stride); the others take one
+// 64 (k) x 32 (n) tile of B each. 256 threads.
+__global__ void __launch_bounds__(256)
+    i32_planes_kernel(const int32_t* __restrict__ A, int64_t lda, int64_t M,
+                      const int32_t* __restrict__ B, int64_t ldb, int64_t N, int64_t K,
+                      int64_t Kp, int a_blocks, int tiles_n, uint8_t* __restrict__ Ap,
+                      uint8_t* __restrict__ Bp) {
+  if ((int)blockIdx.x < a_blocks) {
+    const int64_t q_per_row = Kp >> 2;
+    const int64_t total = M * q_per_row;
+    const int vec = ((lda & 3) == 0) && ((reinterpret_cast<uintptr_t>(A) & 15) == 0);
+    for (int64_t i = blockIdx.x * 256ll + threadIdx.x; i < total; i += (int64_t)a_blocks * 256) {
+      const int64_t m = i / q_per_row;
+      const int64_t k = (i - m * q_per_row) << 2;
+      uint32_t v[4];
+      if (vec && k + 4 <= K) {
+        const int4 t = __ldg(reinterpret_cast<const int4*>(A + m * lda + k));
+        v[0] = (uint32_t)t.x; v[1] = (uint32_t)t.y; v[2] = (uint32_t)t.z; v[3] = (uint32_t)t.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = (k + j < K) ? (uint32_t)__ldg(A + m * lda + k + j) : 0u;
+      }
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const uint32_t packed = ((v[0] >> (8 * p)) & 0xFFu) | (((v[1] >> (8 * p)) & 0xFFu) << 8) |
+                                (((v[2] >> (8 * p)) & 0xFFu) << 16) |
+                                (((v[3] >> (8 * p)) & 0xFFu) << 24);
+        *reinterpret_cast<uint32_t*>(Ap + (p * M + m) * Kp + k) = packed;
+      }
+    }
+    return;
+  }
+  // B tile: k in [k0, k0 + 64), n in [n0, n0 + 32).
+  __shared__ __align__(16) uint8_t t[4][32][80];  // [plane][n][k], 16-byte padded rows
+  const int b = blockIdx.x - a_blocks;
+  const int64_t n0 = (int64_t)(b % tiles_n) * 32;
+  const int64_t k0 = (int64_t)(b / tiles_n) * 64;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int kk = ty + 8 * j;
+    const int64_t k = k0 + kk, n = n0 + tx;
+    const uint32_t v = (k < K && n < N) ? (uint32_t)__ldg(B + k * ldb + n) : 0u;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) t[p][tx][kk] = (uint8_t)(v >> (8 * p));
+  }
+  __syncthreads();
+  // 4 planes x 32 rows x 4 chunks of 16 bytes = 512 chunks, 2 per thread.
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int c = threadIdx.x + 256 * r;
+    const int p = c >> 7, n = (c >> 2) & 31, q = c & 3;
+    const int64_t k = k0 + q * 16;
+    if (n0 + n < N && k < Kp)
+      *reinterpret_cast<uint4*>(Bp + (p * N + n0 + n) * Kp + k) =
+          *reinterpret_cast<const uint4*>(&t[p][n][q * 16]);
+  }
+}
+
+// C = sum_s P_s (+ bias), all modulo 2^32, in a fixed order.
+__global__ void splitk_reduce_i32_kernel(const int32_t* __restrict__ P, int splits,
+                                         int64_t stride, int64_t ldp, int64_t M, int64_t N,
+                                         const int32_t* __restrict__ bias,
+                                         int32_t* __restrict__ C, int64_t ldc) {
+  const int64_t total = M * N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / N, n = i - m * N;
+    uint32_t acc = 0;
+    for (int s = 0; s < splits; ++s) acc += (uint32_t)P[s * stride + m * ldp + n];
+    if (bias) acc += (uint32_t)bias[n];
+    C[m * ldc + n] = (int32_t)acc;
+  }
+}
+
+namespace {
+
+typedef CUresult (*EncodeTiledFnQ)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFnQ encode_fn() {
+  static EncodeTiledFnQ fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFnQ>(p);
+  }
+  return fn;
+}
+
+// Byte planes [4][rows][Kp] as a 3-D u8 tensor {Kp, rows, 4}; box {64, 128, 4}.
+int make_plane_map(CUtensorMap* map, const uint8_t* base, int64_t rows, int64_t Kp) {
+  EncodeTiledFnQ enc = encode_fn();
+  if (!enc) return kErrDriver;
+  cuuint64_t dims[3] = {(cuuint64_t)Kp, (cuuint64_t)rows, 4};
+  cuuint64_t strides[2] = {(cuuint64_t)Kp, (cuuint64_t)(rows * Kp)};
+  cuuint32_t box[3] = {kQBK, 128, 4};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? kOk : kErrDriver;
+}
+
+int64_t al256(int64_t b) { return (b + 255) & ~int64_t(255); }
+int64_t kp_of(int64_t K) { return (K + 15) & ~int64_t(15); }
+
+}  // namespace
+
+// Split-K count: at least ceil(K / 8192) (accumulator range), then a wave
+// model like the f32 one: ten 128 x 128 x 32 int8 MMAs (64 clocks each at the
+// dense int8 rate) per 32 bytes of K, plus the partial-sum traffic.
+int choose_splits_i32(int64_t M, int64_t N, int64_t K) {
+  const int64_t tiles = ((M + kQBM - 1) / kQBM) * ((N + kQBN - 1) / kQBN);
+  const int64_t kb = (K + kQBK - 1) / kQBK;
+  const int s_min = (int)((K + kQMaxKr - 1) / kQMaxKr);
+  const double t_full = (double)((K + 31) / 32) * 10 * 64 / 1.5e9;  // s per CTA, whole K
+  double best_t = 1e30;
+  int best = std::max(1, s_min);
+  for (int s = std::max(1, s_min); s <= std::max(8, s_min); ++s) {
+    if (kb / s < 1) break;
+    const int64_t waves = (tiles * s + 147) / 148;
+    double t = waves * t_full / s;
+    if (s > 1) t += (double)(s + 1) * M * N * 4 / 6.0e12;
+    if (t < best_t * 0.97) {
+      best_t = t;
+      best = s;
+    }
+  }
+  return best;
+}
+
+int64_t gemm_i32_tc_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const int64_t Kp = kp_of(K);
+  const int s = choose_splits_i32(M, N, K);
+  const int64_t part = s > 1 ? al256((int64_t)s * M * ((N + 3) & ~int64_t(3)) * 4) : 0;
+  return al256(4 * M * Kp) + al256(4 * N * Kp) + part;
+}
+
+bool i32_tensor_core_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("B200_I32_TC");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+int gemm_i32_tc(const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb,
+                const int32_t* bias, int32_t* C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                void* ws, int* status, cudaStream_t stream) {
+  if (M <= 0 || N <= 0) return kOk;
+  if (K <= 0) return kErrInvalidArg;  // the caller fills bias / zeros for K == 0
+  static std::atomic<uint64_t> attr_done{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return kErrCuda;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(attr_done.load() & bit)) {
+    if (cudaFuncSetAttribute(gemm_i32_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kQSmemBytes) != cudaSuccess)
+      return kErrCuda;
+    attr_done.fetch_or(bit);
+  }
+  static int sms[64] = {0};
+  if (sms[dev & 63] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return kErrCuda;
+    sms[dev & 63] = n;
+  }
+  const int64_t Kp = kp_of(K);
+  uint8_t* Ap = static_cast<uint8_t*>(ws);
+  uint8_t* Bp = Ap + al256(4 * M * Kp);
+  int32_t* part = reinterpret_cast<int32_t*>(Bp + al256(4 * N * Kp));
+
+  // byte planes
+  const int64_t aq = M * (Kp / 4);
+  const int a_blocks = (int)std::max<int64_t>(1, std::min<int64_t>((aq + 255) / 256, 148 * 8));
+  const int tiles_n32 = (int)((N + 31) / 32);
+  const int64_t b_blocks = (int64_t)tiles_n32 * ((Kp + 63) / 64);
+  i32_planes_kernel<<<(unsigned)(a_blocks + b_blocks), 256, 0, stream>>>(
+      A, lda, M, B, ldb, N, K, Kp, a_blocks, tiles_n32, Ap, Bp);
+  count_launch();
+  if (cudaGetLastError() != cudaSuccess) return kErrCuda;
+
+  CUtensorMap ta, tb;
+  int rc = make_plane_map(&ta, Ap, M, Kp);
+  if (rc == kOk) rc = make_plane_map(&tb, Bp, N, Kp);
+  if (rc != kOk) return rc;
+
+  const int splits = choose_splits_i32(M, N, K);
+  const int tiles_m = (int)((M + kQBM - 1) / kQBM);
+  const int tiles_n = (int)((N + kQBN - 1) / kQBN);
+  const int num_kb = (int)((K + kQBK - 1) / kQBK);
+  const int kbps = (num_kb + splits - 1) / splits;
+  const int nsplit = (num_kb + kbps - 1) / kbps;
+  const int units = tiles_m * tiles_n * nsplit;
+  const int64_t ldp = (N + 3) & ~int64_t(3);
+  QEpilogue ep;
+  ep.M = M;
+  ep.N = N;
+  if (nsplit > 1) {
+    ep.C = part;
+    ep.ldc = ldp;
+    ep.bias = nullptr;
+    ep.vec_out = 1;  // 256-byte aligned base, ldp % 4 == 0
+    ep.split_stride = M * ldp;
+  } else {
+    ep.C = C;
+    ep.ldc = ldc;
+    ep.bias = bias;
+    ep.vec_out = ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
+    ep.split_stride = 0;
+  }
+  const int grid = std::min(units, sms[dev & 63]);
+  gemm_i32_tc_kernel<<<grid, kQThreads, kQSmemBytes, stream>>>(ta, tb, num_kb, kbps, tiles_m,
+                                                                tiles_n, units, ep, status);
+  count_launch();
+  if (cudaGetLastError() != cudaSuccess) return kErrCuda;
+  if (nsplit > 1) {
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((M * N + 255) / 256, 148 * 16));
+    splitk_reduce_i32_kernel<<<blocks, 256, 0, stream>>>(part, nsplit, M * ldp, ldp, M, N, bias,
+                                                        C, ldc);
+    count_launch();
+    if (cudaGetLastError() != cudaSuccess) return kErrCuda;
+  }
+  return kOk;
+}
+
+}  // namespace b200

@@ -92,6 +92,17 @@ int gemm_i32(const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb, int32
              int64_t ldc, int64_t M, int64_t N, int64_t K, const int32_t* bias,
              cudaStream_t stream);
 
+// ---- i32 GEMM on the tensor cores (gemm_i32_tc.cu): byte-sliced
+// tcgen05.mma.kind::i8 products, exact modulo 2^32. ws: at least
+// gemm_i32_tc_workspace_bytes(M, N, K) bytes, 256-byte aligned. K > 0.
+// B200_I32_TC=0 selects the CUDA-core kernel (i32_tensor_core_enabled).
+bool i32_tensor_core_enabled();
+int choose_splits_i32(int64_t M, int64_t N, int64_t K);
+int64_t gemm_i32_tc_workspace_bytes(int64_t M, int64_t N, int64_t K);
+int gemm_i32_tc(const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb,
+                const int32_t* bias, int32_t* C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                void* ws, int* status, cudaStream_t stream);
+
 // ---- elementwise (elementwise.cu)
 int bias_act_f32(const float* X, int64_t ldx, const float* b, float* Y, int64_t ldy, int64_t M,
                  int64_t N, int act, float alpha, cudaStream_t stream);

@@ -215,6 +215,23 @@ __device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint6
       : "memory");
 }
 
+// Instruction descriptor for kind::i8 with unsigned 8-bit A and B (format
+// 0), s32 accumulation (D format 2), both operands K-major, tile M x N.
+__host__ __device__ constexpr uint32_t idesc_u8_s32(int M, int N) {
+  return (2u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] * B[smem] on 8-bit integers (K = 32 per instruction).
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on `bar` once every previously issued tcgen05.mma of this thread
 // has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {

@@ -681,6 +681,17 @@ int run_sharded(int ndev, int64_t M, Fn fn) {
   return kOk;
 }
 
+// C = A B (+ bias) mod 2^32 on the current device: the tensor-core kernel
+// (byte-sliced int8 MMAs; ws >= gemm_i32_tc_workspace_bytes) unless K == 0
+// or B200_I32_TC=0, then the CUDA-core kernel.
+int matmul_i32_device(DeviceCtx* c, const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb,
+                      const int32_t* bias, int32_t* C, int64_t ldc, int64_t M, int64_t N,
+                      int64_t K, void* ws, cudaStream_t st) {
+  if (K > 0 && ws && i32_tensor_core_enabled())
+    return gemm_i32_tc(A, lda, B, ldb, bias, C, ldc, M, N, K, ws, c->status, st);
+  return gemm_i32(A, lda, B, ldb, C, ldc, M, N, K, bias, st);
+}
+
 int simple_host_i32_matmul(int dev, const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb,
                            const int32_t* bias, int32_t* C, int64_t ldc, int64_t M, int64_t N,
                            int64_t K) {
@@ -694,6 +705,8 @@ int simple_host_i32_matmul(int dev, const int32_t* A, int64_t lda, const int32_t
   B200_CUDA(c->w.reserve(std::max<int64_t>(K * N, 1) * 4), "alloc B");
   B200_CUDA(c->y[0].reserve(M * N * 4), "alloc C");
   B200_CUDA(c->bias.reserve(std::max<int64_t>(N, 1) * 4), "alloc bias");
+  const int64_t ws_bytes = gemm_i32_tc_workspace_bytes(M, N, K);
+  if (ws_bytes) B200_CUDA(c->xhi[0].reserve(ws_bytes), "alloc i32 workspace");
   int32_t* dA = static_cast<int32_t*>(c->x[0].p);
   int32_t* dB = static_cast<int32_t*>(c->w.p);
   int32_t* dC = static_cast<int32_t*>(c->y[0].p);
@@ -704,7 +717,8 @@ int simple_host_i32_matmul(int dev, const int32_t* A, int64_t lda, const int32_t
     if ((rc = h2d_rows(c, dB, N * 4, B, ldb * 4, N * 4, K, s))) return rc;
   }
   if (bias) B200_CUDA(cudaMemcpyAsync(db, bias, N * 4, cudaMemcpyHostToDevice, s), "H2D bias");
-  rc = gemm_i32(dA, K, dB, N, dC, N, M, N, K, db, s);
+  rc = matmul_i32_device(c, dA, K, dB, N, db, dC, N, M, N, K, ws_bytes ? c->xhi[0].p : nullptr,
+                         s);
   if (rc) return fail(rc, "i32 matmul launch failed");
   if ((rc = d2h_rows(c, C, ldc * 4, dC, N * 4, N * 4, M, s))) return rc;
   return kOk;
@@ -904,7 +918,22 @@ int b200_matmul_i32(const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb
   int rc = validate_dense(A, lda, B, ldb, C, ldc, M, N, K, kActNone);
   if (rc) return rc;
   if (M == 0 || N == 0) return succeed();
-  rc = gemm_i32(A, lda, B, ldb, C, ldc, M, N, K, bias, static_cast<cudaStream_t>(stream));
+  DeviceCtx* c = nullptr;
+  if ((rc = current_ctx(&c))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* ws = nullptr;
+  const size_t need = (size_t)gemm_i32_tc_workspace_bytes(M, N, K);
+  if (need && i32_tensor_core_enabled()) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    DevBuf& buf = c->scratch[st];
+    if (buf.n < need) {
+      // The old buffer may still be read by queued work on this stream.
+      B200_CUDA(cudaStreamSynchronize(st), "sync before scratch growth");
+      B200_CUDA(buf.reserve(need), "alloc scratch");
+    }
+    ws = buf.p;
+  }
+  rc = matmul_i32_device(c, A, lda, B, ldb, bias, C, ldc, M, N, K, ws, st);
   return rc ? fail(rc, "i32 matmul launch failed") : succeed();
 }
 

@@ -1,4 +1,5 @@
-"""GPU parity of the i32 CUDA-core GEMM (bit-exact) and elementwise kernels."""
+"""GPU parity of the i32 GEMM (tensor-core byte-sliced path, bit-exact modulo
+2^32) and the elementwise kernels."""
 import ctypes
 
 import numpy as np
@@ -49,6 +50,54 @@ def test_i32_2048_config(cuda):
     g = oracle.gen_config_inputs("matmul_i32_2048")
     np.testing.assert_array_equal(_i32_device(torch, g["A"], g["B"]),
                                   oracle.matmul_i32(g["A"], g["B"]))
+
+
+def _full_range(rng, shape):
+    return rng.integers(-2**31, 2**31, shape, dtype=np.int64).astype(np.int32)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (200, 136, 130), (513, 260, 1031),
+                                   (64, 64, 9000), (3, 700, 20000)])
+def test_i32_full_range_tails_and_split(cuda, M, N, K):
+    """Every bit pattern of A and B (the byte planes carry all four bytes),
+    M / N tails of the 128 x 128 tile, K tails of the 64-byte stage, and
+    K > 8192, which the tensor-core path splits so that no s32 accumulator
+    can overflow (partial sums added modulo 2^32)."""
+    import torch
+    rng = np.random.default_rng(M * 7 + N * 3 + K)
+    A, B, bias = _full_range(rng, (M, K)), _full_range(rng, (K, N)), _full_range(rng, (N,))
+    np.testing.assert_array_equal(_i32_device(torch, A, B, bias), oracle.matmul_i32(A, B, bias))
+
+
+def test_i32_strided_operands(cuda):
+    """Row pitches larger than the rows (lda, ldb, ldc not multiples of 4)."""
+    import torch
+    dev = torch.device("cuda:0")
+    rng = np.random.default_rng(5)
+    M, N, K, lda, ldb, ldc = 150, 90, 77, 81, 93, 95
+    Abuf, Bbuf = _full_range(rng, (M, lda)), _full_range(rng, (K, ldb))
+    tA, tB = torch.from_numpy(Abuf).to(dev), torch.from_numpy(Bbuf).to(dev)
+    tC = torch.full((M, ldc), 7, dtype=torch.int32, device=dev)
+    L = _native.lib()
+    _native.check(L.b200_matmul_i32(ptr(tA), lda, ptr(tB), ldb, None, ptr(tC), ldc, M, N, K,
+                                    stream_ptr(torch)))
+    _native.check(L.b200_stream_sync(stream_ptr(torch)))
+    C = tC.cpu().numpy()
+    np.testing.assert_array_equal(C[:, :N], oracle.matmul_i32(Abuf[:, :K], Bbuf[:, :N]))
+    assert (C[:, N:] == 7).all()
+
+
+def test_i32_host_entry_point(cuda):
+    """b200_matmul_i32_host: host buffers, device workspace held by the runtime."""
+    rng = np.random.default_rng(9)
+    A, B, bias = _full_range(rng, (300, 200)), _full_range(rng, (200, 260)), _full_range(rng, (260,))
+    C = np.zeros((300, 260), np.int32)
+    L = _native.lib()
+    c = ctypes.c_void_p
+    _native.check(L.b200_matmul_i32_host(c(A.ctypes.data), 200, c(B.ctypes.data), 260,
+                                         c(bias.ctypes.data), c(C.ctypes.data), 260, 300, 260,
+                                         200, 1))
+    np.testing.assert_array_equal(C, oracle.matmul_i32(A, B, bias))
 
 
 def test_i32_identity_known_answer(cuda):
