@@ -124,6 +124,9 @@ __global__ void __launch_bounds__(kQThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Launched as a programmatic dependent of the planes pass: the prologue
+  // above overlaps its tail; the planes are read only after it has completed.
+  pdl_wait();
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer
@@ -255,13 +258,17 @@ __global__ void __launch_bounds__(kQThreads, 1)
 
 // One HBM pass: A [M, K] -> byte planes Ap [4][M][Kp]; B [K, N] -> transposed
 // byte planes Bp [4][N][Kp]; pad bytes (k >= K) zero. Blocks [0, a_blocks)
-// take A (4 consecutive k per thread, grid-stride); the others take one
-// 64 (k) x 32 (n) tile of B each. 256 threads.
+// take A (4 consecutive k per thread, grid-stride). The others take B in
+// 32 (k) x 32 (n) tiles, one per warp: lane n reads its column's 32 values
+// (each a coalesced 128-byte warp load), packs them by byte in registers and
+// writes 32 bytes (two 16-byte stores) to each plane's row n. 256 threads.
 __global__ void __launch_bounds__(256)
     i32_planes_kernel(const int32_t* __restrict__ A, int64_t lda, int64_t M,
                       const int32_t* __restrict__ B, int64_t ldb, int64_t N, int64_t K,
-                      int64_t Kp, int a_blocks, int tiles_n, uint8_t* __restrict__ Ap,
-                      uint8_t* __restrict__ Bp) {
+                      int64_t Kp, int a_blocks, int tiles_n, int64_t b_tiles,
+                      uint8_t* __restrict__ Ap, uint8_t* __restrict__ Bp) {
+  // The GEMM that follows may start its prologue once every CTA is done.
+  const PdlTriggerOnExit pdl_trigger_on_exit;
   if ((int)blockIdx.x < a_blocks) {
     const int64_t q_per_row = Kp >> 2;
     const int64_t total = M * q_per_row;
@@ -287,30 +294,31 @@ __global__ void __launch_bounds__(256)
     }
     return;
   }
-  // B tile: k in [k0, k0 + 64), n in [n0, n0 + 32).
-  __shared__ __align__(16) uint8_t t[4][32][80];  // [plane][n][k], 16-byte padded rows
-  const int b = blockIdx.x - a_blocks;
-  const int64_t n0 = (int64_t)(b % tiles_n) * 32;
-  const int64_t k0 = (int64_t)(b / tiles_n) * 64;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t tile = (int64_t)(blockIdx.x - a_blocks) * 8 + (threadIdx.x >> 5);
+  if (tile >= b_tiles) return;
+  const int64_t n = (tile % tiles_n) * 32 + (threadIdx.x & 31);
+  const int64_t k0 = (tile / tiles_n) * 32;
+  if (n >= N) return;
+  uint32_t w[4][8];  // [plane][4-byte word of the 32 k]
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int kk = ty + 8 * j;
-    const int64_t k = k0 + kk, n = n0 + tx;
-    const uint32_t v = (k < K && n < N) ? (uint32_t)__ldg(B + k * ldb + n) : 0u;
+  for (int g = 0; g < 8; ++g) {
+    uint32_t v[4];
 #pragma unroll
-    for (int p = 0; p < 4; ++p) t[p][tx][kk] = (uint8_t)(v >> (8 * p));
+    for (int j = 0; j < 4; ++j) {
+      const int64_t k = k0 + 4 * g + j;
+      v[j] = k < K ? (uint32_t)__ldg(B + k * ldb + n) : 0u;
+    }
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+      w[p][g] = ((v[0] >> (8 * p)) & 0xFFu) | (((v[1] >> (8 * p)) & 0xFFu) << 8) |
+                (((v[2] >> (8 * p)) & 0xFFu) << 16) | (((v[3] >> (8 * p)) & 0xFFu) << 24);
   }
-  __syncthreads();
-  // 4 planes x 32 rows x 4 chunks of 16 bytes = 512 chunks, 2 per thread.
 #pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const int c = threadIdx.x + 256 * r;
-    const int p = c >> 7, n = (c >> 2) & 31, q = c & 3;
-    const int64_t k = k0 + q * 16;
-    if (n0 + n < N && k < Kp)
-      *reinterpret_cast<uint4*>(Bp + (p * N + n0 + n) * Kp + k) =
-          *reinterpret_cast<const uint4*>(&t[p][n][q * 16]);
+  for (int p = 0; p < 4; ++p) {
+    uint8_t* row = Bp + (p * N + n) * Kp + k0;
+    *reinterpret_cast<uint4*>(row) = make_uint4(w[p][0], w[p][1], w[p][2], w[p][3]);
+    if (k0 + 16 < Kp)  // Kp is a multiple of 16: the second half is in or out whole
+      *reinterpret_cast<uint4*>(row + 16) = make_uint4(w[p][4], w[p][5], w[p][6], w[p][7]);
   }
 }
 
@@ -439,9 +447,10 @@ int gemm_i32_tc(const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb,
   const int64_t aq = M * (Kp / 4);
   const int a_blocks = (int)std::max<int64_t>(1, std::min<int64_t>((aq + 255) / 256, 148 * 8));
   const int tiles_n32 = (int)((N + 31) / 32);
-  const int64_t b_blocks = (int64_t)tiles_n32 * ((Kp + 63) / 64);
+  const int64_t b_tiles = (int64_t)tiles_n32 * ((Kp + 31) / 32);
+  const int64_t b_blocks = (b_tiles + 7) / 8;
   i32_planes_kernel<<<(unsigned)(a_blocks + b_blocks), 256, 0, stream>>>(
-      A, lda, M, B, ldb, N, K, Kp, a_blocks, tiles_n32, Ap, Bp);
+      A, lda, M, B, ldb, N, K, Kp, a_blocks, tiles_n32, b_tiles, Ap, Bp);
   count_launch();
   if (cudaGetLastError() != cudaSuccess) return kErrCuda;
 
@@ -475,10 +484,20 @@ int gemm_i32_tc(const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb,
     ep.split_stride = 0;
   }
   const int grid = std::min(units, sms[dev & 63]);
-  gemm_i32_tc_kernel<<<grid, kQThreads, kQSmemBytes, stream>>>(ta, tb, num_kb, kbps, tiles_m,
-                                                                tiles_n, units, ep, status);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kQThreads);
+  cfg.dynamicSmemBytes = kQSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_i32_tc_kernel, ta, tb, num_kb, kbps,
+                                           tiles_m, tiles_n, units, ep, status);
   count_launch();
-  if (cudaGetLastError() != cudaSuccess) return kErrCuda;
+  if (e != cudaSuccess) return kErrCuda;
   if (nsplit > 1) {
     const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((M * N + 255) / 256, 148 * 16));
     splitk_reduce_i32_kernel<<<blocks, 256, 0, stream>>>(part, nsplit, M * ldp, ldp, M, N, bias,
