@@ -525,7 +525,7 @@ def run_configs(args):
     emit("mlp_2layer", timed(lambda: (dense(X, W1, b1, H, 1), dense(H, W2, b2, Y, 1))),
          flops=2.0 * 512 * 4096 * 11008 * 2)
     del X, W1, b1, W2, b2, H, Y
-    # i32 2048^3 on the CUDA cores
+    # i32 2048^3 (byte-sliced int8 tensor-core path) and 8192^3 beside it
     g.manual_seed(2)
     A = torch.randint(-8, 9, (2048, 2048), generator=g, device=dev, dtype=torch.int32)
     B = torch.randint(-8, 9, (2048, 2048), generator=g, device=dev, dtype=torch.int32)
@@ -533,7 +533,27 @@ def run_configs(args):
     ms = timed(lambda: _native.check(L.b200_matmul_i32(P(A), 2048, P(B), 2048, None, P(C), 2048,
                                                       2048, 2048, 2048, sp)))
     line = {"config": "matmul_i32_2048", "ms": ms, "Tint-op/s": 2.0 * 2048 ** 3 / ms / 1e9}
-    # roofline: measured INT32 multiply-add issue rate (lib/libb200probe.so)
+    # Roofline of the tensor-core path: one i32 multiply-add is ten u8 x u8
+    # multiply-adds, and the dense int8 rate is twice the bf16 rate (nominal
+    # 4.5 vs 2.25 PFLOP/s), so the peak in i32 int-op/s (2 per multiply-add)
+    # is 2 x measured bf16 FLOP/s / 10.
+    i32_peak = 2.0 * bf16 / 10.0
+    line.update({"tensor_peak_Tint-op/s": i32_peak, "frac_of_tensor_peak":
+                 line["Tint-op/s"] / i32_peak,
+                 "peak_source": "measured cuBLAS bf16 burst x 2 (int8 rate) / 10 (u8 products "
+                                "per i32 product)"})
+    Ab = torch.randint(-2**31, 2**31 - 1, (8192, 8192), generator=g, device=dev,
+                       dtype=torch.int32)
+    Bb = torch.randint(-2**31, 2**31 - 1, (8192, 8192), generator=g, device=dev,
+                       dtype=torch.int32)
+    Cb = torch.empty_like(Ab)
+    ms8 = timed(lambda: _native.check(L.b200_matmul_i32(P(Ab), 8192, P(Bb), 8192, None, P(Cb),
+                                                       8192, 8192, 8192, 8192, sp)))
+    line["i32_8192_full_range_Tint-op/s"] = 2.0 * 8192 ** 3 / ms8 / 1e9
+    line["i32_8192_frac_of_tensor_peak"] = line["i32_8192_full_range_Tint-op/s"] / i32_peak
+    del Ab, Bb, Cb
+    # the CUDA-core alternative's ceiling: measured INT32 multiply-add issue
+    # rate (lib/libb200probe.so)
     probe = ctypes.CDLL(os.path.join(ROOT, "ml-edsl_b200", "lib", "libb200probe.so"))
     probe.b200_probe_imad.restype = ctypes.c_float
     probe.b200_probe_imad.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
