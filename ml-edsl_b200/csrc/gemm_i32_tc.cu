@@ -31,6 +31,7 @@
 #include <cstdint>
 #include <cstdlib>
 #include "ptx.cuh"
+#include "sched.cuh"
 #include "kernels.h"
 
 namespace b200 {
@@ -57,8 +58,8 @@ struct QEpilogue {
   int64_t ldc;
   const int32_t* bias;  // may be null
   int64_t M, N;
-  int vec_out;           // C 16-byte aligned and ldc % 4 == 0
-  int64_t split_stride;  // split-K: split s writes raw sums at C + s * split_stride
+  int vec_out;   // C 16-byte aligned and ldc % 4 == 0
+  int32_t* part; // cut tiles: raw partial sums, tile-local [piece][r][128][128]
 };
 
 // K-major operand tile with 64-byte rows (64 bytes of K), 8-row groups 512 B
@@ -69,8 +70,7 @@ __device__ __forceinline__ uint64_t qdesc(uint32_t addr) { return umma_desc_k<4,
 
 __global__ void __launch_bounds__(kQThreads, 1)
     gemm_i32_tc_kernel(const __grid_constant__ CUtensorMap tmA,
-                       const __grid_constant__ CUtensorMap tmB, int num_kb_total,
-                       int kb_per_split, int tiles_m, int tiles_n, int num_units, QEpilogue ep,
+                       const __grid_constant__ CUtensorMap tmB, Sched sc, QEpilogue ep,
                        int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -84,26 +84,8 @@ __global__ void __launch_bounds__(kQThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tiles = tiles_m * tiles_n;
-
-  struct Unit {
-    int m0, n0, kb0, nkb, split;
-  };
-  auto unit_of = [&](int u) {
-    Unit w;
-    const int tile = u % tiles;
-    w.split = u / tiles;
-    const int tiles_per_group = kQGroupM * tiles_n;
-    const int group = tile / tiles_per_group;
-    const int first_m = group * kQGroupM;
-    const int group_rows = min(tiles_m - first_m, kQGroupM);
-    const int in_group = tile - group * tiles_per_group;
-    w.m0 = (first_m + in_group % group_rows) * kQBM;
-    w.n0 = (in_group / group_rows) * kQBN;
-    w.kb0 = w.split * kb_per_split;
-    w.nkb = min(num_kb_total - w.kb0, kb_per_split);
-    return w;
-  };
+  // Work units (whole tiles, then pieces of cut tiles) of the schedule `sc`.
+  auto unit_of = [&](int u) { return unit_at(sc, u, kQBM, kQBN); };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kQStages; ++s) {
@@ -132,7 +114,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
       int it = 0;
-      for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
+      for (int u = blockIdx.x; u < sc.units && !*abort_flag; u += gridDim.x) {
         const Unit w = unit_of(u);
         bool ok = true;
         for (int kb = 0; kb < w.nkb; ++kb, ++it) {
@@ -158,7 +140,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
       constexpr uint32_t idesc = idesc_u8_s32(kQBM, kQBN);
       int it = 0, tu = 0;  // k-blocks and units issued by this CTA
       bool ok = true;
-      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+      for (int u = blockIdx.x; u < sc.units && ok; u += gridDim.x) {
         const Unit w = unit_of(u);
         if (tu > 0) {  // the previous unit's accumulators must have been read out
           if (!mbar_wait(tempty, (tu - 1) & 1, status, kDevTimeoutAccum, abort_flag)) break;
@@ -200,7 +182,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     int tu = 0;
 #pragma unroll 1
-    for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
+    for (int u = blockIdx.x; u < sc.units && !*abort_flag; u += gridDim.x) {
       const Unit w = unit_of(u);
       if (!mbar_wait(tfull, tu & 1, status, kDevTimeoutAccum, abort_flag)) break;
       tc_fence_after();
@@ -222,10 +204,19 @@ __global__ void __launch_bounds__(kQThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty);  // the next unit's MMAs may start
       ++tu;
-      const int64_t row = (int64_t)w.m0 + quarter * 32 + lane;
-      const int64_t col0 = (int64_t)w.n0 + half * 64;
+      const int lr = quarter * 32 + lane, lc0 = half * 64;
+      if (w.piece >= 0) {  // raw sums of a piece, tile-local, whole rows
+        int32_t* dst = ep.part + ((int64_t)(w.piece * sc.rest + w.r) * kQBM + lr) * kQBN + lc0;
+#pragma unroll
+        for (int j = 0; j < 64; j += 4)
+          *reinterpret_cast<int4*>(dst + j) =
+              make_int4((int)acc[j], (int)acc[j + 1], (int)acc[j + 2], (int)acc[j + 3]);
+        continue;
+      }
+      const int64_t row = (int64_t)w.m0 + lr;
+      const int64_t col0 = (int64_t)w.n0 + lc0;
       if (row < ep.M) {
-        int32_t* dst = ep.C + w.split * ep.split_stride + row * ep.ldc + col0;
+        int32_t* dst = ep.C + row * ep.ldc + col0;
 #pragma unroll
         for (int j = 0; j < 64; j += 4) {
           uint32_t v[4];
@@ -322,19 +313,27 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// C = sum_s P_s (+ bias), all modulo 2^32, in a fixed order.
-__global__ void splitk_reduce_i32_kernel(const int32_t* __restrict__ P, int splits,
-                                         int64_t stride, int64_t ldp, int64_t M, int64_t N,
-                                         const int32_t* __restrict__ bias,
-                                         int32_t* __restrict__ C, int64_t ldc) {
-  const int64_t total = M * N;
+// Cut tiles: C = sum over pieces of part[piece][r] (+ bias), modulo 2^32.
+__global__ void __launch_bounds__(256)
+    piece_reduce_i32_kernel(const int32_t* __restrict__ part, Sched sc, int64_t M, int64_t N,
+                            const int32_t* __restrict__ bias, int32_t* __restrict__ C,
+                            int64_t ldc) {
+  const int64_t tile_elems = (int64_t)kQBM * kQBN;
+  const int64_t total = (int64_t)sc.rest * tile_elems;
+  const int64_t piece_stride = (int64_t)sc.rest * tile_elems;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t m = i / N, n = i - m * N;
+    const int r = (int)(i / tile_elems);
+    const int64_t e = i - r * tile_elems;
+    const int lr = (int)(e / kQBN), lc = (int)(e - (int64_t)lr * kQBN);
+    int mt, nt;
+    tile_coords(sc, sc.whole + r, mt, nt);
+    const int64_t row = (int64_t)mt * kQBM + lr, col = (int64_t)nt * kQBN + lc;
+    if (row >= M || col >= N) continue;
     uint32_t acc = 0;
-    for (int s = 0; s < splits; ++s) acc += (uint32_t)P[s * stride + m * ldp + n];
-    if (bias) acc += (uint32_t)bias[n];
-    C[m * ldc + n] = (int32_t)acc;
+    for (int p = 0; p < sc.pieces; ++p) acc += (uint32_t)part[p * piece_stride + i];
+    if (bias) acc += (uint32_t)bias[col];
+    C[row * ldc + col] = (int32_t)acc;
   }
 }
 
@@ -375,36 +374,39 @@ int make_plane_map(CUtensorMap* map, const uint8_t* base, int64_t rows, int64_t 
 int64_t al256(int64_t b) { return (b + 255) & ~int64_t(255); }
 int64_t kp_of(int64_t K) { return (K + 15) & ~int64_t(15); }
 
+int sm_count_i32() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 148;  // host-side queries without a device
+  }
+  return n;
+}
+
+// Schedule (sched.cuh): 128 x 128 tiles; one tile over all of K costs ten
+// 128 x 128 x 32 int8 MMAs (64 clocks each at the dense int8 rate) per 32
+// bytes of K; no unit spans more than 8192 bytes of K (kQMaxKr), so a longer
+// K cuts every tile.
+Sched sched_i32(int64_t M, int64_t N, int64_t K) {
+  const double t_tile = (double)((K + 31) / 32) * 10 * 64 / 1.5e9;
+  return make_sched(M, N, K, kQBM, kQBN, kQBK, sm_count_i32(), t_tile, 4, kQMaxKr / kQBK, 16,
+                    1, kQGroupM);
+}
+
 }  // namespace
 
-// Split-K count: at least ceil(K / 8192) (accumulator range), then a wave
-// model like the f32 one: ten 128 x 128 x 32 int8 MMAs (64 clocks each at the
-// dense int8 rate) per 32 bytes of K, plus the partial-sum traffic.
 int choose_splits_i32(int64_t M, int64_t N, int64_t K) {
-  const int64_t tiles = ((M + kQBM - 1) / kQBM) * ((N + kQBN - 1) / kQBN);
-  const int64_t kb = (K + kQBK - 1) / kQBK;
-  const int s_min = (int)((K + kQMaxKr - 1) / kQMaxKr);
-  const double t_full = (double)((K + 31) / 32) * 10 * 64 / 1.5e9;  // s per CTA, whole K
-  double best_t = 1e30;
-  int best = std::max(1, s_min);
-  for (int s = std::max(1, s_min); s <= std::max(8, s_min); ++s) {
-    if (kb / s < 1) break;
-    const int64_t waves = (tiles * s + 147) / 148;
-    double t = waves * t_full / s;
-    if (s > 1) t += (double)(s + 1) * M * N * 4 / 6.0e12;
-    if (t < best_t * 0.97) {
-      best_t = t;
-      best = s;
-    }
-  }
-  return best;
+  if (M <= 0 || N <= 0 || K <= 0) return 1;
+  const Sched sc = sched_i32(M, N, K);
+  return sc.rest > 0 ? sc.pieces : 1;
 }
 
 int64_t gemm_i32_tc_workspace_bytes(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const int64_t Kp = kp_of(K);
-  const int s = choose_splits_i32(M, N, K);
-  const int64_t part = s > 1 ? al256((int64_t)s * M * ((N + 3) & ~int64_t(3)) * 4) : 0;
+  const Sched sc = sched_i32(M, N, K);
+  const int64_t part = sc.rest > 0 ? al256((int64_t)sc.pieces * sc.rest * kQBM * kQBN * 4) : 0;
   return al256(4 * M * Kp) + al256(4 * N * Kp) + part;
 }
 
@@ -459,31 +461,17 @@ int gemm_i32_tc(const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb,
   if (rc == kOk) rc = make_plane_map(&tb, Bp, N, Kp);
   if (rc != kOk) return rc;
 
-  const int splits = choose_splits_i32(M, N, K);
-  const int tiles_m = (int)((M + kQBM - 1) / kQBM);
-  const int tiles_n = (int)((N + kQBN - 1) / kQBN);
-  const int num_kb = (int)((K + kQBK - 1) / kQBK);
-  const int kbps = (num_kb + splits - 1) / splits;
-  const int nsplit = (num_kb + kbps - 1) / kbps;
-  const int units = tiles_m * tiles_n * nsplit;
-  const int64_t ldp = (N + 3) & ~int64_t(3);
+  const Sched sc = sched_i32(M, N, K);
+  const int units = sc.units;
   QEpilogue ep;
   ep.M = M;
   ep.N = N;
-  if (nsplit > 1) {
-    ep.C = part;
-    ep.ldc = ldp;
-    ep.bias = nullptr;
-    ep.vec_out = 1;  // 256-byte aligned base, ldp % 4 == 0
-    ep.split_stride = M * ldp;
-  } else {
-    ep.C = C;
-    ep.ldc = ldc;
-    ep.bias = bias;
-    ep.vec_out = ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
-    ep.split_stride = 0;
-  }
-  const int grid = std::min(units, sms[dev & 63]);
+  ep.C = C;
+  ep.ldc = ldc;
+  ep.bias = bias;
+  ep.vec_out = ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
+  ep.part = part;
+  const int grid = std::min(units, sms[dev & 63]);  // persistent
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kQThreads);
@@ -494,14 +482,13 @@ int gemm_i32_tc(const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_i32_tc_kernel, ta, tb, num_kb, kbps,
-                                           tiles_m, tiles_n, units, ep, status);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_i32_tc_kernel, ta, tb, sc, ep, status);
   count_launch();
   if (e != cudaSuccess) return kErrCuda;
-  if (nsplit > 1) {
-    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((M * N + 255) / 256, 148 * 16));
-    splitk_reduce_i32_kernel<<<blocks, 256, 0, stream>>>(part, nsplit, M * ldp, ldp, M, N, bias,
-                                                        C, ldc);
+  if (sc.rest > 0) {
+    const int64_t elems = (int64_t)sc.rest * kQBM * kQBN;
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((elems + 255) / 256, 148 * 16));
+    piece_reduce_i32_kernel<<<blocks, 256, 0, stream>>>(part, sc, M, N, bias, C, ldc);
     count_launch();
     if (cudaGetLastError() != cudaSuccess) return kErrCuda;
   }

@@ -49,6 +49,7 @@
 #include <cstring>
 #include <cstdint>
 #include "ptx.cuh"
+#include "sched.cuh"
 #include "kernels.h"
 
 namespace b200 {
@@ -325,8 +326,47 @@ struct Epilogue {
   int act;
   float alpha;
   int vec_out;  // Y base 16-byte aligned and ldy % 4 == 0
-  int64_t split_stride;  // split-K: split s writes its partial at Y + s * split_stride
+  float* part;  // cut tiles: raw partial sums, tile-local [piece][r][BM][kBN]
 };
+
+// Stores one epilogue thread's 128 consecutive accumulator columns of a unit:
+// tile-local row `lr`, columns [lc0, lc0 + 128). A whole tile's row gets bias,
+// activation and the M / N bounds and goes to Y; a piece's raw sums go to its
+// tile-local partial buffer (whole rows, 16-byte stores).
+template <int kTileM>
+__device__ __forceinline__ void store_tile_row(const Epilogue& ep, const Unit& w, int rest,
+                                               int lr, int lc0, const float (&acc)[128]) {
+  if (w.piece >= 0) {
+    float* dst = ep.part + ((int64_t)(w.piece * rest + w.r) * kTileM + lr) * kBN + lc0;
+#pragma unroll
+    for (int j = 0; j < 128; j += 4)
+      *reinterpret_cast<float4*>(dst + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+    return;
+  }
+  const int64_t row = (int64_t)w.m0 + lr;
+  const int64_t col0 = (int64_t)w.n0 + lc0;
+  if (row >= ep.M) return;
+  float* dst = ep.Y + row * ep.ldy + col0;
+#pragma unroll
+  for (int j = 0; j < 128; j += 4) {
+    float bb[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      bb[q] = (ep.bias != nullptr && col0 + j + q < ep.N) ? __ldg(ep.bias + col0 + j + q) : 0.0f;
+    const float v0 = apply_act(acc[j] + bb[0], ep.act, ep.alpha);
+    const float v1 = apply_act(acc[j + 1] + bb[1], ep.act, ep.alpha);
+    const float v2 = apply_act(acc[j + 2] + bb[2], ep.act, ep.alpha);
+    const float v3 = apply_act(acc[j + 3] + bb[3], ep.act, ep.alpha);
+    if (ep.vec_out && col0 + j + 4 <= ep.N) {
+      *reinterpret_cast<float4*>(dst + j) = make_float4(v0, v1, v2, v3);
+    } else {
+      if (col0 + j < ep.N) dst[j] = v0;
+      if (col0 + j + 1 < ep.N) dst[j + 1] = v1;
+      if (col0 + j + 2 < ep.N) dst[j + 2] = v2;
+      if (col0 + j + 3 < ep.N) dst[j + 3] = v3;
+    }
+  }
+}
 
 // UMMA shared-memory descriptors of the four operand tiles of stage base `st`
 // at k-step k (8 tf32 = 32 bytes along the row).
@@ -380,8 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAhi,
                        const __grid_constant__ CUtensorMap tmAlo,
                        const __grid_constant__ CUtensorMap tmBhi,
-                       const __grid_constant__ CUtensorMap tmBlo, int num_kb_total,
-                       int kb_per_split, int tiles_m, int tiles_n, int num_units, Epilogue ep,
+                       const __grid_constant__ CUtensorMap tmBlo, Sched sc, Epilogue ep,
                        int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -396,28 +435,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tiles = tiles_m * tiles_n;
-
-  // Work unit u = split * tiles + tile; tiles in a grouped raster so that
-  // CTAs running at the same time share A rows and B columns in L2.
-  struct Unit {
-    int m0, n0, kb0, nkb, split;
-  };
-  auto unit_of = [&](int u) {
-    Unit w;
-    const int tile = u % tiles;
-    w.split = u / tiles;
-    const int tiles_per_group = kGroupM * tiles_n;
-    const int group = tile / tiles_per_group;
-    const int first_m = group * kGroupM;
-    const int group_rows = min(tiles_m - first_m, kGroupM);
-    const int in_group = tile - group * tiles_per_group;
-    w.m0 = (first_m + in_group % group_rows) * kBM;
-    w.n0 = (in_group / group_rows) * kBN;
-    w.kb0 = w.split * kb_per_split;
-    w.nkb = min(num_kb_total - w.kb0, kb_per_split);
-    return w;
-  };
+  // Work units (whole tiles, then pieces of cut tiles) of the schedule `sc`.
+  auto unit_of = [&](int u) { return unit_at(sc, u, kBM, kBN); };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < Cfg::Stages; ++s) {
@@ -455,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Lane 0 waits for the stage and posts the byte count; the decision is
     // broadcast so that the whole warp leaves the loop together.
     int it = 0;
-    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+    for (int u = blockIdx.x; u < sc.units; u += gridDim.x) {
       int go = lane == 0 ? !*abort_flag : 0;
       if (!__shfl_sync(0xffffffffu, go, 0)) break;
       const Unit w = unit_of(u);
@@ -492,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
       int it = 0;
-      for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
+      for (int u = blockIdx.x; u < sc.units && !*abort_flag; u += gridDim.x) {
         const Unit w = unit_of(u);
         for (int kb = 0; kb < w.nkb; ++kb, ++it) {
           const int s = it % Cfg::Stages;
@@ -523,7 +542,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       using DB = typename std::conditional<kBMn, UmmaDescBMn<Cfg>, UmmaDesc<Cfg>>::type;
       int it = 0, cc = 0;  // k-blocks and TMEM chunks issued by this CTA
       bool ok = true;
-      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+      for (int u = blockIdx.x; u < sc.units && ok; u += gridDim.x) {
         const Unit w = unit_of(u);
         for (int kb = 0; kb < w.nkb; ++kb, ++it) {
           const int s = it % Cfg::Stages;
@@ -610,7 +629,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       return true;
     };
 #pragma unroll 1
-    for (int u = blockIdx.x; u < num_units && ok && !*abort_flag; u += gridDim.x) {
+    for (int u = blockIdx.x; u < sc.units && ok && !*abort_flag; u += gridDim.x) {
       const Unit w = unit_of(u);
       const int num_chunks = (w.nkb + Cfg::ChunkKB - 1) / Cfg::ChunkKB;
 #pragma unroll
@@ -662,31 +681,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok || *abort_flag) break;
       // The MMAs of the next unit proceed into the two TMEM buffers while
       // this tile is stored.
-      const int64_t row = (int64_t)w.m0 + quarter * 32 + lane;
-      const int64_t col0 = (int64_t)w.n0 + half * 128;
-      if (row < ep.M) {
-        float* dst = ep.Y + w.split * ep.split_stride + row * ep.ldy + col0;
-#pragma unroll
-        for (int j = 0; j < 128; j += 4) {
-          float bb[4];
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            bb[q] = (ep.bias != nullptr && col0 + j + q < ep.N) ? __ldg(ep.bias + col0 + j + q)
-                                                                : 0.0f;
-          const float v0 = apply_act(acc[j] + bb[0], ep.act, ep.alpha);
-          const float v1 = apply_act(acc[j + 1] + bb[1], ep.act, ep.alpha);
-          const float v2 = apply_act(acc[j + 2] + bb[2], ep.act, ep.alpha);
-          const float v3 = apply_act(acc[j + 3] + bb[3], ep.act, ep.alpha);
-          if (ep.vec_out && col0 + j + 4 <= ep.N) {
-            *reinterpret_cast<float4*>(dst + j) = make_float4(v0, v1, v2, v3);
-          } else {
-            if (col0 + j < ep.N) dst[j] = v0;
-            if (col0 + j + 1 < ep.N) dst[j + 1] = v1;
-            if (col0 + j + 2 < ep.N) dst[j + 2] = v2;
-            if (col0 + j + 3 < ep.N) dst[j + 3] = v3;
-          }
-        }
-      }
+      store_tile_row<kBM>(ep, w, sc.rest, quarter * 32 + lane, half * 128, acc);
     }
   }
 
@@ -728,8 +723,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap tmAhi,
                             const __grid_constant__ CUtensorMap tmAlo,
                             const __grid_constant__ CUtensorMap tmBhi,
-                            const __grid_constant__ CUtensorMap tmBlo, int num_kb_total,
-                            int kb_per_split, int tiles_m, int tiles_n, int num_units,
+                            const __grid_constant__ CUtensorMap tmBlo, Sched sc,
                             Epilogue ep, int* status) {
   using Cfg = PairCfg;
   extern __shared__ uint8_t smem_raw[];
@@ -748,26 +742,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const bool leader = rank == 0;
   const int pair = blockIdx.x >> 1;
   const int npairs = gridDim.x >> 1;
-  const int tiles = tiles_m * tiles_n;
-
-  struct Unit {
-    int m0, n0, kb0, nkb, split;
-  };
-  auto unit_of = [&](int u) {
-    Unit w;
-    const int tile = u % tiles;
-    w.split = u / tiles;
-    const int tiles_per_group = kGroupM * tiles_n;
-    const int group = tile / tiles_per_group;
-    const int first_m = group * kGroupM;
-    const int group_rows = min(tiles_m - first_m, kGroupM);
-    const int in_group = tile - group * tiles_per_group;
-    w.m0 = (first_m + in_group % group_rows) * kPairBM;
-    w.n0 = (in_group / group_rows) * kBN;
-    w.kb0 = w.split * kb_per_split;
-    w.nkb = min(num_kb_total - w.kb0, kb_per_split);
-    return w;
-  };
+  auto unit_of = [&](int u) { return unit_at(sc, u, kPairBM, kBN); };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < Cfg::Stages; ++s) {
@@ -798,7 +773,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // ------------------------------------------------ TMA producer (both CTAs)
     if (lane == 0) {
       int it = 0;
-      for (int u = pair; u < num_units && !*abort_flag; u += npairs) {
+      for (int u = pair; u < sc.units && !*abort_flag; u += npairs) {
         const Unit w = unit_of(u);
         const int a_row = w.m0 + (int)rank * 128;
         const int b_row = w.n0 + (int)rank * 128;
@@ -826,7 +801,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       using D = UmmaDesc<Cfg>;
       int it = 0, cc = 0;
       bool ok = true;
-      for (int u = pair; u < num_units && ok; u += npairs) {
+      for (int u = pair; u < sc.units && ok; u += npairs) {
         const Unit w = unit_of(u);
         for (int kb = 0; kb < w.nkb; ++kb, ++it) {
           const int s = it % Cfg::Stages;
@@ -873,7 +848,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     bool ok = true;
     int ce = 0;
 #pragma unroll 1
-    for (int u = pair; u < num_units && ok && !*abort_flag; u += npairs) {
+    for (int u = pair; u < sc.units && ok && !*abort_flag; u += npairs) {
       const Unit w = unit_of(u);
       const int num_chunks = (w.nkb + Cfg::ChunkKB - 1) / Cfg::ChunkKB;
 #pragma unroll
@@ -900,31 +875,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[buf]), 0));
       }
       if (!ok || *abort_flag) break;
-      const int64_t row = (int64_t)w.m0 + rank * 128 + quarter * 32 + lane;
-      const int64_t col0 = (int64_t)w.n0 + half * 128;
-      if (row < ep.M) {
-        float* dst = ep.Y + w.split * ep.split_stride + row * ep.ldy + col0;
-#pragma unroll
-        for (int j = 0; j < 128; j += 4) {
-          float bb[4];
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            bb[q] = (ep.bias != nullptr && col0 + j + q < ep.N) ? __ldg(ep.bias + col0 + j + q)
-                                                                : 0.0f;
-          const float v0 = apply_act(acc[j] + bb[0], ep.act, ep.alpha);
-          const float v1 = apply_act(acc[j + 1] + bb[1], ep.act, ep.alpha);
-          const float v2 = apply_act(acc[j + 2] + bb[2], ep.act, ep.alpha);
-          const float v3 = apply_act(acc[j + 3] + bb[3], ep.act, ep.alpha);
-          if (ep.vec_out && col0 + j + 4 <= ep.N) {
-            *reinterpret_cast<float4*>(dst + j) = make_float4(v0, v1, v2, v3);
-          } else {
-            if (col0 + j < ep.N) dst[j] = v0;
-            if (col0 + j + 1 < ep.N) dst[j + 1] = v1;
-            if (col0 + j + 2 < ep.N) dst[j + 2] = v2;
-            if (col0 + j + 3 < ep.N) dst[j + 3] = v3;
-          }
-        }
-      }
+      store_tile_row<kPairBM>(ep, w, sc.rest, (int)rank * 128 + quarter * 32 + lane,
+                              half * 128, acc);
     }
   }
 
@@ -979,6 +931,26 @@ static EncodeTiledFn get_encode_fn() {
       fn = reinterpret_cast<EncodeTiledFn>(p);
   }
   return fn;
+}
+
+// SMs of the current device (cached per device); without a device (host-side
+// workspace and schedule queries) the B200's 148.
+static int sm_count() {
+  static int sms[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 148;
+  }
+  if (sms[dev & 63] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      cudaGetLastError();
+      return 148;
+    }
+    sms[dev & 63] = n;
+  }
+  return sms[dev & 63];
 }
 
 // 2-D f32 tensor map: `rows` rows of `cols` valid floats, row pitch `pitch`
@@ -1039,15 +1011,6 @@ int64_t dense_f32_workspace_bytes(int64_t M, int64_t N, int64_t K) {
   // hi + lo of X (M x Kp) and of W^T (N x Kp), each region 256-byte aligned
   auto al = [](int64_t b) { return (b + 255) & ~int64_t(255); };
   return 2 * al(M * Kp * 4) + 2 * al(N * Kp * 4);
-}
-
-// Split-K partials are stored with a row pitch padded to 4 floats, so the
-// GEMM epilogue always writes them with 16-byte vector stores.
-static int64_t partials_pitch(int64_t N) { return (N + 3) & ~int64_t(3); }
-
-int64_t splitk_partials_bytes(int64_t M, int64_t N, int64_t K) {
-  const int s = choose_splits(M, N, K);
-  return s > 1 ? ((int64_t)s * M * partials_pitch(N) * 4 + 255) & ~int64_t(255) : 0;
 }
 
 int split_w_f32(const float* W, int64_t ldw, int64_t K, int64_t N, float* whiT, float* wloT,
@@ -1114,7 +1077,7 @@ static cudaError_t launch_dependent(bool pdl, void (*kernel)(KArgs...), unsigned
 template <class Cfg, bool kFusedA, bool kBMn>
 static int launch_gemm(const CUtensorMap& ta_hi, const CUtensorMap& ta_lo,
                        const CUtensorMap& tb_hi, const CUtensorMap& tb_lo, int64_t M, int64_t N,
-                       int64_t K, const Epilogue& ep, int splits, int* status,
+                       int64_t K, const Sched& sc, const Epilogue& ep, int* status,
                        cudaStream_t stream) {
   // The dynamic shared-memory opt-in is made once per device (thread-safe).
   static std::atomic<uint64_t> attr_done{0};
@@ -1128,30 +1091,21 @@ static int launch_gemm(const CUtensorMap& ta_hi, const CUtensorMap& ta_lo,
       return kErrCuda;
     attr_done.fetch_or(bit);
   }
-  const int tiles_m = (int)((M + kBM - 1) / kBM);
-  const int tiles_n = (int)((N + kBN - 1) / kBN);
-  const int num_kb = (int)((K + Cfg::BK - 1) / Cfg::BK);
-  const int kb_per_split = (num_kb + splits - 1) / splits;
-  const int nsplit = (num_kb + kb_per_split - 1) / kb_per_split;  // every split non-empty
-  const int units = tiles_m * tiles_n * nsplit;
+  const int units = sc.units;
   // Persistent: one CTA per SM (the shared-memory ring admits one) walks the
   // work units with stride gridDim.x.
-  static int sms[64] = {0};
-  if (sms[dev & 63] == 0) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return kErrCuda;
-    sms[dev & 63] = n;
-  }
+  const int sms = sm_count();
+  if (sms <= 0) return kErrCuda;
   // B200_PERSIST=0: one CTA per unit (the non-persistent schedule), for A/B.
   static const bool persist = [] {
     const char* e = getenv("B200_PERSIST");
     return !(e && e[0] == '0');
   }();
-  const int grid = persist ? std::min(units, sms[dev & 63]) : units;
+  const int grid = persist ? std::min(units, sms) : units;
   const cudaError_t e =
       launch_dependent(pdl_enabled(M, N, K), gemm_tf32x3_kernel<Cfg, kFusedA, kBMn>,
                        (unsigned)grid, kThreads, Cfg::SmemBytes, stream, ta_hi, ta_lo, tb_hi,
-                       tb_lo, num_kb, kb_per_split, tiles_m, tiles_n, units, ep, status);
+                       tb_lo, sc, ep, status);
   count_launch();
   return e == cudaSuccess ? kOk : kErrCuda;
 }
@@ -1160,8 +1114,8 @@ static int launch_gemm(const CUtensorMap& ta_hi, const CUtensorMap& ta_lo,
 // Kp, or raw X), lo from xlo (pitch Kp); fused: lo derived in the kernel.
 template <class Cfg>
 static int run_gemm(const float* xa, const float* xlo, int64_t ldx, bool fused, const BOp& b,
-                    int64_t M, int64_t N, int64_t K, const Epilogue& ep, int splits, int* status,
-                    cudaStream_t stream) {
+                    int64_t M, int64_t N, int64_t K, const Sched& sc, const Epilogue& ep,
+                    int* status, cudaStream_t stream) {
   const int64_t Kp = (K + 3) & ~int64_t(3);
   CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
   int rc = make_tmap(&ta_hi, xa, K, M, ldx, kBM, Cfg::BK);
@@ -1171,16 +1125,16 @@ static int run_gemm(const float* xa, const float* xlo, int64_t ldx, bool fused, 
     if (rc == kOk) rc = make_tmap_mn(&tb_hi, b.hi, N, K, b.ld_hi, Cfg::BK);
     if (rc == kOk) rc = make_tmap_mn(&tb_lo, b.lo, N, K, b.ld_lo, Cfg::BK);
     if (rc != kOk) return rc;
-    return launch_gemm<Cfg, false, true>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, ep, splits, status,
+    return launch_gemm<Cfg, false, true>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, sc, ep, status,
                                          stream);
   }
   if (rc == kOk) rc = make_tmap(&tb_hi, b.hi, K, N, b.ld_hi, kBN, Cfg::BK);
   if (rc == kOk) rc = make_tmap(&tb_lo, b.lo, K, N, b.ld_lo, kBN, Cfg::BK);
   if (rc != kOk) return rc;
   if (fused)
-    return launch_gemm<Cfg, true, false>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, ep, splits, status,
+    return launch_gemm<Cfg, true, false>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, sc, ep, status,
                                          stream);
-  return launch_gemm<Cfg, false, false>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, ep, splits, status,
+  return launch_gemm<Cfg, false, false>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, sc, ep, status,
                                         stream);
 }
 
@@ -1194,8 +1148,8 @@ static bool pair_variant() {
 }
 
 static int run_gemm_pair(const float* xa, const float* xlo, int64_t ldx, const float* whiT,
-                         const float* wloT, int64_t M, int64_t N, int64_t K, const Epilogue& ep,
-                         int splits, int* status, cudaStream_t stream) {
+                         const float* wloT, int64_t M, int64_t N, int64_t K, const Sched& sc,
+                         const Epilogue& ep, int* status, cudaStream_t stream) {
   using Cfg = PairCfg;
   static std::atomic<uint64_t> attr_done{0};
   int dev = 0;
@@ -1214,18 +1168,12 @@ static int run_gemm_pair(const float* xa, const float* xlo, int64_t ldx, const f
   if (rc == kOk) rc = make_tmap(&tb_hi, whiT, K, N, Kp, 128, Cfg::BK);
   if (rc == kOk) rc = make_tmap(&tb_lo, wloT, K, N, Kp, 128, Cfg::BK);
   if (rc != kOk) return rc;
-  const int tiles_m = (int)((M + kPairBM - 1) / kPairBM);
-  const int tiles_n = (int)((N + kBN - 1) / kBN);
-  const int num_kb = (int)((K + Cfg::BK - 1) / Cfg::BK);
-  const int kb_per_split = (num_kb + splits - 1) / splits;
-  const int nsplit = (num_kb + kb_per_split - 1) / kb_per_split;
-  const int units = tiles_m * tiles_n * nsplit;
-  int sms = 0;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-    return kErrCuda;
+  const int units = sc.units;
+  const int sms = sm_count();
+  if (sms <= 0) return kErrCuda;
   const int pairs = std::max(1, std::min(units, sms / 2));
   gemm_tf32x3_pair_kernel<<<2 * pairs, kThreads, Cfg::SmemBytes, stream>>>(
-      ta_hi, ta_lo, tb_hi, tb_lo, num_kb, kb_per_split, tiles_m, tiles_n, units, ep, status);
+      ta_hi, ta_lo, tb_hi, tb_lo, sc, ep, status);
   count_launch();
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
@@ -1233,19 +1181,116 @@ static int run_gemm_pair(const float* xa, const float* xlo, int64_t ldx, const f
 static bool use_pair(bool fused, const BOp& b) { return !fused && !b.mn && pair_variant(); }
 
 static int dispatch_gemm(const float* xa, const float* xlo, int64_t ldx, bool fused, const BOp& b,
-                         int64_t M, int64_t N, int64_t K, const Epilogue& ep, int splits,
+                         int64_t M, int64_t N, int64_t K, const Sched& sc, const Epilogue& ep,
                          int* status, cudaStream_t stream) {
   if (use_pair(fused, b))
-    return run_gemm_pair(xa, xlo, ldx, b.hi, b.lo, M, N, K, ep, splits, status, stream);
+    return run_gemm_pair(xa, xlo, ldx, b.hi, b.lo, M, N, K, sc, ep, status, stream);
   if (ring_variant() == 0)
-    return run_gemm<CfgBK32S2>(xa, xlo, ldx, fused, b, M, N, K, ep, splits, status, stream);
-  return run_gemm<CfgBK16S4>(xa, xlo, ldx, fused, b, M, N, K, ep, splits, status, stream);
+    return run_gemm<CfgBK32S2>(xa, xlo, ldx, fused, b, M, N, K, sc, ep, status, stream);
+  return run_gemm<CfgBK16S4>(xa, xlo, ldx, fused, b, M, N, K, sc, ep, status, stream);
 }
+
+static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool fused,
+                            const BOp& bop, int64_t M, int64_t N, int64_t K, const float* bias,
+                            float* Y, int64_t ldy, int act, float alpha, int splits,
+                            float* partials, int* status, cudaStream_t stream);
 
 int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
                          const float* wloT, int64_t M, int64_t N, int64_t K, const float* bias,
                          float* Y, int64_t ldy, int act, float alpha, int* status,
                          cudaStream_t stream) {
+  return gemm_with_splits(xhi, xlo, (K + 3) & ~int64_t(3), false, bop_k(whiT, wloT, K), M, N, K,
+                          bias, Y, ldy, act, alpha, 1, nullptr, status, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Schedules (see sched.cuh). One 128 x 256 tile (256 x 256 for a CTA pair)
+// over all of K takes 2 * BM * 256 * K / 1.65e12 s per SM at the measured
+// 3xTF32 rate; a piece spans at least one 128-wide K chunk. Cut tiles arise
+// when the last wave is partial: the 1024^3 layer (32 tiles), the MLP's
+// layers (172 and 64 tiles), 4096^3 (512 tiles = 3.46 waves).
+static Sched sched_f32(int64_t M, int64_t N, int64_t K, bool pair, int bk, bool allow_cut) {
+  const int sms = std::max(1, sm_count());
+  const int bm = pair ? kPairBM : kBM;
+  const int procs = pair ? std::max(1, sms / 2) : sms;
+  const double t_tile = 2.0 * bm * kBN * (double)K / (pair ? 2.0 : 1.0) / 1.65e12;
+  return make_sched(M, N, K, bm, kBN, bk, procs, t_tile, 4, 0, allow_cut ? 16 : 1,
+                    kChunkK / bk, kGroupM);
+}
+
+static int default_bk() { return ring_variant() == 0 ? CfgBK32S2::BK : CfgBK16S4::BK; }
+
+int choose_splits(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 1;
+  const bool pair = pair_variant();
+  const Sched sc = sched_f32(M, N, K, pair, pair ? PairCfg::BK : default_bk(), true);
+  return sc.rest > 0 ? sc.pieces : 1;
+}
+
+__global__ void __launch_bounds__(256)
+    piece_reduce_kernel(const float* __restrict__ part, Sched sc, int tile_m, int64_t M,
+                        int64_t N, const float* __restrict__ bias, int act, float alpha,
+                        float* __restrict__ Y, int64_t ldy, int vec) {
+  pdl_wait();  // launched as a programmatic dependent of the GEMM
+  const int64_t tile_elems = (int64_t)tile_m * kBN;
+  const int64_t quads_per_tile = tile_elems / 4;
+  const int64_t total = (int64_t)sc.rest * quads_per_tile;
+  const int64_t piece_stride = (int64_t)sc.rest * tile_elems;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / quads_per_tile);
+    const int64_t e = (i - r * quads_per_tile) * 4;  // element offset in the tile
+    const int lr = (int)(e / kBN), lc = (int)(e - (int64_t)lr * kBN);
+    int mt, nt;
+    tile_coords(sc, sc.whole + r, mt, nt);
+    const int64_t row = (int64_t)mt * tile_m + lr, col = (int64_t)nt * kBN + lc;
+    if (row >= M || col >= N) continue;
+    const float* src = part + (int64_t)r * tile_elems + e;
+    float4 a = __ldg(reinterpret_cast<const float4*>(src));
+    for (int p = 1; p < sc.pieces; ++p) {  // fixed order: deterministic
+      const float4 t = __ldg(reinterpret_cast<const float4*>(src + p * piece_stride));
+      a.x += t.x; a.y += t.y; a.z += t.z; a.w += t.w;
+    }
+    float v[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (bias && col + q < N) v[q] += bias[col + q];
+      v[q] = apply_act(v[q], act, alpha);
+    }
+    float* dst = Y + row * ldy + col;
+    if (vec && col + 4 <= N) {
+      *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (col + q < N) dst[q] = v[q];
+    }
+  }
+}
+
+// Bytes of cut-tile partial sums for a call of choose_splits(M, N, K) > 1
+// (the larger of the 1-SM and CTA-pair schedules when the pair kernel is
+// selected, since the fused-A path keeps the 1-SM kernel).
+int64_t splitk_partials_bytes(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  auto bytes = [&](bool pair) -> int64_t {
+    const Sched sc = sched_f32(M, N, K, pair, pair ? PairCfg::BK : default_bk(), true);
+    return sc.rest > 0 ? (int64_t)sc.pieces * sc.rest * (pair ? kPairBM : kBM) * kBN * 4 : 0;
+  };
+  const int64_t b = std::max(bytes(false), pair_variant() ? bytes(true) : int64_t(0));
+  return b ? (b + 255) & ~int64_t(255) : 0;
+}
+
+// One GEMM call: `splits` > 1 (with `partials` sized by splitk_partials_bytes)
+// lets the schedule cut the tiles of a partial last wave into K pieces;
+// otherwise every tile runs over all of K.
+static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool fused,
+                            const BOp& bop, int64_t M, int64_t N, int64_t K, const float* bias,
+                            float* Y, int64_t ldy, int act, float alpha, int splits,
+                            float* partials, int* status, cudaStream_t stream) {
+  const bool pair = use_pair(fused, bop);
+  const Sched sc = sched_f32(M, N, K, pair, pair ? PairCfg::BK : default_bk(),
+                             splits > 1 && partials != nullptr);
   Epilogue ep;
   ep.Y = Y;
   ep.ldy = ldy;
@@ -1255,118 +1300,16 @@ int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
   ep.act = act;
   ep.alpha = alpha;
   ep.vec_out = ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(Y) & 15) == 0);
-  ep.split_stride = 0;
-  return dispatch_gemm(xhi, xlo, (K + 3) & ~int64_t(3), false, bop_k(whiT, wloT, K), M, N, K, ep, 1,
-                       status, stream);
-}
-
-// ---------------------------------------------------------------------------
-// Split-K for problems with too few output tiles to fill 148 SMs (the 1024^3
-// dense layer has 32 tiles, the MLP's layers 172 and 64).
-//
-// Cost model: with T tiles and S splits, T*S CTAs run in ceil(T*S/148) waves
-// of CTAs that each do 1/S of the K work, plus an HBM pass that writes and
-// reads S partial tiles. S = 1 whenever the tiles already fill >= 4 waves.
-int choose_splits(int64_t M, int64_t N, int64_t K) {
-  const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
-  const int64_t kb16 = (K + 15) / 16;
-  if (tiles >= 4 * 148 || kb16 < 16) return 1;
-  const double t_cta_full = 2.0 * kBM * kBN * (double)K / 1.65e12;  // s per CTA, whole K
-  double best_t = 1e30;
-  int best = 1;
-  for (int s = 1; s <= 8; ++s) {
-    if (kb16 / s < 8) break;  // at least one 128-wide K chunk per split
-    const int64_t waves = (tiles * s + 147) / 148;
-    double t = waves * t_cta_full / s;
-    if (s > 1) t += (double)(s + 1) * M * N * 4 / 6.0e12;
-    if (t < best_t * 0.97) {
-      best_t = t;
-      best = s;
-    }
-  }
-  return best;
-}
-
-__global__ void splitk_reduce_kernel(const float* __restrict__ P, int splits, int64_t stride,
-                                     int64_t ldp, int64_t M, int64_t N,
-                                     const float* __restrict__ bias, int act, float alpha,
-                                     float* __restrict__ Y, int64_t ldy, int vec) {
-  pdl_wait();  // launched as a programmatic dependent of the GEMM
-  if (vec) {  // N % 4 == 0, Y 16-byte aligned, ldy % 4 == 0
-    const int64_t q = N >> 2, total = M * q;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-      const int64_t m = i / q, n = (i - m * q) << 2;
-      float4 a = __ldg(reinterpret_cast<const float4*>(P + m * ldp + n));
-      for (int s = 1; s < splits; ++s) {  // fixed order: deterministic
-        const float4 t = __ldg(reinterpret_cast<const float4*>(P + s * stride + m * ldp + n));
-        a.x += t.x; a.y += t.y; a.z += t.z; a.w += t.w;
-      }
-      if (bias) {
-        a.x += bias[n]; a.y += bias[n + 1]; a.z += bias[n + 2]; a.w += bias[n + 3];
-      }
-      a.x = apply_act(a.x, act, alpha);
-      a.y = apply_act(a.y, act, alpha);
-      a.z = apply_act(a.z, act, alpha);
-      a.w = apply_act(a.w, act, alpha);
-      *reinterpret_cast<float4*>(Y + m * ldy + n) = a;
-    }
-  } else {
-    const int64_t total = M * N;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-      const int64_t m = i / N, n = i - m * N;
-      float a = P[m * ldp + n];
-      for (int s = 1; s < splits; ++s) a += P[s * stride + m * ldp + n];
-      if (bias) a += bias[n];
-      Y[m * ldy + n] = apply_act(a, act, alpha);
-    }
-  }
-}
-
-// Shared launcher of the split-K and fused paths: GEMM (+ reduce when split).
-static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool fused,
-                            const BOp& bop, int64_t M, int64_t N, int64_t K, const float* bias,
-                            float* Y, int64_t ldy, int act, float alpha, int splits, float* partials, int* status, cudaStream_t stream) {
-  Epilogue ep;
-  ep.M = M;
-  ep.N = N;
-  if (splits <= 1) {
-    ep.Y = Y;
-    ep.ldy = ldy;
-    ep.bias = bias;
-    ep.act = act;
-    ep.alpha = alpha;
-    ep.vec_out = ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(Y) & 15) == 0);
-    ep.split_stride = 0;
-    return dispatch_gemm(xa, xlo, ldx, fused, bop, M, N, K, ep, 1, status, stream);
-  }
-  // Partials: [splits][M][ldp] raw sums (no bias, no activation).
-  const int64_t ldp = partials_pitch(N);
-  ep.Y = partials;
-  ep.ldy = ldp;
-  ep.bias = nullptr;
-  ep.act = kActNone;
-  ep.alpha = 0.0f;
-  ep.vec_out = (reinterpret_cast<uintptr_t>(partials) & 15) == 0;
-  ep.split_stride = M * ldp;
-  // The launcher may use fewer splits so that none is empty; recompute it.
-  const int bk = use_pair(fused, bop) ? PairCfg::BK
-                 : ring_variant() == 0       ? CfgBK32S2::BK
-                                             : CfgBK16S4::BK;
-  const int num_kb = (int)((K + bk - 1) / bk);
-  const int kbps = (num_kb + splits - 1) / splits;
-  const int nsplit = (num_kb + kbps - 1) / kbps;
-  int rc = dispatch_gemm(xa, xlo, ldx, fused, bop, M, N, K, ep, splits, status, stream);
-  if (rc != kOk) return rc;
-  const int vec = ((N & 3) == 0) && ((ldy & 3) == 0) &&
-                  ((reinterpret_cast<uintptr_t>(Y) & 15) == 0) && ep.vec_out;
-  const int64_t work = vec ? M * N / 4 : M * N;
-  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, 148 * 16));
-  const cudaError_t e =
-      launch_dependent(pdl_enabled(M, N, K), splitk_reduce_kernel, (unsigned)blocks, 256, 0,
-                       stream, static_cast<const float*>(partials), nsplit, M * ldp, ldp, M, N,
-                       bias, act, alpha, Y, ldy, vec);
+  ep.part = partials;
+  int rc = dispatch_gemm(xa, xlo, ldx, fused, bop, M, N, K, sc, ep, status, stream);
+  if (rc != kOk || sc.rest == 0) return rc;
+  const int tile_m = pair ? kPairBM : kBM;
+  const int64_t quads = (int64_t)sc.rest * tile_m * (kBN / 4);
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((quads + 255) / 256, 148 * 16));
+  const cudaError_t e = launch_dependent(pdl_enabled(M, N, K), piece_reduce_kernel,
+                                         (unsigned)blocks, 256, 0, stream,
+                                         static_cast<const float*>(partials), sc, tile_m, M, N,
+                                         bias, act, alpha, Y, ldy, ep.vec_out);
   count_launch();
   return e == cudaSuccess ? kOk : kErrCuda;
 }

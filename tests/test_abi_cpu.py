@@ -55,12 +55,13 @@ def test_workspace_formula():
     Kp = 1004
     assert lib.b200_dense_f32_splits(M, N, K) == 1
     assert lib.b200_dense_f32_workspace_bytes(M, N, K) == 2 * al(M * Kp * 4) + 2 * al(N * Kp * 4)
-    # one tile, long K: split-K partial sums (row pitch padded to 4) are added
+    # one tile, long K: the tile is cut into K pieces whose raw sums are kept
+    # tile-local (128 x 256 floats per piece)
     M, N, K = 100, 50, 1001
     s = lib.b200_dense_f32_splits(M, N, K)
-    assert 1 < s <= 8
+    assert 1 < s <= 16
     assert lib.b200_dense_f32_workspace_bytes(M, N, K) == (
-        2 * al(M * Kp * 4) + 2 * al(N * Kp * 4) + al(s * M * ((N + 3) // 4 * 4) * 4))
+        2 * al(M * Kp * 4) + 2 * al(N * Kp * 4) + al(s * 128 * 256 * 4))
     assert lib.b200_dense_f32_workspace_bytes(-1, 2, 3) == -1
 
 
