@@ -837,6 +837,10 @@ int b200_get_default_devices(void) {
 }
 
 int b200_release(void) {
+  // The loop visits every initialised device; the caller's current device is
+  // restored afterwards, so its later device-pointer calls stay on it.
+  int prev = 0;
+  const bool have_prev = cudaGetDevice(&prev) == cudaSuccess;
   for (int d = 0; d < 64; ++d) {
     DeviceCtx& c = g_dev[d];
     std::lock_guard<std::mutex> lk(c.mu);
@@ -854,6 +858,7 @@ int b200_release(void) {
     for (auto& kv : c.scratch) kv.second.release();
     c.scratch.clear();
   }
+  if (have_prev) cudaSetDevice(prev);
   return succeed();
 }
 

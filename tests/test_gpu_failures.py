@@ -52,3 +52,23 @@ def test_injected_allocation_failure(cuda):
                                c(Y.ctypes.data), 40, 64, 40, 48, 0, 0.0, 1)
     assert rc == 0
     assert max_err(Y, oracle.dense_f32(X, W)) <= oracle.f32_bound(48, X, W)
+
+
+def test_release_keeps_the_callers_device(cuda):
+    """b200_release visits every initialised device; afterwards the calling
+    thread must still be on its own device (a device-pointer call that
+    followed on another GPU would read this GPU's buffers from the wrong
+    device). With 2 GPUs, a sharded host call first initialises device 1."""
+    import torch
+    L = _native.lib()
+    c = ctypes.c_void_p
+    if L.b200_device_count() >= 2:
+        X = np.ones((64, 48), np.float32)
+        W = np.ones((48, 40), np.float32)
+        Y = np.zeros((64, 40), np.float32)
+        _native.check(L.b200_dense_f32_host(c(X.ctypes.data), 48, c(W.ctypes.data), 40, None,
+                                            c(Y.ctypes.data), 40, 64, 40, 48, 0, 0.0, 2))
+        assert (Y == 48).all()
+    before = torch.cuda.current_device()
+    _native.check(L.b200_release())
+    assert torch.cuda.current_device() == before
