@@ -461,3 +461,17 @@ def test_back_to_back_small_layers_match_synchronised(cuda):
     for w, bb in zip(Ws, bs):
         h = oracle.dense_f32(h, w, bb, act=1)
     assert max_err(a, h) <= 1e-4 * len(shapes)
+
+
+def test_whole_and_cut_tiles_in_one_call(cuda):
+    """156 output tiles on 148 SMs: one whole wave runs over all of K and the
+    8 tiles of the partial wave are cut into K pieces (tile-local partial sums,
+    reduced in piece order). Every element, of both kinds of tile, against
+    the oracle; the call is deterministic."""
+    import torch
+    M, N, K = 128 * 13, 256 * 12, 2048
+    assert _native.lib().b200_dense_f32_splits(M, N, K) > 1
+    X, W, b = _inputs(M, N, K, seed=156)
+    got = dense_device(torch, X, W, b, act=1)
+    assert max_err(got, oracle.dense_f32(X, W, b, act=1)) <= oracle.f32_bound(K, X, W)
+    np.testing.assert_array_equal(got, dense_device(torch, X, W, b, act=1))
