@@ -112,9 +112,11 @@ class CopyPool {
     static CopyPool pool;
     return pool;
   }
-  // Runs fn(t) for t in [0, nthreads()) and waits for all of them.
+  // Runs fn(t) for t in [0, nthreads()) and waits for all of them. Calls
+  // from several host threads (one per device) take turns: one job at a time.
   template <class Fn>
   void run(Fn fn) {
+    std::lock_guard<std::mutex> one_job(run_mu_);
     std::unique_lock<std::mutex> lk(mu_);
     job_ = [&fn](int t) { fn(t); };
     pending_ = (int)workers_.size();
@@ -163,6 +165,7 @@ class CopyPool {
     }
   }
   std::vector<std::thread> workers_;
+  std::mutex run_mu_;  // serialises run()
   std::mutex mu_;
   std::condition_variable cv_, done_cv_;
   std::function<void(int)> job_;

@@ -330,6 +330,25 @@ def test_host_api_sharded_over_two_devices(cuda):
     assert max_err(Y2[-300:], oracle.dense_f32(X[-300:], W, b, act=1)) <= bound
 
 
+def test_host_api_two_devices_staged_pageable(cuda):
+    """Pageable X and Y large enough that each device's shard is staged
+    through the runtime's pinned buffers: both device threads use the shared
+    host copy pool at the same time. Skipped with fewer than 2 GPUs."""
+    L = _native.lib()
+    if L.b200_device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    M, N, K = 8192, 1024, 1024  # 16 MiB of X and of Y per device
+    X, W, b = _inputs(M, N, K, seed=88)
+    Y = np.full((M, N), np.nan, np.float32)
+    c = ctypes.c_void_p
+    _native.check(L.b200_dense_f32_host(c(X.ctypes.data), K, c(W.ctypes.data), N,
+                                        c(b.ctypes.data), c(Y.ctypes.data), N, M, N, K, 1, 0.0,
+                                        2))
+    rows = np.r_[0:200, 4000:4300, 8000:8192]
+    assert max_err(Y[rows], oracle.dense_f32(X[rows], W, b, act=1)) <= oracle.f32_bound(K, X, W)
+    assert np.isfinite(Y).all()
+
+
 @pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (4096, 1, 4096), (8, 8, 16384),
                                    (65536, 8, 32), (3, 2050, 7), (512, 512, 16384)])
 def test_edge_shapes(cuda, M, N, K):
