@@ -415,8 +415,16 @@ struct UmmaDescBMn {
 // part) and B_lo the row-major lo part, so W needs neither a transpose nor a
 // hi copy. The producer warp's lanes issue the two B tiles and two A tiles of a
 // stage from separate lanes.
-template <class Cfg, bool kFusedA, bool kBMn>
-__global__ void __launch_bounds__(kThreads, 1)
+//
+// kFuseB (with kBMn): W_lo is not read from memory at all. Two more warps
+// (kConvWarps) derive it in shared memory from the raw B tile that TMA has
+// landed, w -> w - tf32(w) truncated, written at the same (swizzled) offset
+// of the B_lo slot, and release the stage to the MMA through conv[s] after a
+// proxy fence. The MMA then issues the usual three products in the usual
+// order, so results are bit-identical to the path that reads W_lo.
+constexpr int kConvWarps = 2;
+template <class Cfg, bool kFusedA, bool kBMn, bool kFuseB>
+__global__ void __launch_bounds__(kThreads + (kFuseB ? 32 * kConvWarps : 0), 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAhi,
                        const __grid_constant__ CUtensorMap tmAlo,
                        const __grid_constant__ CUtensorMap tmBhi,
@@ -447,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], kEpiWarps);
     }
-    for (int s = 0; s < Cfg::Stages; ++s) mbar_init(&conv[s], kEpiWarps);
+    for (int s = 0; s < Cfg::Stages; ++s) mbar_init(&conv[s], kFuseB ? kConvWarps : kEpiWarps);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -469,6 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Ring stages and TMEM chunk buffers are counted across all units of the
   // CTA, so their mbarrier phases run on from one tile to the next.
   static_assert(!(kFusedA && kBMn), "fused A split uses K-major B");
+  static_assert(!kFuseB || kBMn, "the in-kernel B_lo uses the MN-major layout");
   if (warp == 0 && kBMn) {
     // ------------------------------------------------ TMA producer (MN-major B)
     // Lane 0 waits for the stage and posts the byte count; the decision is
@@ -488,7 +497,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               !mbar_wait(&empty[s], (round - 1) & 1, status, kDevTimeoutEmpty, abort_flag))
             go = 0;
           else
-            mbar_arrive_expect_tx(&full[s], Cfg::StageBytes);
+            mbar_arrive_expect_tx(&full[s], kFuseB ? Cfg::StageBytes - Cfg::BTileBytes
+                                                   : Cfg::StageBytes);
         }
         if (!__shfl_sync(0xffffffffu, go, 0)) {
           ok = false;
@@ -496,7 +506,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         uint8_t* st = smem + s * Cfg::StageBytes;
         const int kx = (w.kb0 + kb) * Cfg::BK;
-        if (lane < 2) {  // whole 256-column B tile: {0, kx, n0 / 32}
+        if (lane < (kFuseB ? 1 : 2)) {  // whole 256-column B tile: {0, kx, n0 / 32}
           tma_load_3d(st + 2 * Cfg::ATileBytes + lane * Cfg::BTileBytes,
                       lane == 0 ? &tmBhi : &tmBlo, &full[s], 0, kx, w.n0 / 32);
         } else if (lane == 2) {
@@ -581,6 +591,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int k = 0; k < Cfg::BK / 8; ++k)
               umma_tf32(d_tmem, D::a_lo(st, k), D::b_hi(st, k), idesc, 1u);
           } else {
+            if constexpr (kFuseB) {  // B_lo of this stage derived in shared memory
+              if (!mbar_wait(&conv[s], round & 1, status, kDevTimeoutFull, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+            }
 #pragma unroll
             for (int k = 0; k < Cfg::BK / 8; ++k) {  // tf32 UMMA consumes K = 8
               umma_tf32(d_tmem, D::a_lo(st, k), DB::b_hi(st, k), idesc,
@@ -595,6 +612,40 @@ __global__ void __launch_bounds__(kThreads, 1)
             ++cc;
           }
         }
+      }
+    }
+  } else if (kFuseB && warp >= 2 + kEpiWarps) {
+    // ------------------------------------------------ B_lo converters (kFuseB)
+    const int ct = threadIdx.x - 32 * (2 + kEpiWarps);  // 0 .. 32 * kConvWarps - 1
+    int it = 0;
+    bool ok = true;
+#pragma unroll 1
+    for (int u = blockIdx.x; u < sc.units && ok; u += gridDim.x) {
+      const Unit w = unit_of(u);
+#pragma unroll 1
+      for (int kb = 0; kb < w.nkb; ++kb, ++it) {
+        const int s = it % Cfg::Stages;
+        if (!mbar_wait(&full[s], (it / Cfg::Stages) & 1, status, kDevTimeoutFull, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const float4* hi =
+            reinterpret_cast<const float4*>(smem + s * Cfg::StageBytes + 2 * Cfg::ATileBytes);
+        float4* lo = reinterpret_cast<float4*>(smem + s * Cfg::StageBytes + 2 * Cfg::ATileBytes +
+                                               Cfg::BTileBytes);
+#pragma unroll 4
+        for (int i = ct; i < Cfg::BTileBytes / 16; i += 32 * kConvWarps) {
+          const float4 v = hi[i];
+          float4 h, l;  // h is what the tensor core reads from v
+          tf32_split(v.x, h.x, l.x);
+          tf32_split(v.y, h.y, l.y);
+          tf32_split(v.z, h.z, l.z);
+          tf32_split(v.w, h.w, l.w);
+          lo[i] = l;
+        }
+        fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[s]);
       }
     }
   } else {
@@ -1074,7 +1125,7 @@ static cudaError_t launch_dependent(bool pdl, void (*kernel)(KArgs...), unsigned
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-template <class Cfg, bool kFusedA, bool kBMn>
+template <class Cfg, bool kFusedA, bool kBMn, bool kFuseB = false>
 static int launch_gemm(const CUtensorMap& ta_hi, const CUtensorMap& ta_lo,
                        const CUtensorMap& tb_hi, const CUtensorMap& tb_lo, int64_t M, int64_t N,
                        int64_t K, const Sched& sc, const Epilogue& ep, int* status,
@@ -1085,7 +1136,7 @@ static int launch_gemm(const CUtensorMap& ta_hi, const CUtensorMap& ta_lo,
   if (cudaGetDevice(&dev) != cudaSuccess) return kErrCuda;
   const uint64_t bit = 1ull << (dev & 63);
   if (!(attr_done.load() & bit)) {
-    if (cudaFuncSetAttribute(gemm_tf32x3_kernel<Cfg, kFusedA, kBMn>,
+    if (cudaFuncSetAttribute(gemm_tf32x3_kernel<Cfg, kFusedA, kBMn, kFuseB>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Cfg::SmemBytes) != cudaSuccess)
       return kErrCuda;
@@ -1103,8 +1154,9 @@ static int launch_gemm(const CUtensorMap& ta_hi, const CUtensorMap& ta_lo,
   }();
   const int grid = persist ? std::min(units, sms) : units;
   const cudaError_t e =
-      launch_dependent(pdl_enabled(M, N, K), gemm_tf32x3_kernel<Cfg, kFusedA, kBMn>,
-                       (unsigned)grid, kThreads, Cfg::SmemBytes, stream, ta_hi, ta_lo, tb_hi,
+      launch_dependent(pdl_enabled(M, N, K), gemm_tf32x3_kernel<Cfg, kFusedA, kBMn, kFuseB>,
+                       (unsigned)grid, kThreads + (kFuseB ? 32 * kConvWarps : 0),
+                       Cfg::SmemBytes, stream, ta_hi, ta_lo, tb_hi,
                        tb_lo, sc, ep, status);
   count_launch();
   return e == cudaSuccess ? kOk : kErrCuda;
@@ -1123,6 +1175,11 @@ static int run_gemm(const float* xa, const float* xlo, int64_t ldx, bool fused, 
   if (b.mn) {
     if (fused) return kErrInvalidArg;
     if (rc == kOk) rc = make_tmap_mn(&tb_hi, b.hi, N, K, b.ld_hi, Cfg::BK);
+    if (b.lo == nullptr) {  // B_lo derived in shared memory
+      if (rc != kOk) return rc;
+      return launch_gemm<Cfg, false, true, true>(ta_hi, ta_lo, tb_hi, tb_hi, M, N, K, sc, ep,
+                                                 status, stream);
+    }
     if (rc == kOk) rc = make_tmap_mn(&tb_lo, b.lo, N, K, b.ld_lo, Cfg::BK);
     if (rc != kOk) return rc;
     return launch_gemm<Cfg, false, true>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, sc, ep, status,
@@ -1386,6 +1443,14 @@ bool w_mn_ok(const float* W, int64_t ldw, int64_t M, int64_t N) {
 
 int64_t w_lo_mn_bytes(int64_t K, int64_t N) { return K * ((N + 3) & ~int64_t(3)) * 4; }
 
+bool w_lo_in_kernel() {
+  static const bool on = [] {
+    const char* e = getenv("B200_FUSE_B");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
 int split_lo_xw_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xhi, float* xlo,
                     const float* W, int64_t ldw, int64_t N, float* wlo, cudaStream_t stream) {
   const int64_t Kp = (K + 3) & ~int64_t(3), Np = (N + 3) & ~int64_t(3);
@@ -1408,7 +1473,7 @@ int gemm_tf32x3_wmn(const float* xa, const float* xlo, int64_t ldx, const float*
                     float* Y, int64_t ldy, int act, float alpha, int splits, float* partials,
                     int* status, cudaStream_t stream) {
   if (!fused_a_ok(xa, ldx) || !w_mn_ok(W, ldw, M, N)) return kErrInvalidArg;
-  const BOp b{W, wlo, ldw, (N + 3) & ~int64_t(3), true};
+  const BOp b{W, wlo, ldw, (N + 3) & ~int64_t(3), true};  // wlo == nullptr: derived in-kernel
   return gemm_with_splits(xa, xlo, ldx, false, b, M, N, K, bias, Y, ldy, act, alpha, splits,
                           partials, status, stream);
 }

@@ -66,6 +66,9 @@ bool w_mn_ok(const float* W, int64_t ldw, int64_t M, int64_t N);
 int64_t w_lo_mn_bytes(int64_t K, int64_t N);
 int split_lo_xw_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xhi, float* xlo,
                     const float* W, int64_t ldw, int64_t N, float* wlo, cudaStream_t stream);
+// w_lo_in_kernel (B200_FUSE_B=1): pass wlo == nullptr and the GEMM derives
+// W_lo in shared memory from the raw W tiles (no W pass at all).
+bool w_lo_in_kernel();
 // xa: raw X (pitch ldx) or its pre-split hi part (pitch Kp); xlo pitch Kp.
 int gemm_tf32x3_wmn(const float* xa, const float* xlo, int64_t ldx, const float* W, int64_t ldw,
                     const float* wlo, int64_t M, int64_t N, int64_t K, const float* bias,

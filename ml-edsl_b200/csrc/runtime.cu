@@ -436,8 +436,12 @@ int dense_device(DeviceCtx* c, const float* X, int64_t ldx, const float* W, int6
     // W is read as-is (MN-major B_hi); its row-major lo part goes into the
     // W split region. X likewise when its rows are 16-byte aligned.
     const bool xraw = fused_a_ok(X, ldx);
-    float* wlo = s.whi;
-    rc = split_lo_xw_f32(X, ldx, M, K, xraw ? nullptr : s.xhi, s.xlo, W, ldw, N, wlo, st);
+    float* wlo = w_lo_in_kernel() ? nullptr : s.whi;
+    if (wlo)
+      rc = split_lo_xw_f32(X, ldx, M, K, xraw ? nullptr : s.xhi, s.xlo, W, ldw, N, wlo, st);
+    else
+      rc = xraw ? split_x_lo_f32(X, ldx, M, K, s.xlo, st)
+                : split_x_f32(X, ldx, M, K, s.xhi, s.xlo, st);
     if (rc == kOk)
       rc = gemm_tf32x3_wmn(xraw ? X : s.xhi, s.xlo, xraw ? ldx : (K + 3) & ~int64_t(3), W, ldw,
                            wlo, M, N, K, b, Y, ldy, act, alpha, splits, s.partials, c->status,
@@ -542,7 +546,7 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
   if (K > 0) {
     if ((rc = h2d_rows(c, dW, N * 4, W, ldw * 4, N * 4, K, c->s_comp))) return rc;
     // A single-slab call splits W together with X (one launch) below.
-    if (nslab > 1 && wmn) {
+    if (nslab > 1 && wmn && !w_lo_in_kernel()) {
       rc = split_lo_xw_f32(nullptr, 0, 0, K, nullptr, nullptr, dW, N, N, dWhi, c->s_comp);
       if (rc) return fail(rc, "split W launch failed");
     } else if (!wmn && (nslab > 1 || fuse_a(static_cast<float*>(c->x[0].p), K))) {
@@ -587,14 +591,15 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
         float* xhi = static_cast<float*>(c->xhi[slot].p);
         float* xlo = static_cast<float*>(c->xlo[slot].p);
         const bool xraw = fused_a_ok(dX, K);
-        if (nslab == 1)
-          rc = split_lo_xw_f32(dX, K, rows, K, xraw ? nullptr : xhi, xlo, dW, N, N, dWhi,
+        float* wlo = w_lo_in_kernel() ? nullptr : dWhi;
+        if (nslab == 1 && wlo)
+          rc = split_lo_xw_f32(dX, K, rows, K, xraw ? nullptr : xhi, xlo, dW, N, N, wlo,
                                c->s_comp);
         else
           rc = xraw ? split_x_lo_f32(dX, K, rows, K, xlo, c->s_comp)
                     : split_x_f32(dX, K, rows, K, xhi, xlo, c->s_comp);
         if (rc == kOk)
-          rc = gemm_tf32x3_wmn(xraw ? dX : xhi, xlo, xraw ? K : Kp, dW, N, dWhi, rows, N, K, db,
+          rc = gemm_tf32x3_wmn(xraw ? dX : xhi, xlo, xraw ? K : Kp, dW, N, wlo, rows, N, K, db,
                                dY, N, act, alpha, splits, part, c->status, c->s_comp);
       } else if (fused_a_ok(dX, K)) {
         float* xlo = static_cast<float*>(c->xlo[slot].p);

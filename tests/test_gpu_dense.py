@@ -430,13 +430,17 @@ np.savez(sys.argv[4], *t._wmn_outputs(torch))
 print("ok")
 """
     tests_dir = os.path.dirname(os.path.abspath(__file__))
-    env = dict(os.environ, B200_W_MN="0")
-    r = subprocess.run([sys.executable, "-c", script, ROOT, PKG_PARENT, tests_dir, out], env=env,
-                       capture_output=True, text=True, timeout=600)
-    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
-    ref = np.load(out)
-    for i, (got, shape) in enumerate(zip(_wmn_outputs(torch), _WMN_SHAPES)):
-        np.testing.assert_array_equal(got, ref[f"arr_{i}"], err_msg=str(shape))
+    mine = _wmn_outputs(torch)
+    # B200_W_MN=0: transposed K-major split; B200_FUSE_B=1: W_lo derived in
+    # shared memory by the GEMM's converter warps (no W pass)
+    for var in ({"B200_W_MN": "0"}, {"B200_FUSE_B": "1"}):
+        env = dict(os.environ, **var)
+        r = subprocess.run([sys.executable, "-c", script, ROOT, PKG_PARENT, tests_dir, out],
+                           env=env, capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
+        ref = np.load(out)
+        for i, (got, shape) in enumerate(zip(mine, _WMN_SHAPES)):
+            np.testing.assert_array_equal(got, ref[f"arr_{i}"], err_msg=f"{var} {shape}")
     M, N, K = _WMN_SHAPES[1]
     X, W, b = _inputs(M, N, K, seed=N + K)
     assert max_err(_wmn_outputs(torch)[1], oracle.dense_f32(X, W, b, act=1)) <= \
