@@ -209,6 +209,15 @@ int b200_dot_i32(const int32_t* a, const int32_t* b, int64_t n, int32_t* out, vo
 int b200_selftest_wait_timeout(int64_t limit_ns, void* stream);
 int b200_debug_fail_alloc(int n);
 
+/* b200_debug_schedule(kind, M, N, K, out): the work schedule the persistent
+ * GEMM would use on the current device (148 SMs without one); kind 0 = the
+ * f32 dense layer, 1 = the i32 matmul. out[0..7] = tiles_m, tiles_n, whole
+ * (tiles over all of K), rest (tiles cut into K pieces), pieces, k-blocks per
+ * tile, k-blocks per piece, work units. Returns B200_OK, or
+ * B200_ERR_INVALID_ARG for a bad kind or non-positive dimensions. Test and
+ * tuning aid with no counterpart in the reference. */
+int b200_debug_schedule(int kind, int64_t M, int64_t N, int64_t K, int64_t* out);
+
 /* Page-locked host memory from a runtime pool (blocks are cached after
  * b200_host_free and reused). Results copied back into such buffers move at
  * full PCIe speed; the Python frontend returns its arrays in them. */

@@ -396,6 +396,13 @@ Sched sched_i32(int64_t M, int64_t N, int64_t K) {
 
 }  // namespace
 
+void sched_query_i32(int64_t M, int64_t N, int64_t K, int64_t* out) {
+  const Sched sc = sched_i32(M, N, K);
+  const int64_t v[8] = {sc.tiles_m, sc.tiles_n, sc.whole, sc.rest, sc.pieces, sc.kb, sc.kbp,
+                        sc.units};
+  for (int i = 0; i < 8; ++i) out[i] = v[i];
+}
+
 int choose_splits_i32(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0) return 1;
   const Sched sc = sched_i32(M, N, K);

@@ -1277,6 +1277,14 @@ static Sched sched_f32(int64_t M, int64_t N, int64_t K, bool pair, int bk, bool 
 
 static int default_bk() { return ring_variant() == 0 ? CfgBK32S2::BK : CfgBK16S4::BK; }
 
+void sched_query_f32(int64_t M, int64_t N, int64_t K, int64_t* out) {
+  const bool pair = pair_variant();
+  const Sched sc = sched_f32(M, N, K, pair, pair ? PairCfg::BK : default_bk(), true);
+  const int64_t v[8] = {sc.tiles_m, sc.tiles_n, sc.whole, sc.rest, sc.pieces, sc.kb, sc.kbp,
+                        sc.units};
+  for (int i = 0; i < 8; ++i) out[i] = v[i];
+}
+
 int choose_splits(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0) return 1;
   const bool pair = pair_variant();

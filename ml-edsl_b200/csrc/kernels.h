@@ -37,6 +37,10 @@ int split_w_f32(const float* W, int64_t ldw, int64_t K, int64_t N, float* whiT, 
 // Split-K (few-tile problems): splits chosen by a wave-count cost model;
 // partials scratch of splitk_partials_bytes() (0 when splits == 1).
 int choose_splits(int64_t M, int64_t N, int64_t K);
+// Schedule of the persistent GEMMs (tiles_m, tiles_n, whole, rest, pieces,
+// kb, kbp, units) for b200_debug_schedule.
+void sched_query_f32(int64_t M, int64_t N, int64_t K, int64_t* out);
+void sched_query_i32(int64_t M, int64_t N, int64_t K, int64_t* out);
 int64_t splitk_partials_bytes(int64_t M, int64_t N, int64_t K);
 int gemm_tf32x3_splitk(const float* xhi, const float* xlo, const float* whiT, const float* wloT,
                        int64_t M, int64_t N, int64_t K, const float* bias, float* Y, int64_t ldy,

@@ -1254,6 +1254,16 @@ int b200_selftest_wait_timeout(int64_t limit_ns, void* stream) {
   return rc ? fail(rc, "self-test launch failed") : succeed();
 }
 
+int b200_debug_schedule(int kind, int64_t M, int64_t N, int64_t K, int64_t* out) {
+  if ((kind != 0 && kind != 1) || M <= 0 || N <= 0 || K <= 0 || !out)
+    return fail(kErrInvalidArg, "bad schedule query");
+  if (kind == 0)
+    sched_query_f32(M, N, K, out);
+  else
+    sched_query_i32(M, N, K, out);
+  return succeed();
+}
+
 int b200_debug_fail_alloc(int n) {
   if (n < 0) return fail(kErrInvalidArg, "n must be >= 0");
   g_fail_alloc_in.store(n);

@@ -7,6 +7,7 @@ import re
 
 import numpy as np
 import pytest
+from hypothesis import given, settings, strategies as st
 
 from conftest import HAS_GPU, ROOT
 from mlir_edsl import _native
@@ -129,3 +130,56 @@ def test_missing_library_raises(monkeypatch, tmp_path):
     monkeypatch.setattr(_native, "LIB_PATH", str(tmp_path / "nope.so"))
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         _native.lib()
+
+
+def _schedule(kind, M, N, K):
+    out = (ctypes.c_int64 * 8)()
+    assert _native.lib().b200_debug_schedule(kind, M, N, K, out) == 0
+    keys = ("tiles_m", "tiles_n", "whole", "rest", "pieces", "kb", "kbp", "units")
+    return dict(zip(keys, list(out)))
+
+
+
+@settings(max_examples=300, deadline=None)
+@given(kind=st.sampled_from([0, 1]), M=st.integers(1, 70000), N=st.integers(1, 20000),
+       K=st.integers(1, 40000))
+def test_schedule_invariants(kind, M, N, K):
+    """The persistent GEMMs' work schedule (host logic, no GPU): every tile
+    is covered once, whole tiles fill whole waves of the 148 SMs, a cut tile's
+    pieces are non-empty and cover its K range exactly, an f32 piece spans at
+    least one 128-wide K chunk, and no i32 unit covers more than 8192 bytes of
+    K (so its s32 accumulators cannot overflow)."""
+    s = _schedule(kind, M, N, K)
+    bm, bn, bk = (128, 256, 16) if kind == 0 else (128, 128, 64)
+    cdiv = lambda a, b: -(-a // b)
+    assert s["tiles_m"] == cdiv(M, bm) and s["tiles_n"] == cdiv(N, bn)
+    assert s["kb"] == cdiv(K, bk)
+    tiles = s["tiles_m"] * s["tiles_n"]
+    assert s["whole"] + s["rest"] == tiles
+    assert s["units"] == s["whole"] + s["rest"] * s["pieces"]
+    if s["rest"] == 0:
+        assert s["pieces"] == 1 and s["kbp"] == s["kb"]
+    else:
+        assert s["pieces"] >= 2
+        assert (s["pieces"] - 1) * s["kbp"] < s["kb"] <= s["pieces"] * s["kbp"]
+        assert s["whole"] % 148 == 0
+        if kind == 0:
+            assert s["kbp"] >= 128 // bk
+    if kind == 1:
+        assert (s["kbp"] if s["rest"] else s["kb"]) * bk <= 8192
+
+
+def test_schedule_examples():
+    """The f32 dense layer: 65536 x 4096 x 4096 runs whole (55 full waves and a
+    52-tile tail not worth cutting); 1024^3 cuts its 32 tiles into 4 pieces;
+    the MLP's 172-tile layer runs one whole wave and cuts the other 24 tiles.
+    i32 at 64 x 64 x 20000 cuts every tile (K over 8192 bytes)."""
+    s = _schedule(0, 65536, 4096, 4096)
+    assert (s["whole"], s["rest"]) == (8192, 0)
+    s = _schedule(0, 1024, 1024, 1024)
+    assert (s["whole"], s["rest"], s["pieces"]) == (0, 32, 4)
+    s = _schedule(0, 512, 11008, 4096)
+    assert (s["whole"], s["rest"]) == (148, 24) and s["pieces"] > 1
+    s = _schedule(1, 64, 64, 20000)
+    assert s["whole"] == 0 and s["pieces"] >= 3
+    assert _native.lib().b200_debug_schedule(2, 1, 1, 1, (ctypes.c_int64 * 8)()) == 1
