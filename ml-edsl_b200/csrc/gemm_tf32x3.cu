@@ -86,16 +86,30 @@ struct RingCfg {
 using CfgBK32S2 = RingCfg<32, 2>;  // 2 stages of 96 KB
 using CfgBK16S4 = RingCfg<16, 4>;  // 4 stages of 48 KB
 
+// x -> hi (tf32: low 13 mantissa bits cleared) + lo (the rest, truncated to
+// tf32). The products hi*hi + hi*lo + lo*hi approximate x*y to f32 level.
+//
+// Non-finite operands. Inf and NaN travel in hi. A zero lo would turn the
+// cross term Inf * lo into Inf * 0 = NaN where f32 gives +-Inf (Inf times an
+// exactly representable partner such as 1.0, or Inf * Inf). So the lo of a
+// non-zero value is never zero: when the exact lo is 0 (x representable in
+// tf32, or x = +-Inf), lo = +-FLT_MIN with x's sign. Then Inf * y = +-Inf and
+// Inf * 0 = NaN as in f32, and a finite product gains at most
+// FLT_MIN * |partner| (about 1e-38), below f32 resolution of any result not
+// within ~1e-35 of zero. Zero keeps lo = 0 (exact zeros stay exact); NaN keeps
+// lo = 0 (NaN propagates through hi).
 __device__ __forceinline__ void tf32_split(float x, float& h, float& l) {
   const uint32_t u = __float_as_uint(x);
+  const float tiny = __uint_as_float((u & 0x80000000u) | 0x00800000u);  // +-FLT_MIN
   if ((u & 0x7F800000u) == 0x7F800000u) {  // Inf / NaN travel in the hi part
     h = x;
-    l = 0.0f;
+    l = (u & 0x007FFFFFu) ? 0.0f : tiny;
     return;
   }
   h = __uint_as_float(u & 0xFFFFE000u);
   const float r = x - h;  // exact: r holds the 13 cleared mantissa bits
   l = __uint_as_float(__float_as_uint(r) & 0xFFFFE000u);
+  if ((__float_as_uint(l) & 0x7FFFFFFFu) == 0u && (u & 0x7FFFFFFFu) != 0u) l = tiny;
 }
 
 // ---------------------------------------------------------------------------

@@ -498,3 +498,56 @@ def test_whole_and_cut_tiles_in_one_call(cuda):
     got = dense_device(torch, X, W, b, act=1)
     assert max_err(got, oracle.dense_f32(X, W, b, act=1)) <= oracle.f32_bound(K, X, W)
     np.testing.assert_array_equal(got, dense_device(torch, X, W, b, act=1))
+
+
+def test_split_rule_for_exact_and_non_finite_values(cuda):
+    """tf32 split: zero -> (0, 0); a non-zero value exactly representable in
+    tf32, and +-Inf -> lo = +-FLT_MIN with the value's sign (so that Inf times
+    an exact partner stays Inf); NaN -> hi NaN, lo 0; otherwise hi + lo is x
+    to within 2^-21 relative."""
+    import torch
+    dev = torch.device("cuda:0")
+    L = _native.lib()
+    tiny = np.float32(np.finfo(np.float32).tiny)
+    x = np.array([[0.0, -0.0, 1.0, -0.5, 3.0, np.inf, -np.inf, np.nan,
+                   0.1, -1.2345678, 7.0e-3, 1.0e30]], np.float32)
+    tX = torch.from_numpy(x).to(dev)
+    hi, lo = torch.empty((1, 12), device=dev), torch.empty((1, 12), device=dev)
+    _native.check(L.b200_tf32_split_rows(ptr(tX), 12, 1, 12, ptr(hi), ptr(lo), stream_ptr(torch)))
+    _native.check(L.b200_stream_sync(stream_ptr(torch)))
+    h, l = hi.cpu().numpy()[0], lo.cpu().numpy()[0]
+    assert (l[:2] == 0).all() and (h[:2] == 0).all()
+    np.testing.assert_array_equal(l[2:7], [tiny, -tiny, tiny, tiny, -tiny])
+    np.testing.assert_array_equal(h[2:7], x[0, 2:7])
+    assert np.isnan(h[7]) and l[7] == 0
+    v = x[0, 8:].astype(np.float64)
+    assert np.all(np.abs(h[8:].astype(np.float64) + l[8:] - v) <= np.abs(v) * 2.0 ** -21)
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 64, 32), (300, 257, 100)])
+def test_inf_and_nan_inputs_follow_f32(cuda, M, N, K):
+    """Inf and NaN in X and W give the f32 result class of the reference's
+    FMA chain element by element: Inf * exact values (1.0, 0.5) and Inf * Inf
+    stay +-Inf, Inf * 0 and Inf - Inf give NaN, and finite outputs agree within
+    the f32 bound. N = 64 reads W MN-major, N = 257 the K-major split."""
+    import torch
+    rng = np.random.default_rng(M + N)
+    X = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    W = rng.choice(np.array([1.0, 0.5, -2.0, 0.0, 0.3], np.float32), (K, N))
+    X[3, 5] = np.inf
+    X[7, 1] = -np.inf
+    X[7, 2] = np.inf        # row 7: +Inf and -Inf terms
+    X[9, 4] = np.nan
+    X[11, :] = 0.0
+    W[6, 10] = np.inf       # column 10: Inf weight
+    W[8, 12] = -np.inf
+    b = rng.uniform(-1, 1, N).astype(np.float32)
+    got = dense_device(torch, X, W, b, act=0)
+    ref = oracle.dense_f32(X, W, b, act=0)
+    np.testing.assert_array_equal(np.isnan(got), np.isnan(ref))
+    np.testing.assert_array_equal(np.isposinf(got), np.isposinf(ref))
+    np.testing.assert_array_equal(np.isneginf(got), np.isneginf(ref))
+    fin = np.isfinite(ref)
+    assert np.isinf(ref).any() and np.isnan(ref).any()
+    Xf, Wf = np.nan_to_num(X, posinf=0, neginf=0), np.nan_to_num(W, posinf=0, neginf=0)
+    assert max_err(got[fin], ref[fin]) <= oracle.f32_bound(K, Xf, Wf)
