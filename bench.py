@@ -55,6 +55,11 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-headline", action="store_true")
+    ap.add_argument("--no-gather", action="store_true",
+                    help="N>1: skip the all-gathered (single-device result) measurement")
+    ap.add_argument("--gather-slabs", type=int, default=4)
+    ap.add_argument("--gather-reserve-sms", type=int, default=8,
+                    help="SMs the GEMM leaves free for NCCL while gathering")
     ap.add_argument("--configs", action="store_true",
                     help="measure every BASELINE.json config on one GPU, one JSON line each")
     ap.add_argument("--rows", type=int, default=0,
@@ -394,6 +399,50 @@ def run_b200(args):
                       "buffers, host wall clock, max over ranks"}
         del Xh, Wh, bh, Yh
 
+    # ---- single-device result requested: the full Y on every rank, all-gathered
+    # with NCCL over NVLink slab by slab while the next slab's GEMM runs
+    # (mlir_edsl.sharding.dense_rows(gather=True)); device time, max over ranks
+    gathered = None
+    if world > 1 and not args.no_gather:
+        from mlir_edsl.sharding import dense_rows
+
+        def gtime(slabs, transport="ce"):
+            for _ in range(2):
+                Yf = dense_rows(X, W, b, 1, 0.0, gather=True, slabs=slabs,
+                                reserve_sms=args.gather_reserve_sms, transport=transport)
+            barrier()
+            e0.record(stream)
+            for _ in range(args.steps):
+                Yf = dense_rows(X, W, b, 1, 0.0, gather=True, slabs=slabs,
+                                reserve_sms=args.gather_reserve_sms, transport=transport)
+            e1.record(stream)
+            barrier()
+            return max_over_ranks(e0.elapsed_time(e1) / args.steps), Yf
+
+        g_ms, Yf = gtime(args.gather_slabs)
+        step()
+        torch.cuda.synchronize()
+        bound = 1e-4 * K ** 0.5 * float(X.abs().max()) * float(W.abs().max())
+        g_err = float((Yf.view(world, M, N)[rank] - Y).abs().max())
+        assert g_err <= bound, f"gathered rows differ from the sharded result: {g_err}"
+        g1_ms, Yf = gtime(1)
+        gn_ms, Yf = gtime(args.gather_slabs, "nccl")
+        gn_err = float((Yf.view(world, M, N)[rank] - Y).abs().max())
+        assert gn_err <= bound, f"NCCL-gathered rows differ from the sharded result: {gn_err}"
+        del Yf
+        recv = (world - 1) * M * N * 4
+        gathered = {"value": flops_job / (g_ms / 1e3) / 1e12, "unit": UNIT, "ms_per_step": g_ms,
+                    "slabs": args.gather_slabs, "reserve_sms": args.gather_reserve_sms,
+                    "ms_per_step_unpipelined": g1_ms,
+                    "sharded_ms_per_step": ms_total / args.steps,
+                    "recv_bytes_per_rank": recv, "recv_GBps_per_rank": recv / (g_ms / 1e3) / 1e9,
+                    "transport": "copy engines: each finished slab pushed into every peer's "
+                                 "CUDA-IPC-mapped output buffer (peer DMA over NVLink/NVSwitch) "
+                                 "on a side stream, overlapping the next slab's GEMM",
+                    "nccl_ms_per_step": gn_ms,
+                    "nccl_transport": "NCCL all_gather_into_tensor per slab on a side stream, "
+                                      "GEMM grid leaving reserve_sms SMs free"}
+
     # ---- headline 8192^3 dense (N=1 only)
     headline = None
     if world == 1 and not args.no_headline:
@@ -450,6 +499,7 @@ def run_b200(args):
                        "precision": "3xTF32 tensor cores, f32 accumulation promoted every 128 "
                                     "of K"},
             "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
+            "gathered": gathered,
             "gpu_launches": launches, "headline_8192": headline,
         }
         emit_line(line)

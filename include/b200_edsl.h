@@ -209,6 +209,26 @@ int b200_dot_i32(const int32_t* a, const int32_t* b, int64_t n, int32_t* out, vo
 int b200_selftest_wait_timeout(int64_t limit_ns, void* stream);
 int b200_debug_fail_alloc(int n);
 
+/* Cross-process device buffers for the all-gather of a row-sharded result:
+ * b200_ipc_alloc allocates `bytes` on the current device and writes its
+ * 64-byte CUDA IPC handle to handle_out; another rank maps it with
+ * b200_ipc_open and unmaps it with b200_ipc_close; b200_ipc_free releases it.
+ * b200_memcpy_d2d_async copies on `stream`, also into a mapped peer buffer
+ * (a peer DMA over NVLink on the copy engines). These have no counterpart in
+ * the reference, whose results never leave one device. */
+int b200_ipc_alloc(void** ptr, int64_t bytes, void* handle_out);
+int b200_ipc_free(void* ptr);
+int b200_ipc_open(const void* handle, void** ptr);
+int b200_ipc_close(void* ptr);
+int b200_memcpy_d2d_async(void* dst, const void* src, int64_t bytes, void* stream);
+
+/* b200_set_gemm_sm_limit(n): the f32 GEMM's persistent grid (and its work
+ * schedule) uses at most n SMs from the next call on, leaving the rest free for
+ * concurrent kernels such as an NCCL all-gather of finished row slabs; 0 = all
+ * SMs. Returns the previous limit (process-wide), or -1 with
+ * B200_ERR_INVALID_ARG recorded for n < 0. No counterpart in the reference. */
+int b200_set_gemm_sm_limit(int n);
+
 /* b200_debug_schedule(kind, M, N, K, out): the work schedule the persistent
  * GEMM would use on the current device (148 SMs without one); kind 0 = the
  * f32 dense layer, 1 = the i32 matmul. out[0..7] = tiles_m, tiles_n, whole

@@ -998,9 +998,24 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
+// Most SMs the f32 GEMM's persistent grid may occupy (0: all). A caller that
+// runs a collective concurrently (the slab-pipelined all-gather of a sharded
+// result) leaves SMs free for its kernels.
+static std::atomic<int> g_gemm_sm_limit{0};
+int set_gemm_sm_limit(int n) { return g_gemm_sm_limit.exchange(n > 0 ? n : 0); }
+
+static int device_sm_count();
+// SMs the GEMM's schedule and persistent grid use: the device's, capped by
+// set_gemm_sm_limit.
+static int sm_count() {
+  const int n = device_sm_count();
+  const int lim = g_gemm_sm_limit.load();
+  return lim > 0 && lim < n ? lim : n;
+}
+
 // SMs of the current device (cached per device); without a device (host-side
 // workspace and schedule queries) the B200's 148.
-static int sm_count() {
+static int device_sm_count() {
   static int sms[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {

@@ -37,6 +37,9 @@ int split_w_f32(const float* W, int64_t ldw, int64_t K, int64_t N, float* whiT, 
 // Split-K (few-tile problems): splits chosen by a wave-count cost model;
 // partials scratch of splitk_partials_bytes() (0 when splits == 1).
 int choose_splits(int64_t M, int64_t N, int64_t K);
+// Cap on the SMs the f32 GEMM's persistent grid occupies (0: all); returns the
+// previous cap.
+int set_gemm_sm_limit(int n);
 // Schedule of the persistent GEMMs (tiles_m, tiles_n, whole, rest, pieces,
 // kb, kbp, units) for b200_debug_schedule.
 void sched_query_f32(int64_t M, int64_t N, int64_t K, int64_t* out);

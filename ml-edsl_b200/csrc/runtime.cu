@@ -1254,6 +1254,65 @@ int b200_selftest_wait_timeout(int64_t limit_ns, void* stream) {
   return rc ? fail(rc, "self-test launch failed") : succeed();
 }
 
+// ---------------------------------------------------------------- IPC buffers
+// Device buffers another process (another GPU's rank) can map: a rank pushes
+// its finished row slabs straight into its peers' output buffers with
+// cudaMemcpyAsync, i.e. the copy engines over NVLink, so the transfer needs no
+// SMs and overlaps the next slab's GEMM.
+int b200_ipc_alloc(void** ptr, int64_t bytes, void* handle_out) {
+  if (!ptr || !handle_out || bytes <= 0) return fail(kErrInvalidArg, "bad IPC allocation");
+  *ptr = nullptr;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, (size_t)bytes);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaMalloc (IPC buffer)");
+  cudaIpcMemHandle_t h;
+  e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail_cuda(e, "cudaIpcGetMemHandle");
+  }
+  memcpy(handle_out, &h, sizeof h);
+  *ptr = p;
+  return succeed();
+}
+
+int b200_ipc_free(void* ptr) {
+  if (ptr) B200_CUDA(cudaFree(ptr), "cudaFree (IPC buffer)");
+  return succeed();
+}
+
+int b200_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return fail(kErrInvalidArg, "bad IPC handle");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof h);
+  B200_CUDA(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+  return succeed();
+}
+
+int b200_ipc_close(void* ptr) {
+  if (ptr) B200_CUDA(cudaIpcCloseMemHandle(ptr), "cudaIpcCloseMemHandle");
+  return succeed();
+}
+
+// Asynchronous device-to-device copy on `stream`; src and dst may be on
+// different GPUs (an IPC-mapped peer buffer), which runs as a peer DMA.
+int b200_memcpy_d2d_async(void* dst, const void* src, int64_t bytes, void* stream) {
+  if (bytes < 0 || (bytes > 0 && (!dst || !src))) return fail(kErrInvalidArg, "bad copy");
+  if (bytes)
+    B200_CUDA(cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDeviceToDevice,
+                              static_cast<cudaStream_t>(stream)),
+              "cudaMemcpyAsync D2D");
+  return succeed();
+}
+
+int b200_set_gemm_sm_limit(int n) {
+  if (n < 0) {
+    fail(kErrInvalidArg, "negative SM limit");
+    return -1;
+  }
+  return set_gemm_sm_limit(n);
+}
+
 int b200_debug_schedule(int kind, int64_t M, int64_t N, int64_t K, int64_t* out) {
   if ((kind != 0 && kind != 1) || M <= 0 || N <= 0 || K <= 0 || !out)
     return fail(kErrInvalidArg, "bad schedule query");

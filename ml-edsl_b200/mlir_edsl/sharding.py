@@ -30,3 +30,208 @@ def max_over_ranks(value: float, dist=None, device=None) -> float:
     t = torch.tensor([float(value)], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def slab_bounds(rows: int, slabs: int) -> List[Tuple[int, int]]:
+    """[r0, r1) of `slabs` near-equal row slabs of `rows` rows (no empty slab)."""
+    slabs = max(1, min(int(slabs), rows)) if rows > 0 else 1
+    base, rem = divmod(rows, slabs)
+    out, r0 = [], 0
+    for i in range(slabs):
+        r1 = r0 + base + (1 if i < rem else 0)
+        out.append((r0, r1))
+        r0 = r1
+    return out
+
+
+def gather_rows_pipelined(rows: int, N: int, compute_slab, *, slabs: int = 4, group=None,
+                          device=None, dtype=None):
+    """Assembles on every rank the full [world * rows, N] result of a
+    row-sharded computation, rank r's rows at [r * rows, (r + 1) * rows).
+
+    compute_slab(r0, r1, out) writes this rank's local rows [r0, r1) into
+    `out` (a [r1 - r0, N] view of the full result) on the current stream.
+    Slab s is then all-gathered on a separate stream while slab s + 1 is
+    computed: with NCCL over NVLink the transfer overlaps the next slab's
+    GEMM. Every rank must pass the same `rows`. Without a process group
+    (or with one rank) it just computes.
+    """
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+    rank = dist.get_rank(group) if world > 1 else 0
+    Y = torch.empty((world * rows, N), device=device, dtype=dtype)
+    Yv = Y.view(world, rows, N)
+    bounds = slab_bounds(rows, slabs)
+    if world == 1:
+        for r0, r1 in bounds:
+            compute_slab(r0, r1, Yv[0, r0:r1])
+        return Y
+    on_gpu = Y.is_cuda
+    nccl = dist.get_backend(group) == "nccl"
+    comm = torch.cuda.Stream(device=Y.device) if on_gpu else None
+    max_slab = max(r1 - r0 for r0, r1 in bounds)
+    tmp = [torch.empty((world * max_slab * N,), device=device, dtype=dtype) for _ in range(2)]
+    for s, (r0, r1) in enumerate(bounds):
+        n = r1 - r0
+        mine = Yv[rank, r0:r1]
+        compute_slab(r0, r1, mine)
+        ctx = None
+        if on_gpu:
+            ev = torch.cuda.Event()
+            ev.record()
+            comm.wait_event(ev)
+            ctx = torch.cuda.stream(comm)
+            ctx.__enter__()
+        try:
+            t = tmp[s % 2][: world * n * N].view(world, n, N)
+            if nccl:
+                dist.all_gather_into_tensor(t, mine, group=group)
+            else:
+                dist.all_gather(list(t.unbind(0)), mine, group=group)
+            Yv[:, r0:r1].copy_(t)
+        finally:
+            if ctx is not None:
+                ctx.__exit__(None, None, None)
+    if on_gpu:
+        torch.cuda.current_stream(Y.device).wait_stream(comm)
+    return Y
+
+
+class _DeviceArray:
+    """A raw device buffer exposed through __cuda_array_interface__ (f32)."""
+
+    def __init__(self, ptr, shape):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<f4",
+                                         "data": (int(ptr), False), "version": 3,
+                                         "strides": None, "stream": None}
+
+
+class _PeerRows:
+    """Each rank's [world * rows, N] f32 output buffer, allocated once per
+    shape and mapped into every other rank (CUDA IPC) so that a rank can copy
+    its finished rows straight into all of them. Cached per (rows, N, device,
+    group); held until the process exits."""
+
+    _cache = {}
+
+    @classmethod
+    def get(cls, rows, N, device, group):
+        key = (rows, N, device.index, id(group))
+        if key not in cls._cache:
+            cls._cache[key] = cls(rows, N, device, group)
+        return cls._cache[key]
+
+    def __init__(self, rows, N, device, group):
+        import ctypes
+        import torch
+        import torch.distributed as dist
+        from . import _native
+        L = _native.lib()
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        nbytes = world * rows * N * 4
+        ptr, handle = ctypes.c_void_p(), ctypes.create_string_buffer(64)
+        with torch.cuda.device(device):
+            _native.check(L.b200_ipc_alloc(ctypes.byref(ptr), nbytes, handle))
+        handles = [None] * world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self.ptrs = []
+        with torch.cuda.device(device):
+            for r, h in enumerate(handles):
+                if r == rank:
+                    self.ptrs.append(ptr.value)
+                    continue
+                p = ctypes.c_void_p()
+                _native.check(L.b200_ipc_open(ctypes.create_string_buffer(h, 64), ctypes.byref(p)))
+                self.ptrs.append(p.value)
+        self.local = ptr.value
+        self.Y = torch.as_tensor(_DeviceArray(ptr.value, (world * rows, N)), device=device)
+        self.comm = torch.cuda.Stream(device=device)
+
+
+def gather_rows_ce(rows: int, N: int, compute_slab, *, slabs: int = 4, group=None, device=None):
+    """gather_rows_pipelined over the copy engines: each rank computes its rows
+    slab by slab into its own region of a persistent IPC-shared output buffer
+    and pushes every finished slab into the same region of each peer's buffer
+    with cudaMemcpyAsync (peer DMA over NVLink, no SMs used) while the next
+    slab computes. Returns the full [world * rows, N] result, valid until the
+    next call with the same shape on this group. Needs one GPU per rank with
+    peer access (NVLink/NVSwitch)."""
+    import ctypes
+    import torch
+    import torch.distributed as dist
+    from . import _native
+    L = _native.lib()
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    buf = _PeerRows.get(rows, N, device, group)
+    # every rank is done with the previous result held in its buffer
+    torch.cuda.current_stream(device).synchronize()
+    dist.barrier(group=group)
+    Yv = buf.Y.view(world, rows, N)
+    comm = buf.comm
+    for r0, r1 in slab_bounds(rows, slabs):
+        compute_slab(r0, r1, Yv[rank, r0:r1])
+        ev = torch.cuda.Event()
+        ev.record()
+        comm.wait_event(ev)
+        off = (rank * rows + r0) * N * 4
+        nbytes = (r1 - r0) * N * 4
+        for p in range(world):
+            if p != rank:
+                _native.check(L.b200_memcpy_d2d_async(ctypes.c_void_p(buf.ptrs[p] + off),
+                                                      ctypes.c_void_p(buf.local + off), nbytes,
+                                                      ctypes.c_void_p(comm.cuda_stream)))
+    comm.synchronize()  # this rank's pushes have landed in every peer
+    dist.barrier(group=group)  # ... and every peer's pushes in this buffer
+    return buf.Y
+
+
+def dense_rows(X_local, W, b=None, act: int = 1, alpha: float = 0.0, *, gather: bool = False,
+               slabs: int = 4, group=None, reserve_sms: int = 8, transport: str = "ce"):
+    """Y = act(X_local @ W + b) for this rank's rows on its GPU (torch f32
+    CUDA tensors, rows of X_local contiguous), through the B200 C-ABI on the
+    current stream. gather=False returns this rank's rows (no communication);
+    gather=True returns the full result on every rank, all-gathered with NCCL
+    over NVLink slab by slab while later slabs compute (every rank must hold
+    the same number of rows). transport "ce" pushes finished slabs into the
+    peers' IPC-mapped output buffers with the copy engines (no SMs, overlaps
+    the next slab's GEMM; the result is a persistent buffer valid until the
+    next call of this shape); "nccl" all-gathers each slab with NCCL on a side
+    stream, with the GEMM's grid leaving `reserve_sms` SMs free for NCCL's
+    kernels (cap NCCL's CTAs to match, e.g. NCCL_MAX_CTAS)."""
+    import ctypes
+    import torch
+    from . import _native
+    L = _native.lib()
+    M, K = X_local.shape
+    N = W.shape[1]
+    if X_local.stride(1) != 1 or W.stride(1) != 1:
+        raise ValueError("X_local and W need contiguous rows")
+    p = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+    def compute(r0, r1, out):
+        st = ctypes.c_void_p(torch.cuda.current_stream(out.device).cuda_stream)
+        Xs = X_local[r0:r1]
+        _native.check(L.b200_dense_f32(p(Xs), Xs.stride(0), p(W), W.stride(0), p(b), p(out),
+                                       out.stride(0), r1 - r0, N, K, act, alpha, st))
+
+    if not gather:
+        Y = torch.empty((M, N), device=X_local.device, dtype=torch.float32)
+        compute(0, M, Y)
+        return Y
+    import torch.distributed as dist
+    world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+    if transport == "ce" and world > 1:
+        return gather_rows_ce(M, N, compute, slabs=slabs, group=group, device=X_local.device)
+    if transport not in ("ce", "nccl"):
+        raise ValueError(f"unknown transport {transport!r}")
+    limit = 0
+    if world > 1 and reserve_sms > 0:
+        sms = torch.cuda.get_device_properties(X_local.device).multi_processor_count
+        limit = max(1, sms - int(reserve_sms))
+    prev = L.b200_set_gemm_sm_limit(limit)
+    try:
+        return gather_rows_pipelined(M, N, compute, slabs=slabs, group=group,
+                                     device=X_local.device, dtype=torch.float32)
+    finally:
+        L.b200_set_gemm_sm_limit(max(prev, 0))

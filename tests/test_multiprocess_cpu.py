@@ -60,6 +60,33 @@ def _sharded_dense_worker(rank, world, port, errq):
         errq.put((rank, traceback.format_exc()))
 
 
+def _gather_pipelined_worker(rank, world, port, errq):
+    """Slab-pipelined all-gather of a row-sharded dense layer (the host logic
+    of dense_rows(..., gather=True)); the compute callback is the oracle."""
+    try:
+        dist = _init(rank, world, port)
+        import torch
+        import oracle
+        from mlir_edsl.sharding import gather_rows_pipelined
+        rows, N, K = 37, 20, 16  # rows per rank; 37 rows in 4 uneven slabs
+        rng = np.random.default_rng(5)
+        X = rng.uniform(-1, 1, (world * rows, K)).astype(np.float32)
+        W = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+        calls = []
+
+        def compute(r0, r1, out):
+            calls.append((r0, r1))
+            xs = X[rank * rows + r0: rank * rows + r1]
+            out.copy_(torch.from_numpy(oracle.dense_f32(xs, W, act=oracle.ACT_RELU)))
+
+        Y = gather_rows_pipelined(rows, N, compute, slabs=4, dtype=torch.float32)
+        assert calls == [(0, 10), (10, 19), (19, 28), (28, 37)], calls
+        np.testing.assert_array_equal(Y.numpy(), oracle.dense_f32(X, W, act=oracle.ACT_RELU))
+        dist.destroy_process_group()
+    except Exception:
+        errq.put((rank, traceback.format_exc()))
+
+
 def _failing_rank_worker(rank, world, port, errq):
     """Rank 1 fails before the barrier; rank 0 must learn it through a bounded
     monitored barrier instead of hanging."""
@@ -117,3 +144,20 @@ def test_sharded_dense_gloo_world2():
 def test_failed_rank_is_detected_gloo_world2():
     errs = _spawn(_failing_rank_worker)
     assert not errs, errs
+
+
+def test_slab_pipelined_gather_gloo_world2():
+    errs = _spawn(_gather_pipelined_worker)
+    assert not errs, errs
+
+
+def test_slab_bounds():
+    from mlir_edsl.sharding import slab_bounds
+    for rows in (1, 5, 37, 8192):
+        for slabs in (1, 3, 4, 100):
+            b = slab_bounds(rows, slabs)
+            assert b[0][0] == 0 and b[-1][1] == rows
+            assert all(b[i][1] == b[i + 1][0] for i in range(len(b) - 1))
+            assert all(r1 > r0 for r0, r1 in b)
+            sizes = [r1 - r0 for r0, r1 in b]
+            assert max(sizes) - min(sizes) <= 1
