@@ -417,31 +417,38 @@ def run_b200(args):
                                 reserve_sms=args.gather_reserve_sms, transport=transport)
             e1.record(stream)
             barrier()
-            return max_over_ranks(e0.elapsed_time(e1) / args.steps), Yf
+            ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+            step()
+            torch.cuda.synchronize()
+            # this rank's gathered rows against its sharded result; max over
+            # ranks so that every rank reaches the same verdict
+            err = max_over_ranks(float((Yf.view(world, M, N)[rank] - Y).abs().max()))
+            return ms, err
 
-        g_ms, Yf = gtime(args.gather_slabs)
-        step()
-        torch.cuda.synchronize()
         bound = 1e-4 * K ** 0.5 * float(X.abs().max()) * float(W.abs().max())
-        g_err = float((Yf.view(world, M, N)[rank] - Y).abs().max())
-        assert g_err <= bound, f"gathered rows differ from the sharded result: {g_err}"
-        g1_ms, Yf = gtime(1)
-        gn_ms, Yf = gtime(args.gather_slabs, "nccl")
-        gn_err = float((Yf.view(world, M, N)[rank] - Y).abs().max())
-        assert gn_err <= bound, f"NCCL-gathered rows differ from the sharded result: {gn_err}"
-        del Yf
-        recv = (world - 1) * M * N * 4
-        gathered = {"value": flops_job / (g_ms / 1e3) / 1e12, "unit": UNIT, "ms_per_step": g_ms,
-                    "slabs": args.gather_slabs, "reserve_sms": args.gather_reserve_sms,
-                    "ms_per_step_unpipelined": g1_ms,
-                    "sharded_ms_per_step": ms_total / args.steps,
-                    "recv_bytes_per_rank": recv, "recv_GBps_per_rank": recv / (g_ms / 1e3) / 1e9,
-                    "transport": "copy engines: each finished slab pushed into every peer's "
-                                 "CUDA-IPC-mapped output buffer (peer DMA over NVLink/NVSwitch) "
-                                 "on a side stream, overlapping the next slab's GEMM",
-                    "nccl_ms_per_step": gn_ms,
-                    "nccl_transport": "NCCL all_gather_into_tensor per slab on a side stream, "
-                                      "GEMM grid leaving reserve_sms SMs free"}
+        bound = -max_over_ranks(-bound)  # the tightest rank's bound, the same on every rank
+        try:
+            g_ms, g_err = gtime(args.gather_slabs)
+            g1_ms, _ = gtime(1)
+            gn_ms, gn_err = gtime(args.gather_slabs, "nccl")
+            if max(g_err, gn_err) > bound:
+                raise RuntimeError(f"gathered rows differ from the sharded result: "
+                                   f"{max(g_err, gn_err)} > {bound}")
+            recv = (world - 1) * M * N * 4
+            gathered = {
+                "value": flops_job / (g_ms / 1e3) / 1e12, "unit": UNIT, "ms_per_step": g_ms,
+                "slabs": args.gather_slabs, "reserve_sms": args.gather_reserve_sms,
+                "ms_per_step_unpipelined": g1_ms, "sharded_ms_per_step": ms_total / args.steps,
+                "recv_bytes_per_rank": recv, "recv_GBps_per_rank": recv / (g_ms / 1e3) / 1e9,
+                "transport": "copy engines: each finished slab pushed into every peer's "
+                             "CUDA-IPC-mapped output buffer (peer DMA over NVLink/NVSwitch, one "
+                             "copy stream per peer), overlapping the next slab's GEMM",
+                "nccl_ms_per_step": gn_ms,
+                "nccl_transport": "NCCL all_gather_into_tensor per slab on a side stream, GEMM "
+                                  "grid leaving reserve_sms SMs free"}
+        except RuntimeError as ex:  # raised on every rank alike (agreed collectively)
+            gathered = {"unavailable": str(ex)[:200]}
+        torch.cuda.empty_cache()
 
     # ---- headline 8192^3 dense (N=1 only)
     headline = None

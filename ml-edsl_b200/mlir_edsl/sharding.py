@@ -135,18 +135,30 @@ class _PeerRows:
             _native.check(L.b200_ipc_alloc(ctypes.byref(ptr), nbytes, handle))
         handles = [None] * world
         dist.all_gather_object(handles, handle.raw, group=group)
-        self.ptrs = []
+        self.ptrs, err = [], ""
         with torch.cuda.device(device):
             for r, h in enumerate(handles):
                 if r == rank:
                     self.ptrs.append(ptr.value)
                     continue
                 p = ctypes.c_void_p()
-                _native.check(L.b200_ipc_open(ctypes.create_string_buffer(h, 64), ctypes.byref(p)))
+                rc = L.b200_ipc_open(ctypes.create_string_buffer(h, 64), ctypes.byref(p))
+                if rc != 0:
+                    err = L.b200_last_error().decode(errors="replace")
                 self.ptrs.append(p.value)
+        # all ranks agree before any of them relies on the mappings, so that a
+        # failure on one rank fails every rank the same way (no rank is left
+        # waiting in a later collective)
+        ok = torch.tensor([0 if err else 1], device=device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if not int(ok.item()):
+            raise RuntimeError("CUDA IPC mapping of the peers' output buffers failed"
+                               + (f": {err}" if err else " on another rank"))
         self.local = ptr.value
         self.Y = torch.as_tensor(_DeviceArray(ptr.value, (world * rows, N)), device=device)
-        self.comm = torch.cuda.Stream(device=device)
+        # one copy stream per peer, so that the copy engines move the pushes
+        # to different peers in parallel
+        self.comm = [torch.cuda.Stream(device=device) for _ in range(world)]
 
 
 def gather_rows_ce(rows: int, N: int, compute_slab, *, slabs: int = 4, group=None, device=None):
@@ -168,20 +180,21 @@ def gather_rows_ce(rows: int, N: int, compute_slab, *, slabs: int = 4, group=Non
     torch.cuda.current_stream(device).synchronize()
     dist.barrier(group=group)
     Yv = buf.Y.view(world, rows, N)
-    comm = buf.comm
     for r0, r1 in slab_bounds(rows, slabs):
         compute_slab(r0, r1, Yv[rank, r0:r1])
         ev = torch.cuda.Event()
         ev.record()
-        comm.wait_event(ev)
         off = (rank * rows + r0) * N * 4
         nbytes = (r1 - r0) * N * 4
         for p in range(world):
             if p != rank:
+                buf.comm[p].wait_event(ev)
                 _native.check(L.b200_memcpy_d2d_async(ctypes.c_void_p(buf.ptrs[p] + off),
                                                       ctypes.c_void_p(buf.local + off), nbytes,
-                                                      ctypes.c_void_p(comm.cuda_stream)))
-    comm.synchronize()  # this rank's pushes have landed in every peer
+                                                      ctypes.c_void_p(buf.comm[p].cuda_stream)))
+    for p in range(world):  # this rank's pushes have landed in every peer
+        if p != rank:
+            buf.comm[p].synchronize()
     dist.barrier(group=group)  # ... and every peer's pushes in this buffer
     return buf.Y
 
