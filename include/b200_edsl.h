@@ -209,6 +209,19 @@ int b200_dot_i32(const int32_t* a, const int32_t* b, int64_t n, int32_t* out, vo
 int b200_selftest_wait_timeout(int64_t limit_ns, void* stream);
 int b200_debug_fail_alloc(int n);
 
+/* b200_dense_f32_chain: b200_dense_f32 for stacked layers kept on the
+ * device. Xlo (optional): X's tf32 lo part with row pitch roundup(K, 4), as
+ * the previous layer wrote it to its Ylo, so that X is not split again (X and
+ * Xlo rows 16-byte aligned). Ylo (optional, pitch ldylo >= N): the epilogue
+ * also stores the tf32 lo part of Y (after bias and activation) for the next
+ * layer. The results equal b200_dense_f32's bit for bit. Replaces the
+ * reference's per-layer host round trips of stacked dense nets
+ * (tests/linalg/test_binary_op_execution.py:223-268); no direct counterpart. */
+int b200_dense_f32_chain(const float* X, int64_t ldx, const float* Xlo, const float* W,
+                         int64_t ldw, const float* b, float* Y, int64_t ldy, float* Ylo,
+                         int64_t ldylo, int64_t M, int64_t N, int64_t K, int act, float alpha,
+                         void* stream);
+
 /* Cross-process device buffers for the all-gather of a row-sharded result:
  * b200_ipc_alloc allocates `bytes` on the current device and writes its
  * 64-byte CUDA IPC handle to handle_out; another rank maps it with

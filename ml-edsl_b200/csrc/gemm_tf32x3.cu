@@ -341,7 +341,30 @@ struct Epilogue {
   float alpha;
   int vec_out;  // Y base 16-byte aligned and ldy % 4 == 0
   float* part;  // cut tiles: raw partial sums, tile-local [piece][r][BM][kBN]
+  float* Ylo;   // optional: the tf32 lo part of each final value (the next
+  int64_t ldylo;  // layer's pre-split A_lo), pitch ldylo
 };
+
+// Final values v[0..3] at (row, col..col+3): Y, and when requested the lo
+// part that the next layer's GEMM reads as A_lo.
+__device__ __forceinline__ void store_lo4(const Epilogue& ep, int64_t row, int64_t col,
+                                          const float (&v)[4]) {
+  float lo[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float h;
+    tf32_split(v[q], h, lo[q]);
+  }
+  float* d = ep.Ylo + row * ep.ldylo + col;
+  if ((ep.ldylo & 3) == 0 && ((reinterpret_cast<uintptr_t>(ep.Ylo) & 15) == 0) &&
+      col + 4 <= ep.N) {
+    *reinterpret_cast<float4*>(d) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (col + q < ep.N) d[q] = lo[q];
+  }
+}
 
 // Stores one epilogue thread's 128 consecutive accumulator columns of a unit:
 // tile-local row `lr`, columns [lc0, lc0 + 128). A whole tile's row gets bias,
@@ -378,6 +401,10 @@ __device__ __forceinline__ void store_tile_row(const Epilogue& ep, const Unit& w
       if (col0 + j + 1 < ep.N) dst[j + 1] = v1;
       if (col0 + j + 2 < ep.N) dst[j + 2] = v2;
       if (col0 + j + 3 < ep.N) dst[j + 3] = v3;
+    }
+    if (ep.Ylo && col0 + j < ep.N) {
+      const float v[4] = {v0, v1, v2, v3};
+      store_lo4(ep, row, col0 + j, v);
     }
   }
 }
@@ -1279,7 +1306,8 @@ static int dispatch_gemm(const float* xa, const float* xlo, int64_t ldx, bool fu
 static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool fused,
                             const BOp& bop, int64_t M, int64_t N, int64_t K, const float* bias,
                             float* Y, int64_t ldy, int act, float alpha, int splits,
-                            float* partials, int* status, cudaStream_t stream);
+                            float* partials, int* status, cudaStream_t stream,
+                            float* ylo = nullptr, int64_t ldylo = 0);
 
 int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
                          const float* wloT, int64_t M, int64_t N, int64_t K, const float* bias,
@@ -1324,7 +1352,7 @@ int choose_splits(int64_t M, int64_t N, int64_t K) {
 __global__ void __launch_bounds__(256)
     piece_reduce_kernel(const float* __restrict__ part, Sched sc, int tile_m, int64_t M,
                         int64_t N, const float* __restrict__ bias, int act, float alpha,
-                        float* __restrict__ Y, int64_t ldy, int vec) {
+                        float* __restrict__ Y, int64_t ldy, int vec, Epilogue lo_ep) {
   pdl_wait();  // launched as a programmatic dependent of the GEMM
   const int64_t tile_elems = (int64_t)tile_m * kBN;
   const int64_t quads_per_tile = tile_elems / 4;
@@ -1359,6 +1387,7 @@ __global__ void __launch_bounds__(256)
       for (int q = 0; q < 4; ++q)
         if (col + q < N) dst[q] = v[q];
     }
+    if (lo_ep.Ylo) store_lo4(lo_ep, row, col, v);
   }
 }
 
@@ -1381,7 +1410,8 @@ int64_t splitk_partials_bytes(int64_t M, int64_t N, int64_t K) {
 static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool fused,
                             const BOp& bop, int64_t M, int64_t N, int64_t K, const float* bias,
                             float* Y, int64_t ldy, int act, float alpha, int splits,
-                            float* partials, int* status, cudaStream_t stream) {
+                            float* partials, int* status, cudaStream_t stream, float* ylo,
+                            int64_t ldylo) {
   const bool pair = use_pair(fused, bop);
   const Sched sc = sched_f32(M, N, K, pair, pair ? PairCfg::BK : default_bk(),
                              splits > 1 && partials != nullptr);
@@ -1395,6 +1425,8 @@ static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool
   ep.alpha = alpha;
   ep.vec_out = ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(Y) & 15) == 0);
   ep.part = partials;
+  ep.Ylo = ylo;
+  ep.ldylo = ldylo;
   int rc = dispatch_gemm(xa, xlo, ldx, fused, bop, M, N, K, sc, ep, status, stream);
   if (rc != kOk || sc.rest == 0) return rc;
   const int tile_m = pair ? kPairBM : kBM;
@@ -1403,7 +1435,7 @@ static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool
   const cudaError_t e = launch_dependent(pdl_enabled(M, N, K), piece_reduce_kernel,
                                          (unsigned)blocks, 256, 0, stream,
                                          static_cast<const float*>(partials), sc, tile_m, M, N,
-                                         bias, act, alpha, Y, ldy, ep.vec_out);
+                                         bias, act, alpha, Y, ldy, ep.vec_out, ep);
   count_launch();
   return e == cudaSuccess ? kOk : kErrCuda;
 }
@@ -1411,9 +1443,9 @@ static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool
 int gemm_tf32x3_splitk(const float* xhi, const float* xlo, const float* whiT, const float* wloT,
                        int64_t M, int64_t N, int64_t K, const float* bias, float* Y, int64_t ldy,
                        int act, float alpha, int splits, float* partials, int* status,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, float* ylo, int64_t ldylo) {
   return gemm_with_splits(xhi, xlo, (K + 3) & ~int64_t(3), false, bop_k(whiT, wloT, K), M, N, K,
-                          bias, Y, ldy, act, alpha, splits, partials, status, stream);
+                          bias, Y, ldy, act, alpha, splits, partials, status, stream, ylo, ldylo);
 }
 
 int split_xw_f32(const float* X, int64_t ldx, int64_t M, const float* W, int64_t ldw,
@@ -1444,10 +1476,10 @@ int split_x_lo_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xlo
 int gemm_tf32x3_xraw(const float* X, int64_t ldx, const float* xlo, const float* whiT,
                      const float* wloT, int64_t M, int64_t N, int64_t K, const float* bias,
                      float* Y, int64_t ldy, int act, float alpha, int splits, float* partials,
-                     int* status, cudaStream_t stream) {
+                     int* status, cudaStream_t stream, float* ylo, int64_t ldylo) {
   if (!fused_a_ok(X, ldx)) return kErrInvalidArg;
   return gemm_with_splits(X, xlo, ldx, false, bop_k(whiT, wloT, K), M, N, K, bias, Y, ldy, act,
-                          alpha, splits, partials, status, stream);
+                          alpha, splits, partials, status, stream, ylo, ldylo);
 }
 
 bool fused_a_ok(const float* X, int64_t ldx) {
@@ -1457,10 +1489,10 @@ bool fused_a_ok(const float* X, int64_t ldx) {
 int gemm_tf32x3_fused(const float* X, int64_t ldx, const float* whiT, const float* wloT,
                       int64_t M, int64_t N, int64_t K, const float* bias, float* Y, int64_t ldy,
                       int act, float alpha, int splits, float* partials, int* status,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, float* ylo, int64_t ldylo) {
   if (!fused_a_ok(X, ldx)) return kErrInvalidArg;
   return gemm_with_splits(X, nullptr, ldx, true, bop_k(whiT, wloT, K), M, N, K, bias, Y, ldy, act,
-                          alpha, splits, partials, status, stream);
+                          alpha, splits, partials, status, stream, ylo, ldylo);
 }
 
 // ---------------------------------------------------------------------------
@@ -1508,11 +1540,11 @@ int split_lo_xw_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xh
 int gemm_tf32x3_wmn(const float* xa, const float* xlo, int64_t ldx, const float* W, int64_t ldw,
                     const float* wlo, int64_t M, int64_t N, int64_t K, const float* bias,
                     float* Y, int64_t ldy, int act, float alpha, int splits, float* partials,
-                    int* status, cudaStream_t stream) {
+                    int* status, cudaStream_t stream, float* ylo, int64_t ldylo) {
   if (!fused_a_ok(xa, ldx) || !w_mn_ok(W, ldw, M, N)) return kErrInvalidArg;
   const BOp b{W, wlo, ldw, (N + 3) & ~int64_t(3), true};  // wlo == nullptr: derived in-kernel
   return gemm_with_splits(xa, xlo, ldx, false, b, M, N, K, bias, Y, ldy, act, alpha, splits,
-                          partials, status, stream);
+                          partials, status, stream, ylo, ldylo);
 }
 
 }  // namespace b200

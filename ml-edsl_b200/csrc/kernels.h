@@ -48,7 +48,7 @@ int64_t splitk_partials_bytes(int64_t M, int64_t N, int64_t K);
 int gemm_tf32x3_splitk(const float* xhi, const float* xlo, const float* whiT, const float* wloT,
                        int64_t M, int64_t N, int64_t K, const float* bias, float* Y, int64_t ldy,
                        int act, float alpha, int splits, float* partials, int* status,
-                       cudaStream_t stream);
+                       cudaStream_t stream, float* ylo = nullptr, int64_t ldylo = 0);
 // Both splits in one launch: X -> (xhi,) xlo (xhi == nullptr: lo only) and
 // W -> whiT, wloT.
 int split_xw_f32(const float* X, int64_t ldx, int64_t M, const float* W, int64_t ldw,
@@ -59,10 +59,13 @@ int split_xw_f32(const float* X, int64_t ldx, int64_t M, const float* W, int64_t
 // writes only the lo part [M, Kp]; the GEMM reads X itself as the hi part.
 int split_x_lo_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xlo,
                    cudaStream_t stream);
+// ylo (optional, pitch ldylo): the epilogue also stores the tf32 lo part of
+// every final value, i.e. the next layer's pre-split A_lo.
 int gemm_tf32x3_xraw(const float* X, int64_t ldx, const float* xlo, const float* whiT,
                      const float* wloT, int64_t M, int64_t N, int64_t K, const float* bias,
                      float* Y, int64_t ldy, int act, float alpha, int splits, float* partials,
-                     int* status, cudaStream_t stream);
+                     int* status, cudaStream_t stream, float* ylo = nullptr,
+                     int64_t ldylo = 0);
 
 // MN-major B operand: the GEMM reads the row-major W itself as B_hi and a
 // row-major lo part W_lo [K, Np] (Np = roundup(N, 4)) as B_lo. w_mn_ok:
@@ -80,7 +83,8 @@ bool w_lo_in_kernel();
 int gemm_tf32x3_wmn(const float* xa, const float* xlo, int64_t ldx, const float* W, int64_t ldw,
                     const float* wlo, int64_t M, int64_t N, int64_t K, const float* bias,
                     float* Y, int64_t ldy, int act, float alpha, int splits, float* partials,
-                    int* status, cudaStream_t stream);
+                    int* status, cudaStream_t stream, float* ylo = nullptr,
+                    int64_t ldylo = 0);
 
 // Fused A split: raw X (pitch ldx, 16-byte aligned rows: fused_a_ok) is
 // split to tf32 hi/lo inside the GEMM; W pre-split as whiT/wloT.
@@ -88,7 +92,7 @@ bool fused_a_ok(const float* X, int64_t ldx);
 int gemm_tf32x3_fused(const float* X, int64_t ldx, const float* whiT, const float* wloT,
                       int64_t M, int64_t N, int64_t K, const float* bias, float* Y, int64_t ldy,
                       int act, float alpha, int splits, float* partials, int* status,
-                      cudaStream_t stream);
+                      cudaStream_t stream, float* ylo = nullptr, int64_t ldylo = 0);
 int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
                          const float* wloT, int64_t M, int64_t N, int64_t K, const float* bias,
                          float* Y, int64_t ldy, int act, float alpha, int* status,

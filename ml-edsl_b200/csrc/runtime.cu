@@ -417,19 +417,26 @@ bool fuse_a(const float* X, int64_t ldx) {
   return enabled && fused_a_ok(X, ldx);
 }
 
+// xlo_in (optional): X's tf32 lo part, pitch roundup(K, 4), from the previous
+// layer's epilogue (X rows must then be 16-byte aligned: X itself is A_hi),
+// so X is not split again. ylo (optional, pitch ldylo): the epilogue also
+// writes the lo part of Y for the next layer.
 int dense_device(DeviceCtx* c, const float* X, int64_t ldx, const float* W, int64_t ldw,
                  const float* b, float* Y, int64_t ldy, int64_t M, int64_t N, int64_t K, int act,
-                 float alpha, void* ws, cudaStream_t st) {
+                 float alpha, void* ws, cudaStream_t st, const float* xlo_in = nullptr,
+                 float* ylo = nullptr, int64_t ldylo = 0) {
   if (M == 0 || N == 0) return kOk;
   if (K == 0) return fill_bias_act_f32(b, Y, ldy, M, N, act, alpha, st);
   SplitBufs s = carve(ws, M, N, K);
   const int splits = choose_splits(M, N, K);
+  const int64_t Kp = (K + 3) & ~int64_t(3);
+  float* xlo = xlo_in ? const_cast<float*>(xlo_in) : s.xlo;
   int rc;
-  if (fuse_a(X, ldx)) {
+  if (fuse_a(X, ldx) && !xlo_in) {
     rc = split_w_f32(W, ldw, K, N, s.whi, s.wlo, st);
     if (rc == kOk)
       rc = gemm_tf32x3_fused(X, ldx, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha, splits,
-                             s.partials, c->status, st);
+                             s.partials, c->status, st, ylo, ldylo);
   } else if (w_mn_ok(W, ldw, M, N) &&
              w_lo_mn_bytes(K, N) <= reinterpret_cast<char*>(s.partials) -
                                         reinterpret_cast<char*>(s.whi)) {
@@ -437,25 +444,28 @@ int dense_device(DeviceCtx* c, const float* X, int64_t ldx, const float* W, int6
     // W split region. X likewise when its rows are 16-byte aligned.
     const bool xraw = fused_a_ok(X, ldx);
     float* wlo = w_lo_in_kernel() ? nullptr : s.whi;
-    if (wlo)
+    if (xlo_in)  // X is pre-split: W alone, if anything
+      rc = wlo ? split_lo_xw_f32(nullptr, 0, 0, K, nullptr, nullptr, W, ldw, N, wlo, st) : kOk;
+    else if (wlo)
       rc = split_lo_xw_f32(X, ldx, M, K, xraw ? nullptr : s.xhi, s.xlo, W, ldw, N, wlo, st);
     else
       rc = xraw ? split_x_lo_f32(X, ldx, M, K, s.xlo, st)
                 : split_x_f32(X, ldx, M, K, s.xhi, s.xlo, st);
     if (rc == kOk)
-      rc = gemm_tf32x3_wmn(xraw ? X : s.xhi, s.xlo, xraw ? ldx : (K + 3) & ~int64_t(3), W, ldw,
-                           wlo, M, N, K, b, Y, ldy, act, alpha, splits, s.partials, c->status,
-                           st);
+      rc = gemm_tf32x3_wmn(xraw ? X : s.xhi, xlo, xraw ? ldx : Kp, W, ldw, wlo, M, N, K, b, Y,
+                           ldy, act, alpha, splits, s.partials, c->status, st, ylo, ldylo);
   } else if (fused_a_ok(X, ldx)) {  // X is the hi part; only lo is written
-    rc = split_xw_f32(X, ldx, M, W, ldw, K, N, nullptr, s.xlo, s.whi, s.wlo, st);
+    rc = xlo_in ? split_w_f32(W, ldw, K, N, s.whi, s.wlo, st)
+                : split_xw_f32(X, ldx, M, W, ldw, K, N, nullptr, s.xlo, s.whi, s.wlo, st);
     if (rc == kOk)
-      rc = gemm_tf32x3_xraw(X, ldx, s.xlo, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha, splits,
-                            s.partials, c->status, st);
+      rc = gemm_tf32x3_xraw(X, ldx, xlo, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha, splits,
+                            s.partials, c->status, st, ylo, ldylo);
   } else {
+    if (xlo_in) return fail(kErrInvalidArg, "a pre-split X needs 16-byte aligned X rows");
     rc = split_xw_f32(X, ldx, M, W, ldw, K, N, s.xhi, s.xlo, s.whi, s.wlo, st);
     if (rc == kOk)
       rc = gemm_tf32x3_splitk(s.xhi, s.xlo, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha, splits,
-                              s.partials, c->status, st);
+                              s.partials, c->status, st, ylo, ldylo);
   }
   if (rc != kOk) return fail(rc, std::string("dense_f32 launch failed: ") +
                                      cudaGetErrorString(cudaGetLastError()));
@@ -922,6 +932,35 @@ int b200_dense_f32(const float* X, int64_t ldx, const float* W, int64_t ldw, con
     ws = buf.p;
   }
   rc = dense_device(c, X, ldx, W, ldw, b, Y, ldy, M, N, K, act, alpha, ws, st);
+  return rc ? rc : succeed();
+}
+
+int b200_dense_f32_chain(const float* X, int64_t ldx, const float* Xlo, const float* W,
+                         int64_t ldw, const float* b, float* Y, int64_t ldy, float* Ylo,
+                         int64_t ldylo, int64_t M, int64_t N, int64_t K, int act, float alpha,
+                         void* stream) {
+  int rc = validate_dense(X, ldx, W, ldw, Y, ldy, M, N, K, act);
+  if (rc) return rc;
+  if (Xlo && (!fused_a_ok(X, ldx) || (reinterpret_cast<uintptr_t>(Xlo) & 15) != 0))
+    return fail(kErrInvalidArg, "a pre-split X needs 16-byte aligned X and Xlo rows");
+  if (Ylo && ldylo < N) return fail(kErrInvalidArg, "Ylo pitch < N");
+  if (Ylo && K == 0) return fail(kErrInvalidArg, "Ylo needs K > 0");
+  DeviceCtx* c = nullptr;
+  if ((rc = current_ctx(&c))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* ws = nullptr;
+  if (M > 0 && N > 0 && K > 0) {
+    const size_t need = (size_t)dense_scratch_bytes(M, N, K);
+    std::lock_guard<std::mutex> lk(g_mu);
+    DevBuf& buf = c->scratch[st];
+    if (buf.n < need) {
+      // The old buffer may still be read by queued work on this stream.
+      B200_CUDA(cudaStreamSynchronize(st), "sync before scratch growth");
+      B200_CUDA(buf.reserve(need), "alloc scratch");
+    }
+    ws = buf.p;
+  }
+  rc = dense_device(c, X, ldx, W, ldw, b, Y, ldy, M, N, K, act, alpha, ws, st, Xlo, Ylo, ldylo);
   return rc ? rc : succeed();
 }
 

@@ -243,6 +243,12 @@ class B200Backend:
                 _native.check(L.b200_memcpy_h2d(p, a.ctypes.data_as(ctypes.c_void_p), a.nbytes))
                 dparams[i] = p
             douts = []
+            # f32 GEMM outputs that a later f32 GEMM reads as its A operand:
+            # their epilogue also writes the tf32 lo part, so that the next
+            # layer does not split them again (b200_dense_f32_chain)
+            feeds_a = {st.inputs[0].index for st in plan.steps
+                       if st.op == "gemm_f32" and st.inputs[0].kind == "step"}
+            lo_of = {}
 
             def dref(r: Ref):
                 return dparams[r.index] if r.kind == "param" else douts[r.index]
@@ -260,8 +266,19 @@ class B200Backend:
                     N = shape_of(b)[1]
                     bias = dref(s.inputs[2]) if s.has_bias else None
                     if s.op == "gemm_f32":
-                        _native.check(L.b200_dense_f32(dref(a), K, dref(b), N, bias, out, N, M, N,
-                                                       K, s.act, s.alpha, None))
+                        me = len(douts) - 1
+                        ylo = dmalloc(M * N * 4) if (me in feeds_a and N % 4 == 0 and K > 0) \
+                            else None
+                        xlo = lo_of.get(a.index) if a.kind == "step" else None
+                        if ylo is not None or xlo is not None:
+                            _native.check(L.b200_dense_f32_chain(
+                                dref(a), K, xlo, dref(b), N, bias, out, N, ylo,
+                                N if ylo is not None else 0, M, N, K, s.act, s.alpha, None))
+                            if ylo is not None:
+                                lo_of[me] = ylo
+                        else:
+                            _native.check(L.b200_dense_f32(dref(a), K, dref(b), N, bias, out, N,
+                                                           M, N, K, s.act, s.alpha, None))
                     else:
                         _native.check(L.b200_matmul_i32(dref(a), K, dref(b), N, bias, out, N, M,
                                                         N, K, None))

@@ -551,3 +551,41 @@ def test_inf_and_nan_inputs_follow_f32(cuda, M, N, K):
     assert np.isinf(ref).any() and np.isnan(ref).any()
     Xf, Wf = np.nan_to_num(X, posinf=0, neginf=0), np.nan_to_num(W, posinf=0, neginf=0)
     assert max_err(got[fin], ref[fin]) <= oracle.f32_bound(K, Xf, Wf)
+
+
+@pytest.mark.parametrize("M,K,N1,N2", [(300, 1001, 512, 256), (5000, 512, 260, 128),
+                                       (129, 256, 1024, 64), (64, 96, 4, 32)])
+def test_chained_layers_match_separate_calls(cuda, M, K, N1, N2):
+    """b200_dense_f32_chain: layer 1's epilogue also stores H's tf32 lo part,
+    and layer 2 reads it instead of splitting H again. H, the lo part and Y
+    equal the unchained calls and a separate split of H bit for bit, across
+    the MN-major and K-major B paths, an unaligned first-layer X (K odd: full
+    split), a 4-column layer and cut tiles (lo written by the piece
+    reduction)."""
+    import torch
+    dev = torch.device("cuda:0")
+    L = _native.lib()
+    s = stream_ptr(torch)
+    X, W1, b1 = _inputs(M, N1, K, seed=M + K)
+    _, W2, b2 = _inputs(M, N2, N1, seed=N1 + N2)
+    tX, tW1, tb1, tW2, tb2 = (torch.from_numpy(a).to(dev) for a in (X, W1, b1, W2, b2))
+    H, Hlo = torch.empty((M, N1), device=dev), torch.full((M, N1), np.nan, device=dev)
+    Y = torch.empty((M, N2), device=dev)
+    _native.check(L.b200_dense_f32_chain(ptr(tX), K, None, ptr(tW1), N1, ptr(tb1), ptr(H), N1,
+                                         ptr(Hlo), N1, M, N1, K, 1, 0.0, s))
+    _native.check(L.b200_dense_f32_chain(ptr(H), N1, ptr(Hlo), ptr(tW2), N2, ptr(tb2), ptr(Y),
+                                         N2, None, 0, M, N2, N1, 1, 0.0, s))
+    H2, Y2 = torch.empty_like(H), torch.empty_like(Y)
+    _native.check(L.b200_dense_f32(ptr(tX), K, ptr(tW1), N1, ptr(tb1), ptr(H2), N1, M, N1, K,
+                                   1, 0.0, s))
+    _native.check(L.b200_dense_f32(ptr(H2), N1, ptr(tW2), N2, ptr(tb2), ptr(Y2), N2, M, N2, N1,
+                                   1, 0.0, s))
+    hhi, hlo = torch.empty_like(H), torch.empty_like(H)
+    _native.check(L.b200_tf32_split_rows(ptr(H2), N1, M, N1, ptr(hhi), ptr(hlo), s))
+    _native.check(L.b200_stream_sync(s))
+    np.testing.assert_array_equal(H.cpu().numpy(), H2.cpu().numpy())
+    np.testing.assert_array_equal(Hlo.cpu().numpy(), hlo.cpu().numpy())
+    np.testing.assert_array_equal(Y.cpu().numpy(), Y2.cpu().numpy())
+    if K % 4:  # a pre-split X needs aligned X rows: rejected before any launch
+        assert L.b200_dense_f32_chain(ptr(tX), K, ptr(Hlo), ptr(tW1), N1, None, ptr(H), N1,
+                                      None, 0, M, N1, K, 0, 0.0, s) == 1
