@@ -79,7 +79,9 @@ struct RingCfg {
   static constexpr uint32_t SBO = 8 * BK * 4;  // 8-row core-matrix group stride
   static constexpr int BarOffset = Stages * StageBytes;
   static constexpr int BiasOffset = BarOffset + 256;
-  static constexpr int SmemBytes = BiasOffset + kBN * 4 + 1024;  // + alignment slack
+  // epilogue store staging: 4 KB (32 rows x 32 floats) per epilogue warp
+  static constexpr int StoreStageOffset = BiasOffset + kBN * 4;
+  static constexpr int SmemBytes = StoreStageOffset + kEpiWarps * 4096 + 1024;  // + align slack
   static_assert(BK == 32 || BK == 16, "BK must be 32 (SW128) or 16 (SW64)");
   static_assert(SmemBytes <= 232448, "shared memory over the sm_100 limit");
 };
@@ -343,6 +345,7 @@ struct Epilogue {
   float* part;  // cut tiles: raw partial sums, tile-local [piece][r][BM][kBN]
   float* Ylo;   // optional: the tf32 lo part of each final value (the next
   int64_t ldylo;  // layer's pre-split A_lo), pitch ldylo
+  int stage_store;  // 1: coalesce the epilogue's stores through shared memory
 };
 
 // Final values v[0..3] at (row, col..col+3): Y, and when requested the lo
@@ -369,19 +372,78 @@ __device__ __forceinline__ void store_lo4(const Epilogue& ep, int64_t row, int64
 // Stores one epilogue thread's 128 consecutive accumulator columns of a unit:
 // tile-local row `lr`, columns [lc0, lc0 + 128). A whole tile's row gets bias,
 // activation and the M / N bounds and goes to Y; a piece's raw sums go to its
-// tile-local partial buffer (whole rows, 16-byte stores).
+// tile-local partial buffer.
+//
+// Coalescing. A thread owns one row, so a direct float4 store per thread
+// scatters each warp instruction over 32 rows (16 bytes each). With `stage`
+// (4 KB of shared memory per warp) the warp instead passes 32 x 32 blocks
+// through shared memory: every thread writes its row's 32 values (16-byte
+// chunks XOR-swizzled by row, conflict-free both ways), then the warp reads
+// them back transposed so that each store instruction writes four whole
+// 128-byte row segments. A warp whose 32 x 128 region is cut by the M / N
+// edges, unaligned Y and the Ylo output keep the per-thread stores.
 template <int kTileM>
 __device__ __forceinline__ void store_tile_row(const Epilogue& ep, const Unit& w, int rest,
-                                               int lr, int lc0, const float (&acc)[128]) {
+                                               int lr, int lc0, const float (&acc)[128],
+                                               float* stage, int lane) {
+  const int lr0 = lr - lane;  // the warp's first row
   if (w.piece >= 0) {
-    float* dst = ep.part + ((int64_t)(w.piece * rest + w.r) * kTileM + lr) * kBN + lc0;
+    float* tile = ep.part + (int64_t)(w.piece * rest + w.r) * kTileM * kBN;
+    if (stage) {
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) {
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch)
+          *reinterpret_cast<float4*>(stage + lane * 32 + ((ch ^ (lane & 7)) << 2)) =
+              make_float4(acc[cb * 32 + ch * 4], acc[cb * 32 + ch * 4 + 1],
+                          acc[cb * 32 + ch * 4 + 2], acc[cb * 32 + ch * 4 + 3]);
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int r = k * 4 + (lane >> 3), ch = lane & 7;
+          *reinterpret_cast<float4*>(tile + (int64_t)(lr0 + r) * kBN + lc0 + cb * 32 + ch * 4) =
+              *reinterpret_cast<const float4*>(stage + r * 32 + ((ch ^ (r & 7)) << 2));
+        }
+        __syncwarp();
+      }
+      return;
+    }
+    float* dst = tile + (int64_t)lr * kBN + lc0;
 #pragma unroll
     for (int j = 0; j < 128; j += 4)
       *reinterpret_cast<float4*>(dst + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
     return;
   }
   const int64_t row = (int64_t)w.m0 + lr;
+  const int64_t row0 = (int64_t)w.m0 + lr0;
   const int64_t col0 = (int64_t)w.n0 + lc0;
+  // warp-uniform: the warp's whole 32 x 128 region lies inside Y
+  if (stage != nullptr && ep.vec_out && ep.Ylo == nullptr && row0 + 32 <= ep.M &&
+      col0 + 128 <= ep.N) {
+#pragma unroll
+    for (int cb = 0; cb < 4; ++cb) {
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        const int c = cb * 32 + ch * 4;
+        float v[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          v[q] = apply_act(acc[c + q] + (ep.bias != nullptr ? __ldg(ep.bias + col0 + c + q) : 0.0f),
+                           ep.act, ep.alpha);
+        *reinterpret_cast<float4*>(stage + lane * 32 + ((ch ^ (lane & 7)) << 2)) =
+            make_float4(v[0], v[1], v[2], v[3]);
+      }
+      __syncwarp();
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int r = k * 4 + (lane >> 3), ch = lane & 7;
+        *reinterpret_cast<float4*>(ep.Y + (row0 + r) * ep.ldy + col0 + cb * 32 + ch * 4) =
+            *reinterpret_cast<const float4*>(stage + r * 32 + ((ch ^ (r & 7)) << 2));
+      }
+      __syncwarp();
+    }
+    return;
+  }
   if (row >= ep.M) return;
   float* dst = ep.Y + row * ep.ldy + col0;
 #pragma unroll
@@ -773,7 +835,12 @@ __global__ void __launch_bounds__(kThreads + (kFuseB ? 32 * kConvWarps : 0), 1)
       if (!ok || *abort_flag) break;
       // The MMAs of the next unit proceed into the two TMEM buffers while
       // this tile is stored.
-      store_tile_row<kBM>(ep, w, sc.rest, quarter * 32 + lane, half * 128, acc);
+      store_tile_row<kBM>(
+          ep, w, sc.rest, quarter * 32 + lane, half * 128, acc,
+          ep.stage_store
+              ? reinterpret_cast<float*>(smem + Cfg::StoreStageOffset + (warp - 2) * 4096)
+              : nullptr,
+          lane);
     }
   }
 
@@ -968,7 +1035,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
       if (!ok || *abort_flag) break;
       store_tile_row<kPairBM>(ep, w, sc.rest, (int)rank * 128 + quarter * 32 + lane,
-                              half * 128, acc);
+                              half * 128, acc, nullptr, lane);
     }
   }
 
@@ -1156,6 +1223,18 @@ static int ring_variant() {
 // multiply-adds (2048^3): there the launch and prologue latency it hides is
 // 10-20% of a call (dense 1024^3: 31.0 -> 26.9 us; 256^3: 22.7 -> 18.6 us);
 // for long GEMMs it gained nothing measurable. B200_PDL=0 turns it off.
+static bool pdl_enabled(int64_t M, int64_t N, int64_t K);
+
+// The epilogue's stores go through shared memory (store_tile_row) unless
+// B200_STORE_STAGE=0 (per-thread row stores, for A/B measurements).
+static bool store_staging_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("B200_STORE_STAGE");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 static bool pdl_enabled(int64_t M, int64_t N, int64_t K) {
   static const bool on = [] {
     const char* e = getenv("B200_PDL");
@@ -1427,6 +1506,7 @@ static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool
   ep.part = partials;
   ep.Ylo = ylo;
   ep.ldylo = ldylo;
+  ep.stage_store = store_staging_enabled() ? 1 : 0;
   int rc = dispatch_gemm(xa, xlo, ldx, fused, bop, M, N, K, sc, ep, status, stream);
   if (rc != kOk || sc.rest == 0) return rc;
   const int tile_m = pair ? kPairBM : kBM;
