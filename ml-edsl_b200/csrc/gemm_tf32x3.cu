@@ -346,7 +346,19 @@ struct Epilogue {
   float* Ylo;   // optional: the tf32 lo part of each final value (the next
   int64_t ldylo;  // layer's pre-split A_lo), pitch ldylo
   int stage_store;  // 1: coalesce the epilogue's stores through shared memory
+  int bias_vec;     // bias non-null and 16-byte aligned: float4 bias loads
 };
+
+// Bias of columns c .. c+3 (c a multiple of 4 from a 16-byte aligned tile
+// origin), zeros without bias. Every lane of a warp loads the same values.
+__device__ __forceinline__ float4 bias4(const Epilogue& ep, int64_t c) {
+  if (ep.bias_vec) return __ldg(reinterpret_cast<const float4*>(ep.bias + c));
+  if (ep.bias == nullptr) return make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  return make_float4(c < ep.N ? __ldg(ep.bias + c) : 0.0f,
+                     c + 1 < ep.N ? __ldg(ep.bias + c + 1) : 0.0f,
+                     c + 2 < ep.N ? __ldg(ep.bias + c + 2) : 0.0f,
+                     c + 3 < ep.N ? __ldg(ep.bias + c + 3) : 0.0f);
+}
 
 // Final values v[0..3] at (row, col..col+3): Y, and when requested the lo
 // part that the next layer's GEMM reads as A_lo.
@@ -425,13 +437,12 @@ __device__ __forceinline__ void store_tile_row(const Epilogue& ep, const Unit& w
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {
         const int c = cb * 32 + ch * 4;
-        float v[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          v[q] = apply_act(acc[c + q] + (ep.bias != nullptr ? __ldg(ep.bias + col0 + c + q) : 0.0f),
-                           ep.act, ep.alpha);
+        const float4 bv = bias4(ep, col0 + c);
         *reinterpret_cast<float4*>(stage + lane * 32 + ((ch ^ (lane & 7)) << 2)) =
-            make_float4(v[0], v[1], v[2], v[3]);
+            make_float4(apply_act(acc[c] + bv.x, ep.act, ep.alpha),
+                        apply_act(acc[c + 1] + bv.y, ep.act, ep.alpha),
+                        apply_act(acc[c + 2] + bv.z, ep.act, ep.alpha),
+                        apply_act(acc[c + 3] + bv.w, ep.act, ep.alpha));
       }
       __syncwarp();
 #pragma unroll
@@ -448,14 +459,19 @@ __device__ __forceinline__ void store_tile_row(const Epilogue& ep, const Unit& w
   float* dst = ep.Y + row * ep.ldy + col0;
 #pragma unroll
   for (int j = 0; j < 128; j += 4) {
-    float bb[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-      bb[q] = (ep.bias != nullptr && col0 + j + q < ep.N) ? __ldg(ep.bias + col0 + j + q) : 0.0f;
-    const float v0 = apply_act(acc[j] + bb[0], ep.act, ep.alpha);
-    const float v1 = apply_act(acc[j + 1] + bb[1], ep.act, ep.alpha);
-    const float v2 = apply_act(acc[j + 2] + bb[2], ep.act, ep.alpha);
-    const float v3 = apply_act(acc[j + 3] + bb[3], ep.act, ep.alpha);
+    float4 bv;
+    if (ep.bias_vec && col0 + j + 4 <= ep.N) {
+      bv = bias4(ep, col0 + j);
+    } else {
+      bv.x = (ep.bias != nullptr && col0 + j < ep.N) ? __ldg(ep.bias + col0 + j) : 0.0f;
+      bv.y = (ep.bias != nullptr && col0 + j + 1 < ep.N) ? __ldg(ep.bias + col0 + j + 1) : 0.0f;
+      bv.z = (ep.bias != nullptr && col0 + j + 2 < ep.N) ? __ldg(ep.bias + col0 + j + 2) : 0.0f;
+      bv.w = (ep.bias != nullptr && col0 + j + 3 < ep.N) ? __ldg(ep.bias + col0 + j + 3) : 0.0f;
+    }
+    const float v0 = apply_act(acc[j] + bv.x, ep.act, ep.alpha);
+    const float v1 = apply_act(acc[j + 1] + bv.y, ep.act, ep.alpha);
+    const float v2 = apply_act(acc[j + 2] + bv.z, ep.act, ep.alpha);
+    const float v3 = apply_act(acc[j + 3] + bv.w, ep.act, ep.alpha);
     if (ep.vec_out && col0 + j + 4 <= ep.N) {
       *reinterpret_cast<float4*>(dst + j) = make_float4(v0, v1, v2, v3);
     } else {
@@ -1507,6 +1523,7 @@ static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool
   ep.Ylo = ylo;
   ep.ldylo = ldylo;
   ep.stage_store = store_staging_enabled() ? 1 : 0;
+  ep.bias_vec = (bias != nullptr && (reinterpret_cast<uintptr_t>(bias) & 15) == 0) ? 1 : 0;
   int rc = dispatch_gemm(xa, xlo, ldx, fused, bop, M, N, K, sc, ep, status, stream);
   if (rc != kOk || sc.rest == 0) return rc;
   const int tile_m = pair ? kPairBM : kBM;
