@@ -491,6 +491,17 @@ def run_b200(args):
                "sample": f"X[{rows_s},{K_DIM}] rows of the workload @ W + b, relu, one run "
                          f"({dt:.1f} s); oracle/ref_linalg.c restatement of the reference CPU "
                          f"pipeline"}
+        # NumPy (BLAS) on the same rows, as the reference's benchmarks time it
+        # for context (benchmarks/bench_dense_layer.py); not the baseline
+        Xs, Ws, bs = _oracle_inputs(rows_s)
+        np.maximum(Xs[:64] @ Ws + bs, 0)
+        t0 = time.perf_counter()
+        np.maximum(Xs @ Ws + bs, 0)
+        dtn = time.perf_counter() - t0
+        cpu["numpy_context"] = {"value": 2.0 * rows_s * N_DIM * K_DIM / dtn / 1e12,
+                                "unit": UNIT, "sample": f"np.maximum(X @ W + b, 0) on the same "
+                                                        f"{rows_s} rows ({dtn:.2f} s)"}
+        del Xs, Ws, bs
 
     if rank == 0:
         line = {
