@@ -45,7 +45,8 @@ constexpr int kQPlaneA = kQBM * kQBK;  // 8 KB
 constexpr int kQPlaneB = kQBN * kQBK;  // 8 KB
 constexpr int kQStageBytes = 4 * kQPlaneA + 4 * kQPlaneB;  // 64 KB
 constexpr int kQBarOffset = kQStages * kQStageBytes;
-constexpr int kQSmemBytes = kQBarOffset + 256 + 1024;  // barriers + alignment slack
+constexpr int kQStoreStage = kQBarOffset + 256;  // 4 KB per epilogue warp (store staging)
+constexpr int kQSmemBytes = kQStoreStage + 8 * 4096 + 1024;  // + alignment slack
 constexpr int kQEpiWarps = 8;
 constexpr int kQThreads = 64 + 32 * kQEpiWarps;
 constexpr int kQTmemCols = 4 * kQBN;  // one 128 x 128 s32 accumulator per shift
@@ -215,6 +216,43 @@ __global__ void __launch_bounds__(kQThreads, 1)
       }
       const int64_t row = (int64_t)w.m0 + lr;
       const int64_t col0 = (int64_t)w.n0 + lc0;
+      const int64_t row0 = row - lane;
+      // The warp's whole 32 x 64 region inside C: pass it through shared
+      // memory in 32 x 32 blocks (16-byte chunks XOR-swizzled by row) so that
+      // each store instruction writes four whole 128-byte row segments
+      // instead of 32 scattered 16-byte pieces.
+      if (ep.vec_out && row0 + 32 <= ep.M && col0 + 64 <= ep.N) {
+        uint32_t* stage = reinterpret_cast<uint32_t*>(smem + kQStoreStage + (warp - 2) * 4096);
+        const bool bvec = ep.bias != nullptr && (reinterpret_cast<uintptr_t>(ep.bias) & 15) == 0;
+#pragma unroll
+        for (int cb = 0; cb < 2; ++cb) {
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) {
+            const int c = cb * 32 + ch * 4;
+            uint4 bv = make_uint4(0u, 0u, 0u, 0u);
+            if (bvec) {
+              bv = __ldg(reinterpret_cast<const uint4*>(ep.bias + col0 + c));
+            } else if (ep.bias != nullptr) {
+              bv = make_uint4((uint32_t)__ldg(ep.bias + col0 + c),
+                              (uint32_t)__ldg(ep.bias + col0 + c + 1),
+                              (uint32_t)__ldg(ep.bias + col0 + c + 2),
+                              (uint32_t)__ldg(ep.bias + col0 + c + 3));
+            }
+            *reinterpret_cast<uint4*>(stage + lane * 32 + ((ch ^ (lane & 7)) << 2)) =
+                make_uint4(acc[c] + bv.x, acc[c + 1] + bv.y, acc[c + 2] + bv.z,
+                           acc[c + 3] + bv.w);  // modulo 2^32
+          }
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int r = k * 4 + (lane >> 3), ch = lane & 7;
+            *reinterpret_cast<uint4*>(ep.C + (row0 + r) * ep.ldc + col0 + cb * 32 + ch * 4) =
+                *reinterpret_cast<const uint4*>(stage + r * 32 + ((ch ^ (r & 7)) << 2));
+          }
+          __syncwarp();
+        }
+        continue;
+      }
       if (row < ep.M) {
         int32_t* dst = ep.C + row * ep.ldc + col0;
 #pragma unroll
