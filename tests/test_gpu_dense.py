@@ -589,3 +589,52 @@ def test_chained_layers_match_separate_calls(cuda, M, K, N1, N2):
     if K % 4:  # a pre-split X needs aligned X rows: rejected before any launch
         assert L.b200_dense_f32_chain(ptr(tX), K, ptr(Hlo), ptr(tW1), N1, None, ptr(H), N1,
                                       None, 0, M, N1, K, 0, 0.0, s) == 1
+
+
+def test_random_shapes_and_pitches_against_oracle(cuda):
+    """40 seeded random problems: M, N, K in [1, 700], row pitches above the
+    rows (aligned or not), bias present or not, each activation, through
+    b200_dense_f32 and b200_dense_f32_chain (which also writes Y's lo part).
+    Covers the staged and per-thread epilogue stores at M / N edges, cut
+    tiles, both B layouts and the X split variants."""
+    import torch
+    dev = torch.device("cuda:0")
+    L = _native.lib()
+    s = stream_ptr(torch)
+    rng = np.random.default_rng(2024)
+    for case in range(40):
+        M, N, K = (int(v) for v in rng.integers(1, 701, 3))
+        ldx = K + int(rng.integers(0, 9)) * int(rng.integers(0, 2))
+        ldw = N + int(rng.integers(0, 9)) * int(rng.integers(0, 2))
+        ldy = N + int(rng.integers(0, 9)) * int(rng.integers(0, 2))
+        act, alpha = int(rng.integers(0, 3)), 0.05
+        with_b = bool(rng.integers(0, 2))
+        X = rng.uniform(-1, 1, (M, ldx)).astype(np.float32)
+        W = rng.uniform(-1, 1, (K, ldw)).astype(np.float32)
+        b = rng.uniform(-1, 1, N).astype(np.float32) if with_b else None
+        tX, tW = torch.from_numpy(X).to(dev), torch.from_numpy(W).to(dev)
+        tb = torch.from_numpy(b).to(dev) if with_b else None
+        ref = oracle.dense_f32(X[:, :K], W[:, :N], b, act=act, alpha=alpha)
+        bound = oracle.f32_bound(K, X[:, :K], W[:, :N])
+        for chain in (False, True):
+            tY = torch.full((M, ldy), 7.0, device=dev)
+            tlo = torch.full((M, N), 9.0, device=dev)
+            if chain:
+                rc = L.b200_dense_f32_chain(ptr(tX), ldx, None, ptr(tW), ldw, ptr(tb), ptr(tY),
+                                            ldy, ptr(tlo), N, M, N, K, act, alpha, s)
+            else:
+                rc = L.b200_dense_f32(ptr(tX), ldx, ptr(tW), ldw, ptr(tb), ptr(tY), ldy, M, N, K,
+                                      act, alpha, s)
+            _native.check(rc)
+            _native.check(L.b200_stream_sync(s))
+            Y = tY.cpu().numpy()
+            what = f"case {case}: M={M} N={N} K={K} ld=({ldx},{ldw},{ldy}) act={act} " \
+                   f"bias={with_b} chain={chain}"
+            assert max_err(Y[:, :N], ref) <= bound, what
+            assert (Y[:, N:] == 7.0).all(), what
+            if chain:  # the lo part equals a separate split of Y (pitch roundup(N, 4))
+                Np = (N + 3) // 4 * 4
+                hi, lo = torch.empty((M, Np), device=dev), torch.empty((M, Np), device=dev)
+                _native.check(L.b200_tf32_split_rows(ptr(tY), ldy, M, N, ptr(hi), ptr(lo), s))
+                _native.check(L.b200_stream_sync(s))
+                np.testing.assert_array_equal(tlo.cpu().numpy(), lo.cpu().numpy()[:, :N], what)
