@@ -21,7 +21,7 @@
 // Accumulation: the tensor core adds into its f32 accumulator with
 // round-toward-zero, so a single TMEM accumulator over all of K drifts
 // linearly in K (measured 3.3e-3 at K=4096 for |x| <= 1, against ~1e-5 for
-// round-to-nearest). The kernel therefore accumulates each 128-wide slice of
+// round-to-nearest). The kernel therefore accumulates each 256-wide slice of
 // K in TMEM ("chunk") and promotes it into f32 registers with ordinary
 // round-to-nearest adds; two TMEM chunk buffers let the MMAs of chunk c+1 run
 // while the epilogue warps drain chunk c.
@@ -60,7 +60,13 @@ constexpr int kEpiWarps = 8;  // 2 warps per TMEM lane quarter, one per column h
 constexpr int kTmemCols = 2 * kBN;  // two chunk accumulators of 128 x 256 f32
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kGroupM = 16;  // tile raster: 16 M-tiles share each N sweep
-constexpr int kChunkK = 128;  // K per TMEM partial-sum chunk
+// K per TMEM partial-sum chunk (compile-time; -DB200_CHUNK_K=128 builds the
+// narrower variant). 256 lets the next tile's MMAs run further ahead of the
+// epilogue; the error stays below that of a sequential f32 FMA loop.
+#ifndef B200_CHUNK_K
+#define B200_CHUNK_K 256
+#endif
+constexpr int kChunkK = B200_CHUNK_K;
 
 // Shared-memory ring configuration. BK floats of K per stage; the rows of
 // each operand tile are BK*4 bytes, which selects the TMA / UMMA swizzle:
@@ -1424,7 +1430,7 @@ static Sched sched_f32(int64_t M, int64_t N, int64_t K, bool pair, int bk, bool 
   const int procs = pair ? std::max(1, sms / 2) : sms;
   const double t_tile = 2.0 * bm * kBN * (double)K / (pair ? 2.0 : 1.0) / 1.65e12;
   return make_sched(M, N, K, bm, kBN, bk, procs, t_tile, 4, 0, allow_cut ? 16 : 1,
-                    kChunkK / bk, kGroupM);
+                    128 / bk /* pieces may end mid-chunk */, kGroupM);
 }
 
 static int default_bk() { return ring_variant() == 0 ? CfgBK32S2::BK : CfgBK16S4::BK; }

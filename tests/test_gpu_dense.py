@@ -64,14 +64,17 @@ def test_leaky_relu_epilogue(cuda):
 
 
 def test_precision_is_fp32_level(cuda):
-    """3xTF32 must be far tighter than 1xTF32: error vs float64 ~ f32 rounding."""
+    """3xTF32 must be far tighter than 1xTF32: the error against float64 is
+    that of an f32 computation, i.e. within a small factor of the reference
+    CPU pipeline's own (sequential f32 FMA) error on the same data."""
     import torch
     X, W, b = _inputs(512, 512, 4096, seed=11)
     got = dense_device(torch, X, W, b, act=0)
     exact = X.astype(np.float64) @ W.astype(np.float64) + b
     err = float(np.max(np.abs(got - exact)))
-    # 1xTF32 gives ~1e-2 here; f32 FMA accumulation gives ~1e-5
-    assert err < 2e-4, err
+    ref_err = float(np.max(np.abs(oracle.dense_f32(X, W, b, act=0) - exact)))
+    # 1xTF32 gives ~1e-2 here; the f32 reference pipeline ~2e-4
+    assert err < 1e-3 and err <= 2 * ref_err, (err, ref_err)
 
 
 def test_relu_nan_and_signed_zero(cuda):
@@ -288,8 +291,10 @@ for (M, N, K) in [(512, 512, 4096), (300, 500, 1000), (1000, 999, 1001)]:
     b = rng.uniform(-1, 1, (N,)).astype(np.float32)
     got = dense_device(torch, X, W, b, act=0)
     exact = X.astype(np.float64) @ W.astype(np.float64) + b
-    assert float(np.max(np.abs(got - exact))) < 2e-4, (M, N, K)
     ref = oracle.dense_f32(X, W, b)
+    err = float(np.max(np.abs(got - exact)))
+    ref_err = float(np.max(np.abs(ref - exact)))
+    assert err < 1e-3 and err <= 2 * ref_err, (M, N, K, err, ref_err)
     assert max_err(got, ref) <= oracle.f32_bound(K, X, W), (M, N, K)
 print("ok")
 """
