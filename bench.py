@@ -514,7 +514,7 @@ def run_b200(args):
                        "rows_per_gpu": M, "parallelism": f"dp{world} (row shards, W/b "
                                                          "replicated, no collective)",
                        "l2": "inputs larger than L2 (X rows >= 128 MiB + W 64 MiB per GPU)",
-                       "precision": "3xTF32 tensor cores, f32 accumulation promoted every 128 "
+                       "precision": "3xTF32 tensor cores, f32 accumulation promoted every 256 "
                                     "of K"},
             "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
             "gathered": gathered,
