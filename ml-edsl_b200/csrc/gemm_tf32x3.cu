@@ -121,34 +121,72 @@ __device__ __forceinline__ void tf32_split(float x, float& h, float& l) {
 }
 
 // ---------------------------------------------------------------------------
-// Pre-pass 1: X[M,K] (row pitch ldx) -> hi[M,Kp], lo[M,Kp]; pad columns zero.
-__global__ void split_rows_kernel(const float* __restrict__ X, int64_t ldx, int64_t M, int64_t K,
-                                  int64_t Kp, float* __restrict__ hi, float* __restrict__ lo,
-                                  int vec_in) {
-  // The GEMM that follows may start its prologue once every CTA is done.
-  const PdlTriggerOnExit pdl_trigger_on_exit;
-  const int64_t q_per_row = Kp >> 2;
-  const int64_t total = M * q_per_row;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t m = i / q_per_row;
-    const int64_t k = (i - m * q_per_row) << 2;
+__device__ __forceinline__ void split_quad_store(const float (&v)[4], float* __restrict__ hi,
+                                                 float* __restrict__ lo, int64_t off) {
+  float4 h, l;
+  tf32_split(v[0], h.x, l.x);
+  tf32_split(v[1], h.y, l.y);
+  tf32_split(v[2], h.z, l.z);
+  tf32_split(v[3], h.w, l.w);
+  if (hi) *reinterpret_cast<float4*>(hi + off) = h;
+  *reinterpret_cast<float4*>(lo + off) = l;
+}
+
+// Splits src [rows, cols] (pitch ld) into hi/lo [rows, pc] (pc = cols rounded
+// up to 4, zero padded), one 4-float quad per thread and iteration of a
+// grid-stride loop. Four quads are loaded before any is split so that each
+// thread keeps four 16-byte loads in flight (the pass is HBM-bound).
+__device__ __forceinline__ void split_quads(const float* __restrict__ src, int64_t ld,
+                                            int64_t rows, int64_t cols, int64_t pc,
+                                            float* __restrict__ hi, float* __restrict__ lo,
+                                            int64_t i0, int64_t step) {
+  constexpr int kU = 4;
+  const int64_t q_per_row = pc >> 2;
+  const int64_t total = rows * q_per_row;
+  const int vec_in = ((ld & 3) == 0) && ((reinterpret_cast<uintptr_t>(src) & 15) == 0);
+  if (vec_in && ld == cols && cols == pc) {
+    // contiguous rows without padding: a flat array of quads
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    int64_t i = i0;
+    for (; i + (kU - 1) * step < total; i += kU * step) {
+      float4 t[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) t[u] = __ldg(s4 + i + u * step);
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const float v[4] = {t[u].x, t[u].y, t[u].z, t[u].w};
+        split_quad_store(v, hi, lo, (i + u * step) << 2);
+      }
+    }
+    for (; i < total; i += step) {
+      const float4 t = __ldg(s4 + i);
+      const float v[4] = {t.x, t.y, t.z, t.w};
+      split_quad_store(v, hi, lo, i << 2);
+    }
+    return;
+  }
+  for (int64_t i = i0; i < total; i += step) {
+    const int64_t r = i / q_per_row;
+    const int64_t c = (i - r * q_per_row) << 2;
     float v[4];
-    if (vec_in && k + 4 <= K) {
-      const float4 t = __ldg(reinterpret_cast<const float4*>(X + m * ldx + k));
+    if (vec_in && c + 4 <= cols) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(src + r * ld + c));
       v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
     } else {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) v[j] = (k + j < K) ? __ldg(X + m * ldx + k + j) : 0.0f;
+      for (int j = 0; j < 4; ++j) v[j] = (c + j < cols) ? __ldg(src + r * ld + c + j) : 0.0f;
     }
-    float4 h, l;
-    tf32_split(v[0], h.x, l.x);
-    tf32_split(v[1], h.y, l.y);
-    tf32_split(v[2], h.z, l.z);
-    tf32_split(v[3], h.w, l.w);
-    *reinterpret_cast<float4*>(hi + m * Kp + k) = h;
-    *reinterpret_cast<float4*>(lo + m * Kp + k) = l;
+    split_quad_store(v, hi, lo, r * pc + c);
   }
+}
+
+// Pre-pass 1: X[M,K] (row pitch ldx) -> hi[M,Kp], lo[M,Kp]; pad columns zero.
+__global__ void split_rows_kernel(const float* __restrict__ X, int64_t ldx, int64_t M, int64_t K,
+                                  int64_t Kp, float* __restrict__ hi, float* __restrict__ lo) {
+  // The GEMM that follows may start its prologue once every CTA is done.
+  const PdlTriggerOnExit pdl_trigger_on_exit;
+  split_quads(X, ldx, M, K, Kp, hi, lo, blockIdx.x * (int64_t)blockDim.x + threadIdx.x,
+              (int64_t)gridDim.x * blockDim.x);
 }
 
 // Pre-pass 1b: lo part only, lo[M,Kp]. The GEMM then reads X itself as the
@@ -159,28 +197,8 @@ __global__ void split_rows_lo_kernel(const float* __restrict__ X, int64_t ldx, i
                                      int64_t K, int64_t Kp, float* __restrict__ lo) {
   // The GEMM that follows may start its prologue once every CTA is done.
   const PdlTriggerOnExit pdl_trigger_on_exit;
-  const int64_t q_per_row = Kp >> 2;
-  const int64_t total = M * q_per_row;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t m = i / q_per_row;
-    const int64_t k = (i - m * q_per_row) << 2;
-    float v[4];
-    if (k + 4 <= K) {
-      const float4 t = __ldg(reinterpret_cast<const float4*>(X + m * ldx + k));
-      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
-    } else {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) v[j] = (k + j < K) ? __ldg(X + m * ldx + k + j) : 0.0f;
-    }
-    float h;
-    float4 l;
-    tf32_split(v[0], h, l.x);
-    tf32_split(v[1], h, l.y);
-    tf32_split(v[2], h, l.z);
-    tf32_split(v[3], h, l.w);
-    *reinterpret_cast<float4*>(lo + m * Kp + k) = l;
-  }
+  split_quads(X, ldx, M, K, Kp, nullptr, lo, blockIdx.x * (int64_t)blockDim.x + threadIdx.x,
+              (int64_t)gridDim.x * blockDim.x);
 }
 
 // Pre-pass 2: W[K,N] (row pitch ldw) -> hiT[N,Kp], loT[N,Kp] (K-major).
@@ -225,28 +243,8 @@ __global__ void __launch_bounds__(256)
   // The GEMM that follows may start its prologue once every CTA is done.
   const PdlTriggerOnExit pdl_trigger_on_exit;
   if ((int)blockIdx.x < x_blocks) {
-    const int64_t q_per_row = Kp >> 2;
-    const int64_t total = M * q_per_row;
-    const int vec_in = ((ldx & 3) == 0) && ((reinterpret_cast<uintptr_t>(X) & 15) == 0);
-    for (int64_t i = blockIdx.x * 256ll + threadIdx.x; i < total; i += (int64_t)x_blocks * 256) {
-      const int64_t m = i / q_per_row;
-      const int64_t k = (i - m * q_per_row) << 2;
-      float v[4];
-      if (vec_in && k + 4 <= K) {
-        const float4 t = __ldg(reinterpret_cast<const float4*>(X + m * ldx + k));
-        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
-      } else {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) v[j] = (k + j < K) ? __ldg(X + m * ldx + k + j) : 0.0f;
-      }
-      float4 h, l;
-      tf32_split(v[0], h.x, l.x);
-      tf32_split(v[1], h.y, l.y);
-      tf32_split(v[2], h.z, l.z);
-      tf32_split(v[3], h.w, l.w);
-      if (xhi) *reinterpret_cast<float4*>(xhi + m * Kp + k) = h;
-      *reinterpret_cast<float4*>(xlo + m * Kp + k) = l;
-    }
+    split_quads(X, ldx, M, K, Kp, xhi, xlo, blockIdx.x * 256ll + threadIdx.x,
+                (int64_t)x_blocks * 256);
     return;
   }
   __shared__ float th[32][33];
@@ -278,34 +276,6 @@ __global__ void __launch_bounds__(256)
 // Rows of a row-major [rows, cols] matrix (pitch ld) -> lo (and hi when
 // non-null) with pitch pc = roundup(cols, 4); pad columns zero. Quads
 // i0, i0 + step, ... of the rows * pc / 4 output quads.
-__device__ __forceinline__ void split_quads(const float* __restrict__ src, int64_t ld,
-                                            int64_t rows, int64_t cols, int64_t pc,
-                                            float* __restrict__ hi, float* __restrict__ lo,
-                                            int64_t i0, int64_t step) {
-  const int64_t q_per_row = pc >> 2;
-  const int64_t total = rows * q_per_row;
-  const int vec_in = ((ld & 3) == 0) && ((reinterpret_cast<uintptr_t>(src) & 15) == 0);
-  for (int64_t i = i0; i < total; i += step) {
-    const int64_t r = i / q_per_row;
-    const int64_t c = (i - r * q_per_row) << 2;
-    float v[4];
-    if (vec_in && c + 4 <= cols) {
-      const float4 t = __ldg(reinterpret_cast<const float4*>(src + r * ld + c));
-      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
-    } else {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) v[j] = (c + j < cols) ? __ldg(src + r * ld + c + j) : 0.0f;
-    }
-    float4 h, l;
-    tf32_split(v[0], h.x, l.x);
-    tf32_split(v[1], h.y, l.y);
-    tf32_split(v[2], h.z, l.z);
-    tf32_split(v[3], h.w, l.w);
-    if (hi) *reinterpret_cast<float4*>(hi + r * pc + c) = h;
-    *reinterpret_cast<float4*>(lo + r * pc + c) = l;
-  }
-}
-
 // Pre-pass 4, for the MN-major B operand: X -> X_lo [M, Kp] (and X_hi when
 // xhi is non-null) and W [K, N] -> W_lo [K, Np] (row-major, not transposed)
 // in one launch; the GEMM reads the raw W as B_hi. Blocks [0, x_blocks)
@@ -1221,11 +1191,10 @@ int split_w_f32(const float* W, int64_t ldw, int64_t K, int64_t N, float* whiT, 
 int split_x_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xhi, float* xlo,
                 cudaStream_t stream) {
   const int64_t Kp = (K + 3) & ~int64_t(3);
-  const int vec_in = ((ldx & 3) == 0) && ((reinterpret_cast<uintptr_t>(X) & 15) == 0);
   const int64_t total = M * (Kp / 4);
   int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
   if (blocks < 1) blocks = 1;
-  split_rows_kernel<<<blocks, 256, 0, stream>>>(X, ldx, M, K, Kp, xhi, xlo, vec_in);
+  split_rows_kernel<<<blocks, 256, 0, stream>>>(X, ldx, M, K, Kp, xhi, xlo);
   count_launch();
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
