@@ -285,7 +285,7 @@ def run_b200(args):
     value = flops_job * args.steps / (ms_total / 1e3) / 1e12
 
     # ---- roofline: the GEMM kernel alone on pre-split operands
-    Kp = (K + 3) // 4 * 4
+    Kp = _native.split_pitch(K)
     xhi = torch.empty((M, Kp), device=dev)
     xlo = torch.empty_like(xhi)
     whi = torch.empty((N, Kp), device=dev)

@@ -113,7 +113,7 @@ int b200_dense_f32_ws(const float* X, int64_t ldx, const float* W, int64_t ldw, 
  * has no counterpart in the reference.
  * The call allocates nothing: its scratch is a fixed 64 MiB device array that
  * every GPU loading this library holds until the process exits. Problems
- * needing more than that (8 * (M + N) * roundup(K, 4) bytes plus alignment)
+ * needing more than that (8 * (M + N) * roundup(K, 8) bytes plus alignment)
  * fail with B200_ERR_TOO_LARGE. All calls on a device share the array, so
  * calls that overlap on the GPU race; the call synchronises `stream` before
  * it returns. The first call on a device resolves the array's device address
@@ -150,7 +150,7 @@ int b200_stream_sync(void* stream);
  * matrix can be split once and reused across calls:
  *   b200_tf32_split_rows:      X[M,K] -> hi[M,Kp], lo[M,Kp]
  *   b200_tf32_split_transpose: W[K,N] -> hiT[N,Kp], loT[N,Kp] (K-major)
- * with Kp = K rounded up to a multiple of 4, x = hi + lo, hi and lo exact
+ * with Kp = K rounded up to a multiple of 8 (32-byte rows), x = hi + lo, hi and lo exact
  * tf32 values (Inf/NaN travel in hi). Outputs must be 16-byte aligned. */
 int b200_tf32_split_rows(const float* X, int64_t ldx, int64_t M, int64_t K, float* hi, float* lo,
                          void* stream);
@@ -210,7 +210,7 @@ int b200_selftest_wait_timeout(int64_t limit_ns, void* stream);
 int b200_debug_fail_alloc(int n);
 
 /* b200_dense_f32_chain: b200_dense_f32 for stacked layers kept on the
- * device. Xlo (optional): X's tf32 lo part with row pitch roundup(K, 4), as
+ * device. Xlo (optional): X's tf32 lo part with row pitch roundup(K, 8), as
  * the previous layer wrote it to its Ylo, so that X is not split again (X and
  * Xlo rows 16-byte aligned). Ylo (optional, pitch ldylo >= N): the epilogue
  * also stores the tf32 lo part of Y (after bias and activation) for the next

@@ -1168,12 +1168,12 @@ struct BOp {
   bool mn;
 };
 static BOp bop_k(const float* whiT, const float* wloT, int64_t K) {
-  const int64_t Kp = (K + 3) & ~int64_t(3);
+  const int64_t Kp = split_pitch(K);
   return BOp{whiT, wloT, Kp, Kp, false};
 }
 
 int64_t dense_f32_workspace_bytes(int64_t M, int64_t N, int64_t K) {
-  const int64_t Kp = (K + 3) & ~int64_t(3);
+  const int64_t Kp = split_pitch(K);
   // hi + lo of X (M x Kp) and of W^T (N x Kp), each region 256-byte aligned
   auto al = [](int64_t b) { return (b + 255) & ~int64_t(255); };
   return 2 * al(M * Kp * 4) + 2 * al(N * Kp * 4);
@@ -1181,7 +1181,7 @@ int64_t dense_f32_workspace_bytes(int64_t M, int64_t N, int64_t K) {
 
 int split_w_f32(const float* W, int64_t ldw, int64_t K, int64_t N, float* whiT, float* wloT,
                 cudaStream_t stream) {
-  const int64_t Kp = (K + 3) & ~int64_t(3);
+  const int64_t Kp = split_pitch(K);
   dim3 grid((unsigned)((N + 31) / 32), (unsigned)((Kp + 31) / 32));
   split_transpose_kernel<<<grid, dim3(32, 8), 0, stream>>>(W, ldw, K, N, Kp, whiT, wloT);
   count_launch();
@@ -1190,7 +1190,7 @@ int split_w_f32(const float* W, int64_t ldw, int64_t K, int64_t N, float* whiT, 
 
 int split_x_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xhi, float* xlo,
                 cudaStream_t stream) {
-  const int64_t Kp = (K + 3) & ~int64_t(3);
+  const int64_t Kp = split_pitch(K);
   const int64_t total = M * (Kp / 4);
   int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
   if (blocks < 1) blocks = 1;
@@ -1294,7 +1294,7 @@ template <class Cfg>
 static int run_gemm(const float* xa, const float* xlo, int64_t ldx, bool fused, const BOp& b,
                     int64_t M, int64_t N, int64_t K, const Sched& sc, const Epilogue& ep,
                     int* status, cudaStream_t stream) {
-  const int64_t Kp = (K + 3) & ~int64_t(3);
+  const int64_t Kp = split_pitch(K);
   CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
   int rc = make_tmap(&ta_hi, xa, K, M, ldx, kBM, Cfg::BK);
   if (rc == kOk) rc = make_tmap(&ta_lo, fused ? xa : xlo, K, M, fused ? ldx : Kp, kBM, Cfg::BK);
@@ -1344,7 +1344,7 @@ static int run_gemm_pair(const float* xa, const float* xlo, int64_t ldx, const f
       return kErrCuda;
     attr_done.fetch_or(bit);
   }
-  const int64_t Kp = (K + 3) & ~int64_t(3);
+  const int64_t Kp = split_pitch(K);
   CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
   int rc = make_tmap(&ta_hi, xa, K, M, ldx, 128, Cfg::BK);
   if (rc == kOk) rc = make_tmap(&ta_lo, xlo, K, M, Kp, 128, Cfg::BK);
@@ -1383,7 +1383,7 @@ int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
                          const float* wloT, int64_t M, int64_t N, int64_t K, const float* bias,
                          float* Y, int64_t ldy, int act, float alpha, int* status,
                          cudaStream_t stream) {
-  return gemm_with_splits(xhi, xlo, (K + 3) & ~int64_t(3), false, bop_k(whiT, wloT, K), M, N, K,
+  return gemm_with_splits(xhi, xlo, split_pitch(K), false, bop_k(whiT, wloT, K), M, N, K,
                           bias, Y, ldy, act, alpha, 1, nullptr, status, stream);
 }
 
@@ -1516,14 +1516,14 @@ int gemm_tf32x3_splitk(const float* xhi, const float* xlo, const float* whiT, co
                        int64_t M, int64_t N, int64_t K, const float* bias, float* Y, int64_t ldy,
                        int act, float alpha, int splits, float* partials, int* status,
                        cudaStream_t stream, float* ylo, int64_t ldylo) {
-  return gemm_with_splits(xhi, xlo, (K + 3) & ~int64_t(3), false, bop_k(whiT, wloT, K), M, N, K,
+  return gemm_with_splits(xhi, xlo, split_pitch(K), false, bop_k(whiT, wloT, K), M, N, K,
                           bias, Y, ldy, act, alpha, splits, partials, status, stream, ylo, ldylo);
 }
 
 int split_xw_f32(const float* X, int64_t ldx, int64_t M, const float* W, int64_t ldw,
                  int64_t K, int64_t N, float* xhi, float* xlo, float* whiT, float* wloT,
                  cudaStream_t stream) {
-  const int64_t Kp = (K + 3) & ~int64_t(3);
+  const int64_t Kp = split_pitch(K);
   const int64_t xq = M * (Kp / 4);
   const int x_blocks = (int)std::max<int64_t>(1, std::min<int64_t>((xq + 255) / 256, 148 * 16));
   const int tiles_n = (int)((N + 31) / 32);
@@ -1536,7 +1536,7 @@ int split_xw_f32(const float* X, int64_t ldx, int64_t M, const float* W, int64_t
 
 int split_x_lo_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xlo,
                    cudaStream_t stream) {
-  const int64_t Kp = (K + 3) & ~int64_t(3);
+  const int64_t Kp = split_pitch(K);
   const int64_t total = M * (Kp / 4);
   int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
   if (blocks < 1) blocks = 1;
@@ -1594,7 +1594,7 @@ bool w_lo_in_kernel() {
 
 int split_lo_xw_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xhi, float* xlo,
                     const float* W, int64_t ldw, int64_t N, float* wlo, cudaStream_t stream) {
-  const int64_t Kp = (K + 3) & ~int64_t(3), Np = (N + 3) & ~int64_t(3);
+  const int64_t Kp = split_pitch(K), Np = (N + 3) & ~int64_t(3);
   const int64_t xq = X ? M * (Kp / 4) : 0, wq = K * (Np / 4);
   // blocks in proportion to each part's quads, together about 16 per SM
   const int64_t cap = 148 * 16;

@@ -29,6 +29,11 @@ int report_error(int code, const char* msg);
 int report_ok();
 
 // ---- 3xTF32 GEMM (gemm_tf32x3.cu)
+// Row pitch (floats) of every tf32 hi/lo split buffer of K columns: K
+// rounded up to 8, so that every row starts on a 32-byte L2 sector and each
+// 64-byte TMA row segment of a K-major operand covers exactly two sectors
+// (with a pitch of 4 mod 8 floats, every other row straddles three).
+inline int64_t split_pitch(int64_t K) { return (K + 7) & ~int64_t(7); }
 int64_t dense_f32_workspace_bytes(int64_t M, int64_t N, int64_t K);
 int split_x_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xhi, float* xlo,
                 cudaStream_t stream);

@@ -121,7 +121,7 @@ extern "C" int b200_dense_f32_noalloc(const float* X, int64_t ldx, const float* 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
   if (K > 0) {
-    const int64_t Kp = (K + 3) / 4 * 4;
+    const int64_t Kp = split_pitch(K);
     const int64_t need = dense_f32_workspace_bytes(M, N, K);
     if (need > kNoAllocScratchBytes) {
       char buf[240];

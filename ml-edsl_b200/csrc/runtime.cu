@@ -389,7 +389,7 @@ int64_t dense_scratch_bytes(int64_t M, int64_t N, int64_t K) {
   return dense_f32_workspace_bytes(M, N, K) + splitk_partials_bytes(M, N, K);
 }
 SplitBufs carve(void* ws, int64_t M, int64_t N, int64_t K) {
-  const int64_t Kp = round_up(K, 4);
+  const int64_t Kp = split_pitch(K);
   auto al = [](int64_t b) { return round_up(b, 256); };
   char* p = static_cast<char*>(ws);
   SplitBufs s;
@@ -417,7 +417,7 @@ bool fuse_a(const float* X, int64_t ldx) {
   return enabled && fused_a_ok(X, ldx);
 }
 
-// xlo_in (optional): X's tf32 lo part, pitch roundup(K, 4), from the previous
+// xlo_in (optional): X's tf32 lo part, pitch split_pitch(K), from the previous
 // layer's epilogue (X rows must then be 16-byte aligned: X itself is A_hi),
 // so X is not split again. ylo (optional, pitch ldylo): the epilogue also
 // writes the lo part of Y for the next layer.
@@ -429,7 +429,7 @@ int dense_device(DeviceCtx* c, const float* X, int64_t ldx, const float* W, int6
   if (K == 0) return fill_bias_act_f32(b, Y, ldy, M, N, act, alpha, st);
   SplitBufs s = carve(ws, M, N, K);
   const int splits = choose_splits(M, N, K);
-  const int64_t Kp = (K + 3) & ~int64_t(3);
+  const int64_t Kp = split_pitch(K);
   float* xlo = xlo_in ? const_cast<float*>(xlo_in) : s.xlo;
   int rc;
   if (fuse_a(X, ldx) && !xlo_in) {
@@ -503,7 +503,7 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
   std::lock_guard<std::mutex> lk(c->mu);
   B200_CUDA(cudaSetDevice(dev), "cudaSetDevice");
   if (M == 0 || N == 0) return kOk;
-  const int64_t Kp = round_up(std::max<int64_t>(K, 1), 4);
+  const int64_t Kp = split_pitch(std::max<int64_t>(K, 1));
 
   // Slab size: one slab for small calls, else B200_HOST_SLABS (default 16)
   // slabs of >= 512 rows, so the first copy-in and the last copy-out that
@@ -1081,7 +1081,7 @@ int b200_dense_f32_wsplit(const float* X, int64_t ldx, const float* whiT, const 
   const int splits = choose_splits(M, N, K);
   const bool fused = fuse_a(X, ldx);
   // Scratch: [X hi | X lo] (separate split pass) then the split-K partials.
-  const int64_t Kp = round_up(K, 4);
+  const int64_t Kp = split_pitch(K);
   const int64_t xsplit = fused ? 0 : 2 * round_up(M * Kp * 4, 256);
   void* ws = nullptr;
   {

@@ -161,6 +161,12 @@ def launch_count():
     return int(lib().b200_launch_count())
 
 
+def split_pitch(K):
+    """Row pitch (elements) of the library's tf32 hi/lo split buffers for K
+    columns: K rounded up to 8 (32-byte rows), as in csrc/kernels.h."""
+    return (K + 7) // 8 * 8
+
+
 def dense_launches(M, N, K):
     """Kernel launches of one f32 dense layer through b200_dense_f32: one
     split pass (X and W together), the GEMM, and a split-K reduction when the

@@ -267,13 +267,15 @@ class B200Backend:
                     bias = dref(s.inputs[2]) if s.has_bias else None
                     if s.op == "gemm_f32":
                         me = len(douts) - 1
-                        ylo = dmalloc(M * N * 4) if (me in feeds_a and N % 4 == 0 and K > 0) \
-                            else None
+                        # the next layer reads this lo part with its split pitch
+                        ldylo = _native.split_pitch(N)
+                        ylo = dmalloc(M * ldylo * 4) \
+                            if (me in feeds_a and N % 4 == 0 and K > 0) else None
                         xlo = lo_of.get(a.index) if a.kind == "step" else None
                         if ylo is not None or xlo is not None:
                             _native.check(L.b200_dense_f32_chain(
                                 dref(a), K, xlo, dref(b), N, bias, out, N, ylo,
-                                N if ylo is not None else 0, M, N, K, s.act, s.alpha, None))
+                                ldylo if ylo is not None else 0, M, N, K, s.act, s.alpha, None))
                             if ylo is not None:
                                 lo_of[me] = ylo
                         else:

@@ -53,7 +53,7 @@ def test_workspace_formula():
     al = lambda b: (b + 255) // 256 * 256
     # many tiles: no split-K, scratch = the four split operands
     M, N, K = 8192, 8192, 1001
-    Kp = 1004
+    Kp = 1008  # split rows are K rounded up to 8 floats
     assert lib.b200_dense_f32_splits(M, N, K) == 1
     assert lib.b200_dense_f32_workspace_bytes(M, N, K) == 2 * al(M * Kp * 4) + 2 * al(N * Kp * 4)
     # one tile, long K: the tile is cut into K pieces whose raw sums are kept

@@ -229,7 +229,7 @@ def test_split_k_matches_unsplit(cuda, M, N, K):
     assert L.b200_dense_f32_splits(M, N, K) > 1
     X, W, b = _inputs(M, N, K, seed=K)
     got = dense_device(torch, X, W, b, act=1)
-    Kp = (K + 3) // 4 * 4
+    Kp = _native.split_pitch(K)
     tX, tW, tb = (torch.from_numpy(a).to(dev) for a in (X, W, b))
     xhi, xlo = torch.empty((M, Kp), device=dev), torch.empty((M, Kp), device=dev)
     whi, wlo = torch.empty((N, Kp), device=dev), torch.empty((N, Kp), device=dev)
@@ -256,7 +256,7 @@ def test_fused_x_split_matches_split_pass(cuda, M, N, K):
     dev = torch.device("cuda:0")
     L = _native.lib()
     X, W, b = _inputs(M, N, K, seed=M + K)
-    Kp = (K + 3) // 4 * 4
+    Kp = _native.split_pitch(K)
     tX, tW, tb = (torch.from_numpy(a).to(dev) for a in (X, W, b))
     xhi, xlo = torch.empty((M, Kp), device=dev), torch.empty((M, Kp), device=dev)
     whi, wlo = torch.empty((N, Kp), device=dev), torch.empty((N, Kp), device=dev)
@@ -517,10 +517,11 @@ def test_split_rule_for_exact_and_non_finite_values(cuda):
     x = np.array([[0.0, -0.0, 1.0, -0.5, 3.0, np.inf, -np.inf, np.nan,
                    0.1, -1.2345678, 7.0e-3, 1.0e30]], np.float32)
     tX = torch.from_numpy(x).to(dev)
-    hi, lo = torch.empty((1, 12), device=dev), torch.empty((1, 12), device=dev)
+    kp = _native.split_pitch(12)  # output row pitch
+    hi, lo = torch.empty((1, kp), device=dev), torch.empty((1, kp), device=dev)
     _native.check(L.b200_tf32_split_rows(ptr(tX), 12, 1, 12, ptr(hi), ptr(lo), stream_ptr(torch)))
     _native.check(L.b200_stream_sync(stream_ptr(torch)))
-    h, l = hi.cpu().numpy()[0], lo.cpu().numpy()[0]
+    h, l = hi.cpu().numpy()[0, :12], lo.cpu().numpy()[0, :12]
     assert (l[:2] == 0).all() and (h[:2] == 0).all()
     np.testing.assert_array_equal(l[2:7], [tiny, -tiny, tiny, tiny, -tiny])
     np.testing.assert_array_equal(h[2:7], x[0, 2:7])
@@ -574,10 +575,11 @@ def test_chained_layers_match_separate_calls(cuda, M, K, N1, N2):
     X, W1, b1 = _inputs(M, N1, K, seed=M + K)
     _, W2, b2 = _inputs(M, N2, N1, seed=N1 + N2)
     tX, tW1, tb1, tW2, tb2 = (torch.from_numpy(a).to(dev) for a in (X, W1, b1, W2, b2))
-    H, Hlo = torch.empty((M, N1), device=dev), torch.full((M, N1), np.nan, device=dev)
+    n1p = _native.split_pitch(N1)  # the pitch layer 2 reads Hlo with
+    H, Hlo = torch.empty((M, N1), device=dev), torch.full((M, n1p), np.nan, device=dev)
     Y = torch.empty((M, N2), device=dev)
     _native.check(L.b200_dense_f32_chain(ptr(tX), K, None, ptr(tW1), N1, ptr(tb1), ptr(H), N1,
-                                         ptr(Hlo), N1, M, N1, K, 1, 0.0, s))
+                                         ptr(Hlo), n1p, M, N1, K, 1, 0.0, s))
     _native.check(L.b200_dense_f32_chain(ptr(H), N1, ptr(Hlo), ptr(tW2), N2, ptr(tb2), ptr(Y),
                                          N2, None, 0, M, N2, N1, 1, 0.0, s))
     H2, Y2 = torch.empty_like(H), torch.empty_like(Y)
@@ -585,11 +587,11 @@ def test_chained_layers_match_separate_calls(cuda, M, K, N1, N2):
                                    1, 0.0, s))
     _native.check(L.b200_dense_f32(ptr(H2), N1, ptr(tW2), N2, ptr(tb2), ptr(Y2), N2, M, N2, N1,
                                    1, 0.0, s))
-    hhi, hlo = torch.empty_like(H), torch.empty_like(H)
+    hhi, hlo = torch.empty((M, n1p), device=dev), torch.empty((M, n1p), device=dev)
     _native.check(L.b200_tf32_split_rows(ptr(H2), N1, M, N1, ptr(hhi), ptr(hlo), s))
     _native.check(L.b200_stream_sync(s))
     np.testing.assert_array_equal(H.cpu().numpy(), H2.cpu().numpy())
-    np.testing.assert_array_equal(Hlo.cpu().numpy(), hlo.cpu().numpy())
+    np.testing.assert_array_equal(Hlo.cpu().numpy()[:, :N1], hlo.cpu().numpy()[:, :N1])
     np.testing.assert_array_equal(Y.cpu().numpy(), Y2.cpu().numpy())
     if K % 4:  # a pre-split X needs aligned X rows: rejected before any launch
         assert L.b200_dense_f32_chain(ptr(tX), K, ptr(Hlo), ptr(tW1), N1, None, ptr(H), N1,
@@ -637,8 +639,8 @@ def test_random_shapes_and_pitches_against_oracle(cuda):
                    f"bias={with_b} chain={chain}"
             assert max_err(Y[:, :N], ref) <= bound, what
             assert (Y[:, N:] == 7.0).all(), what
-            if chain:  # the lo part equals a separate split of Y (pitch roundup(N, 4))
-                Np = (N + 3) // 4 * 4
+            if chain:  # the lo part equals a separate split of Y (pitch roundup(N, 8))
+                Np = _native.split_pitch(N)
                 hi, lo = torch.empty((M, Np), device=dev), torch.empty((M, Np), device=dev)
                 _native.check(L.b200_tf32_split_rows(ptr(tY), ldy, M, N, ptr(hi), ptr(lo), s))
                 _native.check(L.b200_stream_sync(s))
