@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(256)
   for (int p = 0; p < 4; ++p) {
     uint8_t* row = Bp + (p * N + n) * Kp + k0;
     *reinterpret_cast<uint4*>(row) = make_uint4(w[p][0], w[p][1], w[p][2], w[p][3]);
-    if (k0 + 16 < Kp)  // Kp is a multiple of 16: the second half is in or out whole
+    if (k0 + 16 < Kp)  // Kp is a multiple of 16 (of 32 today): each half is in or out whole
       *reinterpret_cast<uint4*>(row + 16) = make_uint4(w[p][4], w[p][5], w[p][6], w[p][7]);
   }
 }
@@ -410,7 +410,11 @@ int make_plane_map(CUtensorMap* map, const uint8_t* base, int64_t rows, int64_t 
 }
 
 int64_t al256(int64_t b) { return (b + 255) & ~int64_t(255); }
-int64_t kp_of(int64_t K) { return (K + 15) & ~int64_t(15); }
+// Row pitch (bytes) of the byte planes: K rounded up to 32, so every row
+// starts on a 32-byte L2 sector and each 64-byte TMA row segment covers
+// exactly two sectors (a pitch of 16 mod 32 makes every other row straddle
+// three).
+int64_t kp_of(int64_t K) { return (K + 31) & ~int64_t(31); }
 
 int sm_count_i32() {
   int dev = 0, n = 0;
