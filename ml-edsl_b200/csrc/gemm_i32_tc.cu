@@ -19,7 +19,7 @@
 // is below 2^31: the s32 accumulators never overflow.
 //
 // Layout: A's bytes as four planes [4][M][Kp] and B's as four transposed
-// planes [4][N][Kp] (K-major, Kp = roundup(K, 16), pad bytes zero), written by
+// planes [4][N][Kp] (K-major, Kp = roundup(K, 32), pad bytes zero), written by
 // one HBM pass. Per stage the producer loads all four planes of a 128 x 64-byte
 // A tile and of a 128 x 64-byte B tile with one 3-D TMA each (64-byte swizzle).
 // Roles as in the f32 kernel: warp 0 TMA, warp 1 TMEM allocation + MMA issue,

@@ -15,7 +15,8 @@
 // hi*hi + hi*lo + lo*hi in f32 (the lo*lo term is below f32 resolution).
 // The split runs in two HBM-bound pre-pass kernels that also
 //   * transpose W to K-major (both UMMA operands are K-major), and
-//   * pad the row pitch to a multiple of 4 floats (TMA needs 16-byte strides),
+//   * pad the row pitch to a multiple of 8 floats (TMA needs 16-byte strides;
+//     32-byte rows keep each 64-byte row segment within two L2 sectors),
 // which is how ragged shapes such as K=1001 reach the TMA path.
 //
 // Accumulation: the tensor core adds into its f32 accumulator with
@@ -1390,7 +1391,8 @@ int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
 // ---------------------------------------------------------------------------
 // Schedules (see sched.cuh). One 128 x 256 tile (256 x 256 for a CTA pair)
 // over all of K takes 2 * BM * 256 * K / 1.65e12 s per SM at the measured
-// 3xTF32 rate; a piece spans at least one 128-wide K chunk. Cut tiles arise
+// 3xTF32 rate; a piece spans at least 128 of K (half a TMEM promotion
+// chunk: a piece may end mid-chunk). Cut tiles arise
 // when the last wave is partial: the 1024^3 layer (32 tiles), the MLP's
 // layers (172 and 64 tiles), 4096^3 (512 tiles = 3.46 waves).
 static Sched sched_f32(int64_t M, int64_t N, int64_t K, bool pair, int bk, bool allow_cut) {
