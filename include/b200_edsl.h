@@ -150,8 +150,10 @@ int b200_stream_sync(void* stream);
  * matrix can be split once and reused across calls:
  *   b200_tf32_split_rows:      X[M,K] -> hi[M,Kp], lo[M,Kp]
  *   b200_tf32_split_transpose: W[K,N] -> hiT[N,Kp], loT[N,Kp] (K-major)
- * with Kp = K rounded up to a multiple of 8 (32-byte rows), x = hi + lo, hi and lo exact
- * tf32 values (Inf/NaN travel in hi). Outputs must be 16-byte aligned. */
+ * with Kp = K rounded up to a multiple of 8 (32-byte rows; pad columns zero).
+ * hi and lo are exact tf32 values: hi is x with its low 13 mantissa bits
+ * cleared, lo the remainder truncated to tf32, so hi + lo is x to 2^-21
+ * relative (Inf/NaN travel in hi). Outputs must be 16-byte aligned. */
 int b200_tf32_split_rows(const float* X, int64_t ldx, int64_t M, int64_t K, float* hi, float* lo,
                          void* stream);
 int b200_tf32_split_transpose(const float* W, int64_t ldw, int64_t K, int64_t N, float* hiT,

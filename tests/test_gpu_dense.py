@@ -505,6 +505,39 @@ def test_whole_and_cut_tiles_in_one_call(cuda):
     np.testing.assert_array_equal(got, dense_device(torch, X, W, b, act=1))
 
 
+@pytest.mark.parametrize("K", [1001, 1004, 1005, 1008, 12, 3])
+def test_split_buffers_use_the_32_byte_row_pitch(cuda, K):
+    """b200_tf32_split_rows / _transpose write rows of split_pitch(K) = K
+    rounded up to 8 floats: pad columns zero, nothing past M * pitch (canary
+    words after the buffer stay untouched), and hi + lo is x to 2^-21."""
+    import torch
+    dev = torch.device("cuda:0")
+    L = _native.lib()
+    s = stream_ptr(torch)
+    M, N = 37, 29
+    kp = _native.split_pitch(K)
+    assert kp % 8 == 0 and K <= kp < K + 8
+    X, W, _ = _inputs(M, N, K, seed=K)
+    tX, tW = torch.from_numpy(X).to(dev), torch.from_numpy(W).to(dev)
+    canary = 64
+    for rows, call in ((M, lambda hi, lo: L.b200_tf32_split_rows(ptr(tX), K, M, K, ptr(hi),
+                                                                   ptr(lo), s)),
+                       (N, lambda hi, lo: L.b200_tf32_split_transpose(ptr(tW), N, K, N, ptr(hi),
+                                                                        ptr(lo), s))):
+        hi = torch.full((rows * kp + canary,), 5.0, device=dev)
+        lo = torch.full((rows * kp + canary,), 5.0, device=dev)
+        _native.check(call(hi, lo))
+        _native.check(L.b200_stream_sync(s))
+        h, l = hi.cpu().numpy(), lo.cpu().numpy()
+        assert (h[rows * kp:] == 5.0).all() and (l[rows * kp:] == 5.0).all()
+        h, l = h[:rows * kp].reshape(rows, kp), l[:rows * kp].reshape(rows, kp)
+        assert (h[:, K:] == 0).all() and (l[:, K:] == 0).all()
+        src = (X if rows == M else W.T).astype(np.float64)
+        # lo is the remainder truncated to tf32: hi + lo is x to 2^-21 relative
+        err = np.abs(h[:, :K].astype(np.float64) + l[:, :K] - src)
+        assert (err <= np.abs(src) * 2.0 ** -21).all()
+
+
 def test_split_rule_for_exact_and_non_finite_values(cuda):
     """tf32 split: zero -> (0, 0); a non-zero value exactly representable in
     tf32, and +-Inf -> lo = +-FLT_MIN with the value's sign (so that Inf times
