@@ -224,6 +224,21 @@ int b200_dense_f32_chain(const float* X, int64_t ldx, const float* Xlo, const fl
                          int64_t ldylo, int64_t M, int64_t N, int64_t K, int act, float alpha,
                          void* stream);
 
+/* b200_dense_f32_peers: b200_dense_f32 that also stores every final value
+ * of Y into npeers (0..7) other output buffers, at the same element offsets
+ * with the same pitch ldy: peer_y is a host array of device addresses, in
+ * practice the rows of this call inside other GPUs' output buffers mapped
+ * with b200_ipc_open. The GEMM epilogue (and the cut-tile reduction) write
+ * them with ordinary stores over NVLink as tiles finish, so a row-sharded
+ * layer assembles its full result on every GPU during the GEMM itself. The
+ * writes are complete when the call's work on `stream` is; the caller orders
+ * them against the peers (a stream synchronisation and a cross-process
+ * barrier). No counterpart in the reference, whose results never leave one
+ * device. */
+int b200_dense_f32_peers(const float* X, int64_t ldx, const float* W, int64_t ldw,
+                         const float* b, float* Y, int64_t ldy, float* const* peer_y, int npeers,
+                         int64_t M, int64_t N, int64_t K, int act, float alpha, void* stream);
+
 /* Cross-process device buffers for the all-gather of a row-sharded result:
  * b200_ipc_alloc allocates `bytes` on the current device and writes its
  * 64-byte CUDA IPC handle to handle_out; another rank maps it with

@@ -324,7 +324,24 @@ struct Epilogue {
   int64_t ldylo;  // layer's pre-split A_lo), pitch ldylo
   int stage_store;  // 1: coalesce the epilogue's stores through shared memory
   int bias_vec;     // bias non-null and 16-byte aligned: float4 bias loads
+  // Gathered result: every final value is also stored at the same element
+  // offset from each peer base (another GPU's output rows, mapped through
+  // CUDA IPC), with ordinary stores that travel over NVLink as tiles finish.
+  int npeers;
+  float* peer[kMaxEpiloguePeers];
 };
+
+// Final values: Y and every peer copy.
+__device__ __forceinline__ void store_final4(const Epilogue& ep, int64_t off, float4 v) {
+  *reinterpret_cast<float4*>(ep.Y + off) = v;
+#pragma unroll 1
+  for (int p = 0; p < ep.npeers; ++p) *reinterpret_cast<float4*>(ep.peer[p] + off) = v;
+}
+__device__ __forceinline__ void store_final1(const Epilogue& ep, int64_t off, float v) {
+  ep.Y[off] = v;
+#pragma unroll 1
+  for (int p = 0; p < ep.npeers; ++p) ep.peer[p][off] = v;
+}
 
 // Bias of columns c .. c+3 (c a multiple of 4 from a 16-byte aligned tile
 // origin), zeros without bias. Every lane of a warp loads the same values.
@@ -425,15 +442,15 @@ __device__ __forceinline__ void store_tile_row(const Epilogue& ep, const Unit& w
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const int r = k * 4 + (lane >> 3), ch = lane & 7;
-        *reinterpret_cast<float4*>(ep.Y + (row0 + r) * ep.ldy + col0 + cb * 32 + ch * 4) =
-            *reinterpret_cast<const float4*>(stage + r * 32 + ((ch ^ (r & 7)) << 2));
+        store_final4(ep, (row0 + r) * ep.ldy + col0 + cb * 32 + ch * 4,
+                     *reinterpret_cast<const float4*>(stage + r * 32 + ((ch ^ (r & 7)) << 2)));
       }
       __syncwarp();
     }
     return;
   }
   if (row >= ep.M) return;
-  float* dst = ep.Y + row * ep.ldy + col0;
+  const int64_t base = row * ep.ldy + col0;
 #pragma unroll
   for (int j = 0; j < 128; j += 4) {
     float4 bv;
@@ -450,12 +467,12 @@ __device__ __forceinline__ void store_tile_row(const Epilogue& ep, const Unit& w
     const float v2 = apply_act(acc[j + 2] + bv.z, ep.act, ep.alpha);
     const float v3 = apply_act(acc[j + 3] + bv.w, ep.act, ep.alpha);
     if (ep.vec_out && col0 + j + 4 <= ep.N) {
-      *reinterpret_cast<float4*>(dst + j) = make_float4(v0, v1, v2, v3);
+      store_final4(ep, base + j, make_float4(v0, v1, v2, v3));
     } else {
-      if (col0 + j < ep.N) dst[j] = v0;
-      if (col0 + j + 1 < ep.N) dst[j + 1] = v1;
-      if (col0 + j + 2 < ep.N) dst[j + 2] = v2;
-      if (col0 + j + 3 < ep.N) dst[j + 3] = v3;
+      if (col0 + j < ep.N) store_final1(ep, base + j, v0);
+      if (col0 + j + 1 < ep.N) store_final1(ep, base + j + 1, v1);
+      if (col0 + j + 2 < ep.N) store_final1(ep, base + j + 2, v2);
+      if (col0 + j + 3 < ep.N) store_final1(ep, base + j + 3, v3);
     }
     if (ep.Ylo && col0 + j < ep.N) {
       const float v[4] = {v0, v1, v2, v3};
@@ -1374,6 +1391,16 @@ static int dispatch_gemm(const float* xa, const float* xlo, int64_t ldx, bool fu
   return run_gemm<CfgBK16S4>(xa, xlo, ldx, fused, b, M, N, K, sc, ep, status, stream);
 }
 
+namespace {
+thread_local int tl_npeers = 0;
+thread_local float* tl_peers[kMaxEpiloguePeers] = {};
+}  // namespace
+
+void set_epilogue_peers(float* const* peers, int n) {
+  tl_npeers = (peers != nullptr && n > 0) ? std::min(n, kMaxEpiloguePeers) : 0;
+  for (int i = 0; i < kMaxEpiloguePeers; ++i) tl_peers[i] = i < tl_npeers ? peers[i] : nullptr;
+}
+
 static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool fused,
                             const BOp& bop, int64_t M, int64_t N, int64_t K, const float* bias,
                             float* Y, int64_t ldy, int act, float alpha, int splits,
@@ -1451,13 +1478,14 @@ __global__ void __launch_bounds__(256)
       if (bias && col + q < N) v[q] += bias[col + q];
       v[q] = apply_act(v[q], act, alpha);
     }
-    float* dst = Y + row * ldy + col;
+    // lo_ep carries Y, ldy and the peer copies of this call
+    const int64_t off = row * lo_ep.ldy + col;
     if (vec && col + 4 <= N) {
-      *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+      store_final4(lo_ep, off, make_float4(v[0], v[1], v[2], v[3]));
     } else {
 #pragma unroll
       for (int q = 0; q < 4; ++q)
-        if (col + q < N) dst[q] = v[q];
+        if (col + q < N) store_final1(lo_ep, off + q, v[q]);
     }
     if (lo_ep.Ylo) store_lo4(lo_ep, row, col, v);
   }
@@ -1501,6 +1529,11 @@ static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool
   ep.ldylo = ldylo;
   ep.stage_store = store_staging_enabled() ? 1 : 0;
   ep.bias_vec = (bias != nullptr && (reinterpret_cast<uintptr_t>(bias) & 15) == 0) ? 1 : 0;
+  ep.npeers = tl_npeers;
+  for (int i = 0; i < kMaxEpiloguePeers; ++i) {
+    ep.peer[i] = tl_peers[i];
+    if (i < ep.npeers && (reinterpret_cast<uintptr_t>(tl_peers[i]) & 15) != 0) ep.vec_out = 0;
+  }
   int rc = dispatch_gemm(xa, xlo, ldx, fused, bop, M, N, K, sc, ep, status, stream);
   if (rc != kOk || sc.rest == 0) return rc;
   const int tile_m = pair ? kPairBM : kBM;

@@ -34,6 +34,19 @@ int report_ok();
 // 64-byte TMA row segment of a K-major operand covers exactly two sectors
 // (with a pitch of 4 mod 8 floats, every other row straddles three).
 inline int64_t split_pitch(int64_t K) { return (K + 7) & ~int64_t(7); }
+// Gathered dense results: the f32 epilogue can also store every final value
+// into up to kMaxEpiloguePeers other GPUs' output buffers. The peer bases
+// (device addresses valid on the launching device, same element offsets and
+// pitch as Y) apply to the dense launches this thread makes while an
+// EpiloguePeersScope is alive.
+constexpr int kMaxEpiloguePeers = 7;
+void set_epilogue_peers(float* const* peers, int n);
+struct EpiloguePeersScope {
+  EpiloguePeersScope(float* const* peers, int n) { set_epilogue_peers(peers, n); }
+  ~EpiloguePeersScope() { set_epilogue_peers(nullptr, 0); }
+  EpiloguePeersScope(const EpiloguePeersScope&) = delete;
+  EpiloguePeersScope& operator=(const EpiloguePeersScope&) = delete;
+};
 int64_t dense_f32_workspace_bytes(int64_t M, int64_t N, int64_t K);
 int split_x_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xhi, float* xlo,
                 cudaStream_t stream);

@@ -935,6 +935,41 @@ int b200_dense_f32(const float* X, int64_t ldx, const float* W, int64_t ldw, con
   return rc ? rc : succeed();
 }
 
+int b200_dense_f32_peers(const float* X, int64_t ldx, const float* W, int64_t ldw,
+                         const float* b, float* Y, int64_t ldy, float* const* peer_y, int npeers,
+                         int64_t M, int64_t N, int64_t K, int act, float alpha, void* stream) {
+  int rc = validate_dense(X, ldx, W, ldw, Y, ldy, M, N, K, act);
+  if (rc) return rc;
+  if (npeers < 0 || npeers > kMaxEpiloguePeers || (npeers > 0 && peer_y == nullptr))
+    return fail(kErrInvalidArg, "npeers must be 0..7, with that many peer output pointers");
+  for (int i = 0; i < npeers; ++i)
+    if (peer_y[i] == nullptr) return fail(kErrInvalidArg, "null peer output");
+  DeviceCtx* c = nullptr;
+  if ((rc = current_ctx(&c))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* ws = nullptr;
+  if (M > 0 && N > 0 && K > 0) {
+    const size_t need = (size_t)dense_scratch_bytes(M, N, K);
+    std::lock_guard<std::mutex> lk(g_mu);
+    DevBuf& buf = c->scratch[st];
+    if (buf.n < need) {
+      // The old buffer may still be read by queued work on this stream.
+      B200_CUDA(cudaStreamSynchronize(st), "sync before scratch growth");
+      B200_CUDA(buf.reserve(need), "alloc scratch");
+    }
+    ws = buf.p;
+  }
+  {
+    const EpiloguePeersScope peers(peer_y, npeers);
+    rc = dense_device(c, X, ldx, W, ldw, b, Y, ldy, M, N, K, act, alpha, ws, st);
+  }
+  // K == 0 fills Y with act(b) by a separate kernel: fill the peers the same way
+  for (int i = 0; rc == kOk && K == 0 && i < npeers; ++i)
+    if (fill_bias_act_f32(b, peer_y[i], ldy, M, N, act, alpha, st) != kOk)
+      rc = fail(kErrCuda, "peer fill launch failed");
+  return rc ? rc : succeed();
+}
+
 int b200_dense_f32_chain(const float* X, int64_t ldx, const float* Xlo, const float* W,
                          int64_t ldw, const float* b, float* Y, int64_t ldy, float* Ylo,
                          int64_t ldylo, int64_t M, int64_t N, int64_t K, int act, float alpha,

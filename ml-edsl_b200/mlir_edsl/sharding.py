@@ -199,6 +199,43 @@ def gather_rows_ce(rows: int, N: int, compute_slab, *, slabs: int = 4, group=Non
     return buf.Y
 
 
+def dense_rows_fused(X_local, W, b, act: int, alpha: float, *, group=None):
+    """The gathered dense layer with the collective inside the GEMM: this
+    rank's rows are computed once by b200_dense_f32_peers, whose epilogue
+    stores every finished value both into this rank's region of its own
+    persistent IPC-shared output buffer and into the same region of every
+    peer's buffer (stores over NVLink while later tiles compute; no copy
+    pass). Returns the full [world * rows, N] result, valid until the next
+    call with the same shape on this group."""
+    import ctypes
+    import torch
+    import torch.distributed as dist
+    from . import _native
+    L = _native.lib()
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    rows, K = X_local.shape
+    N = W.shape[1]
+    if world - 1 > 7:
+        raise ValueError("the fused transport stores into at most 7 peers")
+    device = X_local.device
+    buf = _PeerRows.get(rows, N, device, group)
+    # every rank is done with the previous result held in its buffer
+    torch.cuda.current_stream(device).synchronize()
+    dist.barrier(group=group)
+    off = rank * rows * N * 4
+    peers = [buf.ptrs[p] + off for p in range(world) if p != rank]
+    arr = (ctypes.c_void_p * max(1, len(peers)))(*peers)
+    p = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None
+    st = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    _native.check(L.b200_dense_f32_peers(p(X_local), X_local.stride(0), p(W), W.stride(0), p(b),
+                                         ctypes.c_void_p(buf.local + off), N, arr, len(peers),
+                                         rows, N, K, act, alpha, st))
+    # this rank's stores have landed in every peer ...
+    torch.cuda.current_stream(device).synchronize()
+    dist.barrier(group=group)  # ... and every peer's stores in this buffer
+    return buf.Y
+
+
 def dense_rows(X_local, W, b=None, act: int = 1, alpha: float = 0.0, *, gather: bool = False,
                slabs: int = 4, group=None, reserve_sms: int = 8, transport: str = "ce"):
     """Y = act(X_local @ W + b) for this rank's rows on its GPU (torch f32
@@ -209,9 +246,11 @@ def dense_rows(X_local, W, b=None, act: int = 1, alpha: float = 0.0, *, gather: 
     the same number of rows). transport "ce" pushes finished slabs into the
     peers' IPC-mapped output buffers with the copy engines (no SMs, overlaps
     the next slab's GEMM; the result is a persistent buffer valid until the
-    next call of this shape); "nccl" all-gathers each slab with NCCL on a side
-    stream, with the GEMM's grid leaving `reserve_sms` SMs free for NCCL's
-    kernels (cap NCCL's CTAs to match, e.g. NCCL_MAX_CTAS)."""
+    next call of this shape); "fused" has the GEMM's epilogue store every
+    finished tile into the peers' buffers directly (one launch sequence, no
+    slabs; see dense_rows_fused); "nccl" all-gathers each slab with NCCL on a
+    side stream, with the GEMM's grid leaving `reserve_sms` SMs free for
+    NCCL's kernels (cap NCCL's CTAs to match, e.g. NCCL_MAX_CTAS)."""
     import ctypes
     import torch
     from . import _native
@@ -234,9 +273,11 @@ def dense_rows(X_local, W, b=None, act: int = 1, alpha: float = 0.0, *, gather: 
         return Y
     import torch.distributed as dist
     world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+    if transport == "fused" and world > 1:
+        return dense_rows_fused(X_local, W, b, act, alpha, group=group)
     if transport == "ce" and world > 1:
         return gather_rows_ce(M, N, compute, slabs=slabs, group=group, device=X_local.device)
-    if transport not in ("ce", "nccl"):
+    if transport not in ("ce", "nccl", "fused"):
         raise ValueError(f"unknown transport {transport!r}")
     limit = 0
     if world > 1 and reserve_sms > 0:

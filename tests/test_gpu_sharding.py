@@ -1,7 +1,8 @@
 """Row-sharded dense layer over 2 GPUs with a single-device result requested:
 dense_rows(gather=True) assembles Y on every rank slab by slab while later
-slabs compute, by peer DMA into IPC-mapped buffers (transport "ce") or by
-NCCL all-gather (transport "nccl"). Run as 2 ranks under torchrun; skipped with fewer
+slabs compute, by peer DMA into IPC-mapped buffers (transport "ce"), by
+NCCL all-gather (transport "nccl"), or by the GEMM epilogue's own stores into
+the peers' buffers (transport "fused"). Run as 2 ranks under torchrun; skipped with fewer
 than 2 GPUs."""
 import os
 import socket
@@ -33,7 +34,7 @@ b = rng.uniform(-1, 1, N).astype(np.float32)
 tX = torch.from_numpy(X[rank * rows:(rank + 1) * rows]).to(dev)
 tW, tb = torch.from_numpy(W).to(dev), torch.from_numpy(b).to(dev)
 ref = oracle.dense_f32(X, W, b, act=1)
-for transport in ("ce", "nccl"):
+for transport in ("ce", "nccl", "fused"):
     for slabs in (1, 3, 3):  # the repeated call reuses the persistent IPC buffers
         Y = dense_rows(tX, tW, tb, 1, 0.0, gather=True, slabs=slabs, transport=transport)
         torch.cuda.synchronize()
