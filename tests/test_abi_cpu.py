@@ -48,6 +48,20 @@ def test_version_and_counters():
     assert lib.b200_launch_count() >= 0
 
 
+def test_split_pitch_agrees_with_the_library():
+    """The frontend sizes chained layers' lo buffers with _native.split_pitch;
+    the library's scratch formula must use the same pitch (K rounded up to 8)
+    for every K residue."""
+    lib = _native.lib()
+    al = lambda b: (b + 255) // 256 * 256
+    M, N = 8192, 8192  # many tiles: no split-K partials in the formula
+    for K in range(1001, 1017):
+        kp = _native.split_pitch(K)
+        assert kp % 8 == 0 and K <= kp < K + 8
+        assert lib.b200_dense_f32_splits(M, N, K) == 1
+        assert lib.b200_dense_f32_workspace_bytes(M, N, K) == 2 * al(M * kp * 4) + 2 * al(N * kp * 4)
+
+
 def test_workspace_formula():
     lib = _native.lib()
     al = lambda b: (b + 255) // 256 * 256
