@@ -199,6 +199,16 @@ def gather_rows_ce(rows: int, N: int, compute_slab, *, slabs: int = 4, group=Non
     return buf.Y
 
 
+def fused_output_bases(ptrs, rank: int, rows: int, N: int):
+    """Where rank `rank`'s rows go in the gathered [world * rows, N] f32
+    result: (its own base, the same rows in every other rank's buffer).
+    ptrs[r] is rank r's buffer as mapped on this device (ptrs[rank] its own);
+    every buffer holds world * rows rows of N floats, this rank's at row
+    rank * rows."""
+    off = rank * rows * N * 4
+    return ptrs[rank] + off, [p + off for r, p in enumerate(ptrs) if r != rank]
+
+
 def dense_rows_fused(X_local, W, b, act: int, alpha: float, *, group=None):
     """The gathered dense layer with the collective inside the GEMM: this
     rank's rows are computed once by b200_dense_f32_peers, whose epilogue
@@ -222,13 +232,12 @@ def dense_rows_fused(X_local, W, b, act: int, alpha: float, *, group=None):
     # every rank is done with the previous result held in its buffer
     torch.cuda.current_stream(device).synchronize()
     dist.barrier(group=group)
-    off = rank * rows * N * 4
-    peers = [buf.ptrs[p] + off for p in range(world) if p != rank]
+    own, peers = fused_output_bases(buf.ptrs, rank, rows, N)
     arr = (ctypes.c_void_p * max(1, len(peers)))(*peers)
     p = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None
     st = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
     _native.check(L.b200_dense_f32_peers(p(X_local), X_local.stride(0), p(W), W.stride(0), p(b),
-                                         ctypes.c_void_p(buf.local + off), N, arr, len(peers),
+                                         ctypes.c_void_p(own), N, arr, len(peers),
                                          rows, N, K, act, alpha, st))
     # this rank's stores have landed in every peer ...
     torch.cuda.current_stream(device).synchronize()

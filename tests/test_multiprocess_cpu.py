@@ -161,3 +161,29 @@ def test_slab_bounds():
             assert all(r1 > r0 for r0, r1 in b)
             sizes = [r1 - r0 for r0, r1 in b]
             assert max(sizes) - min(sizes) <= 1
+
+
+def test_fused_output_bases():
+    """Each rank's rows land at row rank * rows of every buffer: its own and,
+    for the fused transport's epilogue stores, each peer's (never its own
+    twice), so the world's regions tile every buffer exactly once."""
+    for p in (ROOT, PKG_PARENT):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    from mlir_edsl.sharding import fused_output_bases
+    rows, N = 1000, 768
+    for world in (2, 3, 8):
+        size = world * rows * N * 4
+        ptrs = [0x7f0000000000 + r * (1 << 36) for r in range(world)]
+        written = {r: [] for r in range(world)}  # buffer -> regions stored into it
+        for rank in range(world):
+            own, peers = fused_output_bases(ptrs, rank, rows, N)
+            assert len(peers) == world - 1 <= 7
+            for base in [own] + peers:
+                owner = max(r for r in range(world) if ptrs[r] <= base)
+                assert base + rows * N * 4 <= ptrs[owner] + size
+                written[owner].append(base - ptrs[owner])
+            assert own == ptrs[rank] + rank * rows * N * 4
+        for r in range(world):
+            assert sorted(written[r]) == [q * rows * N * 4 for q in range(world)]
+
