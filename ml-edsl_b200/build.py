@@ -11,7 +11,6 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIBDIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIBDIR, "libb200edsl.so")
-PROBE_LIB = os.path.join(LIBDIR, "libb200probe.so")  # measurement probes (bench only)
 SOURCES = ["gemm_tf32x3.cu", "gemm_i32.cu", "gemm_i32_tc.cu", "elementwise.cu", "runtime.cu", "noalloc.cu", "reduce.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -38,11 +37,6 @@ def needs_build():
 
 
 def build(force=False, verbose=False, extra=()):
-    if force or not os.path.exists(PROBE_LIB) or (
-            os.path.getmtime(PROBE_LIB) < os.path.getmtime(os.path.join(CSRC, "probe_imad.cu"))):
-        os.makedirs(LIBDIR, exist_ok=True)
-        subprocess.run([nvcc()] + NVCC_FLAGS + [os.path.join(CSRC, "probe_imad.cu"), "-o",
-                                                PROBE_LIB], check=True)
     if not force and not needs_build():
         return LIB
     os.makedirs(LIBDIR, exist_ok=True)

@@ -109,7 +109,7 @@ int bias_act_f32(const float* X, int64_t ldx, const float* b, float* Y, int64_t 
   else
     bias_act_f32_kernel<<<grid_for(M * N), 256, 0, stream>>>(X, ldx, b, Y, ldy, M, N, act, alpha);
   count_launch();
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return launch_result();
 }
 
 int fill_bias_act_f32(const float* b, float* Y, int64_t ldy, int64_t M, int64_t N, int act,
@@ -118,7 +118,7 @@ int fill_bias_act_f32(const float* b, float* Y, int64_t ldy, int64_t M, int64_t 
   bias_act_f32_kernel<<<grid_for(M * N), 256, 0, stream>>>(nullptr, 0, b, Y, ldy, M, N, act,
                                                            alpha);
   count_launch();
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return launch_result();
 }
 
 int act_f32(const float* X, float* Y, int64_t count, int act, float alpha, cudaStream_t stream) {
@@ -127,7 +127,7 @@ int act_f32(const float* X, float* Y, int64_t count, int act, float alpha, cudaS
   act_f32_kernel<<<grid_for(vec ? count / 4 + 1 : count), 256, 0, stream>>>(X, Y, count, act,
                                                                             alpha, vec);
   count_launch();
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return launch_result();
 }
 
 int bias_add_i32(const int32_t* X, int64_t ldx, const int32_t* b, int32_t* Y, int64_t ldy,
@@ -135,7 +135,7 @@ int bias_add_i32(const int32_t* X, int64_t ldx, const int32_t* b, int32_t* Y, in
   if (M <= 0 || N <= 0) return kOk;
   bias_add_i32_kernel<<<grid_for(M * N), 256, 0, stream>>>(X, ldx, b, Y, ldy, M, N);
   count_launch();
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return launch_result();
 }
 
 }  // namespace b200

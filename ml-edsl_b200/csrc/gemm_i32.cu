@@ -133,7 +133,7 @@ int gemm_i32(const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb, int32
   dim3 grid((unsigned)((N + kIBN - 1) / kIBN), (unsigned)((M + kIBM - 1) / kIBM));
   gemm_i32_kernel<<<grid, 256, 0, stream>>>(A, lda, B, ldb, C, ldc, M, N, K, bias);
   count_launch();
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return launch_result();
 }
 
 }  // namespace b200

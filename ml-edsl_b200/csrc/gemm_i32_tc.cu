@@ -398,7 +398,7 @@ EncodeTiledFnQ encode_fn() {
 // Byte planes [4][rows][Kp] as a 3-D u8 tensor {Kp, rows, 4}; box {64, 128, 4}.
 int make_plane_map(CUtensorMap* map, const uint8_t* base, int64_t rows, int64_t Kp) {
   EncodeTiledFnQ enc = encode_fn();
-  if (!enc) return kErrDriver;
+  if (!enc) return driver_failure("cuTensorMapEncodeTiled entry point", 0);
   cuuint64_t dims[3] = {(cuuint64_t)Kp, (cuuint64_t)rows, 4};
   cuuint64_t strides[2] = {(cuuint64_t)Kp, (cuuint64_t)(rows * Kp)};
   cuuint32_t box[3] = {kQBK, 128, 4};
@@ -406,7 +406,7 @@ int make_plane_map(CUtensorMap* map, const uint8_t* base, int64_t rows, int64_t 
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(base), dims,
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? kOk : kErrDriver;
+  return r == CUDA_SUCCESS ? kOk : driver_failure("cuTensorMapEncodeTiled", (int)r);
 }
 
 int64_t al256(int64_t b) { return (b + 255) & ~int64_t(255); }
@@ -479,7 +479,7 @@ int gemm_i32_tc(const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb,
   if (!(attr_done.load() & bit)) {
     if (cudaFuncSetAttribute(gemm_i32_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kQSmemBytes) != cudaSuccess)
-      return kErrCuda;
+      return launch_result();
     attr_done.fetch_or(bit);
   }
   static int sms[64] = {0};
@@ -503,7 +503,7 @@ int gemm_i32_tc(const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb,
   i32_planes_kernel<<<(unsigned)(a_blocks + b_blocks), 256, 0, stream>>>(
       A, lda, M, B, ldb, N, K, Kp, a_blocks, tiles_n32, b_tiles, Ap, Bp);
   count_launch();
-  if (cudaGetLastError() != cudaSuccess) return kErrCuda;
+  if (const int lr = launch_result()) return lr;
 
   CUtensorMap ta, tb;
   int rc = make_plane_map(&ta, Ap, M, Kp);
@@ -533,13 +533,13 @@ int gemm_i32_tc(const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb,
   cfg.numAttrs = 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_i32_tc_kernel, ta, tb, sc, ep, status);
   count_launch();
-  if (e != cudaSuccess) return kErrCuda;
+  if (const int lr = launch_result(e)) return lr;
   if (sc.rest > 0) {
     const int64_t elems = (int64_t)sc.rest * kQBM * kQBN;
     const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((elems + 255) / 256, 148 * 16));
     piece_reduce_i32_kernel<<<blocks, 256, 0, stream>>>(part, sc, M, N, bias, C, ldc);
     count_launch();
-    if (cudaGetLastError() != cudaSuccess) return kErrCuda;
+    if (const int lr = launch_result()) return lr;
   }
   return kOk;
 }

@@ -1078,7 +1078,7 @@ __global__ void wait_timeout_selftest_kernel(uint64_t limit_ns, int* status) {
 int wait_timeout_selftest(uint64_t limit_ns, int* status, cudaStream_t stream) {
   wait_timeout_selftest_kernel<<<1, 32, 0, stream>>>(limit_ns, status);
   count_launch();
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return launch_result();
 }
 
 // ---------------------------------------------------------------------------
@@ -1143,7 +1143,7 @@ static int device_sm_count() {
 static int make_tmap(CUtensorMap* map, const float* base, int64_t cols, int64_t rows,
                      int64_t pitch, int box_rows, int bk) {
   EncodeTiledFn enc = get_encode_fn();
-  if (!enc) return kErrDriver;
+  if (!enc) return driver_failure("cuTensorMapEncodeTiled entry point", 0);
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)pitch * 4};
   cuuint32_t box[2] = {(cuuint32_t)bk, (cuuint32_t)box_rows};
@@ -1152,7 +1152,7 @@ static int make_tmap(CUtensorMap* map, const float* base, int64_t cols, int64_t 
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? kOk : kErrDriver;
+  return r == CUDA_SUCCESS ? kOk : driver_failure("cuTensorMapEncodeTiled", (int)r);
 }
 
 // Tensor map of a row-major [rows = K, cols = N] operand read MN-major, N a
@@ -1164,7 +1164,7 @@ static int make_tmap(CUtensorMap* map, const float* base, int64_t cols, int64_t 
 static int make_tmap_mn(CUtensorMap* map, const float* base, int64_t cols, int64_t rows,
                         int64_t pitch, int bk) {
   EncodeTiledFn enc = get_encode_fn();
-  if (!enc) return kErrDriver;
+  if (!enc) return driver_failure("cuTensorMapEncodeTiled entry point", 0);
   if (cols % 32) return kErrInvalidArg;
   cuuint64_t dims[3] = {32, (cuuint64_t)rows, (cuuint64_t)(cols / 32)};
   cuuint64_t strides[2] = {(cuuint64_t)pitch * 4, 128};
@@ -1174,7 +1174,7 @@ static int make_tmap_mn(CUtensorMap* map, const float* base, int64_t cols, int64
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? kOk : kErrDriver;
+  return r == CUDA_SUCCESS ? kOk : driver_failure("cuTensorMapEncodeTiled", (int)r);
 }
 
 // The B operand of one GEMM: K-major split W^T (hi, lo with pitch Kp), or
@@ -1203,7 +1203,7 @@ int split_w_f32(const float* W, int64_t ldw, int64_t K, int64_t N, float* whiT, 
   dim3 grid((unsigned)((N + 31) / 32), (unsigned)((Kp + 31) / 32));
   split_transpose_kernel<<<grid, dim3(32, 8), 0, stream>>>(W, ldw, K, N, Kp, whiT, wloT);
   count_launch();
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return launch_result();
 }
 
 int split_x_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xhi, float* xlo,
@@ -1214,7 +1214,7 @@ int split_x_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xhi, f
   if (blocks < 1) blocks = 1;
   split_rows_kernel<<<blocks, 256, 0, stream>>>(X, ldx, M, K, Kp, xhi, xlo);
   count_launch();
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return launch_result();
 }
 
 // Ring configuration used by gemm_tf32x3_presplit. B200_GEMM_RING=bk32s2
@@ -1283,7 +1283,7 @@ static int launch_gemm(const CUtensorMap& ta_hi, const CUtensorMap& ta_lo,
     if (cudaFuncSetAttribute(gemm_tf32x3_kernel<Cfg, kFusedA, kBMn, kFuseB>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Cfg::SmemBytes) != cudaSuccess)
-      return kErrCuda;
+      return launch_result();
     attr_done.fetch_or(bit);
   }
   const int units = sc.units;
@@ -1303,7 +1303,7 @@ static int launch_gemm(const CUtensorMap& ta_hi, const CUtensorMap& ta_lo,
                        Cfg::SmemBytes, stream, ta_hi, ta_lo, tb_hi,
                        tb_lo, sc, ep, status);
   count_launch();
-  return e == cudaSuccess ? kOk : kErrCuda;
+  return launch_result(e);
 }
 
 // A operand: hi from `xa` with row pitch ldx (the pre-split xhi with pitch
@@ -1359,7 +1359,7 @@ static int run_gemm_pair(const float* xa, const float* xlo, int64_t ldx, const f
   if (!(attr_done.load() & bit)) {
     if (cudaFuncSetAttribute(gemm_tf32x3_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Cfg::SmemBytes) != cudaSuccess)
-      return kErrCuda;
+      return launch_result();
     attr_done.fetch_or(bit);
   }
   const int64_t Kp = split_pitch(K);
@@ -1376,7 +1376,7 @@ static int run_gemm_pair(const float* xa, const float* xlo, int64_t ldx, const f
   gemm_tf32x3_pair_kernel<<<2 * pairs, kThreads, Cfg::SmemBytes, stream>>>(
       ta_hi, ta_lo, tb_hi, tb_lo, sc, ep, status);
   count_launch();
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return launch_result();
 }
 
 static bool use_pair(bool fused, const BOp& b) { return !fused && !b.mn && pair_variant(); }
@@ -1544,7 +1544,7 @@ static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool
                                          static_cast<const float*>(partials), sc, tile_m, M, N,
                                          bias, act, alpha, Y, ldy, ep.vec_out, ep);
   count_launch();
-  return e == cudaSuccess ? kOk : kErrCuda;
+  return launch_result(e);
 }
 
 int gemm_tf32x3_splitk(const float* xhi, const float* xlo, const float* whiT, const float* wloT,
@@ -1566,7 +1566,7 @@ int split_xw_f32(const float* X, int64_t ldx, int64_t M, const float* W, int64_t
   split_xw_kernel<<<(unsigned)(x_blocks + w_blocks), 256, 0, stream>>>(
       X, ldx, M, x_blocks, xhi, xlo, W, ldw, K, N, Kp, tiles_n, whiT, wloT);
   count_launch();
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return launch_result();
 }
 
 int split_x_lo_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xlo,
@@ -1577,7 +1577,7 @@ int split_x_lo_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xlo
   if (blocks < 1) blocks = 1;
   split_rows_lo_kernel<<<blocks, 256, 0, stream>>>(X, ldx, M, K, Kp, xlo);
   count_launch();
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return launch_result();
 }
 
 int gemm_tf32x3_xraw(const float* X, int64_t ldx, const float* xlo, const float* whiT,
@@ -1641,7 +1641,7 @@ int split_lo_xw_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xh
   split_lo_xw_kernel<<<(unsigned)(x_blocks + w_blocks), 256, 0, stream>>>(
       X, ldx, M, K, Kp, x_blocks, xhi, xlo, W, ldw, N, Np, wlo);
   count_launch();
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return launch_result();
 }
 
 int gemm_tf32x3_wmn(const float* xa, const float* xlo, int64_t ldx, const float* W, int64_t ldw,

@@ -28,6 +28,14 @@ void count_launch();
 int report_error(int code, const char* msg);
 int report_ok();
 
+// Status of the kernel launch just queued on this thread: kOk, or kErrCuda
+// with the CUDA error's text kept for launch_error_text() (the error is
+// cleared). driver_failure() keeps the text of a failed driver call (tensor
+// map encoding) the same way and returns kErrDriver.
+int launch_result(cudaError_t e = cudaGetLastError());
+int driver_failure(const char* what, int code);
+const char* launch_error_text();
+
 // ---- 3xTF32 GEMM (gemm_tf32x3.cu)
 // Row pitch (floats) of every tf32 hi/lo split buffer of K columns: K
 // rounded up to 8, so that every row starts on a 32-byte L2 sector and each

@@ -12,7 +12,7 @@
 // Cost and limits:
 //   * every GPU that loads this library holds kNoAllocScratchBytes (64 MiB)
 //     of device memory for the array until the process exits;
-//   * a problem fits when 8 * (M + N) * roundup(K, 4) bytes (plus 256-byte
+//   * a problem fits when 8 * (M + N) * roundup(K, 8) bytes (plus 256-byte
 //     alignment of the four split regions) is at most 64 MiB, e.g.
 //     M = N = K = 2040; larger problems are rejected with B200_ERR_TOO_LARGE;
 //   * all calls on a device share the one array and it keeps the last
@@ -89,6 +89,17 @@ int cuda_error(cudaError_t e, const char* what) {
   return report_error(kErrCuda, buf);
 }
 
+// A launch step failed: its own status and message. Steps queued before it
+// may still be using the shared array, so the stream is drained first (the
+// array is free again when the call returns, on every path).
+int step_error(int rc, const char* step, cudaStream_t st) {
+  char buf[240];
+  snprintf(buf, sizeof buf, "b200_dense_f32_noalloc: %s: %s", step, launch_error_text());
+  cudaStreamSynchronize(st);
+  cudaGetLastError();
+  return report_error(rc, buf);
+}
+
 }  // namespace
 }  // namespace b200
 
@@ -145,15 +156,21 @@ extern "C" int b200_dense_f32_noalloc(const float* X, int64_t ldx, const float* 
     // rewritten (padding columns included) before the GEMM reads them.
     e = cudaMemsetAsync(addr.status, 0, sizeof(int), st);
     if (e != cudaSuccess) return cuda_error(e, "clear status");
+    const char* step = "split of W";
     rc = split_w_f32(W, ldw, K, N, whi, wlo, st);
-    if (rc == kOk) rc = split_x_f32(X, ldx, M, K, xhi, xlo, st);
-    if (rc == kOk)
+    if (rc == kOk) {
+      step = "split of X";
+      rc = split_x_f32(X, ldx, M, K, xhi, xlo, st);
+    }
+    if (rc == kOk) {
+      step = "GEMM";
       rc = gemm_tf32x3_presplit(xhi, xlo, whi, wlo, M, N, K, b, Y, ldy, act, alpha, addr.status,
                                 st);
-    if (rc) return cuda_error(cudaGetLastError(), "dense launch");
+    }
+    if (rc) return step_error(rc, step, st);
   } else {
     rc = fill_bias_act_f32(b, Y, ldy, M, N, act, alpha, st);
-    if (rc) return cuda_error(cudaGetLastError(), "bias launch");
+    if (rc) return step_error(rc, "bias fill", st);
   }
 
   // Synchronous: the shared scratch is free again when the call returns.

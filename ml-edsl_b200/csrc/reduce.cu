@@ -190,7 +190,7 @@ static int reduce_impl(const T* x, const T* y, int64_t n, int op, T init, T* out
   count_launch();
   reduce_pass2<T><<<1, kRedThreads, 0, st>>>(partials, (int)blocks, op, init, out);
   count_launch();
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  return launch_result();
 }
 
 int reduce_f32(const float* x, const float* y, int64_t n, int op, float init, float* out,

@@ -17,6 +17,7 @@
 #include <cmath>
 #include <cstring>
 #include <map>
+#include <memory>
 #include <mutex>
 #include <string>
 #include <thread>
@@ -83,6 +84,15 @@ struct DevBuf {
 };
 
 constexpr int kRing = 3;  // slab buffers in flight per device
+
+// Scratch of the device-pointer calls on one (device, stream). Its mutex is
+// held from the size check until the call has queued every kernel that uses
+// the buffer, so a second host thread on the same stream can neither free it
+// (growth) nor hand it out while the first is still enqueueing.
+struct StreamScratch {
+  std::mutex mu;
+  DevBuf buf;
+};
 
 // Grow-only page-locked host buffer (staging for pageable user memory).
 struct PinnedBuf {
@@ -213,8 +223,9 @@ struct DeviceCtx {
   PinnedBuf sx[kRing], sy[kRing];  // staging for pageable X / Y slabs
   PinnedBuf sc[2];                 // chunk staging for other pageable copies
   cudaEvent_t ev_h2d[kRing], ev_comp[kRing], ev_d2h[kRing], ev_sc[2];
-  // device-pointer call scratch, keyed by stream
-  std::map<cudaStream_t, DevBuf> scratch;
+  // device-pointer call scratch, keyed by stream (entries are never erased:
+  // a lease may hold a pointer to one while another thread releases buffers)
+  std::map<cudaStream_t, std::unique_ptr<StreamScratch>> scratch;
 };
 
 std::mutex g_mu;
@@ -264,6 +275,33 @@ int current_ctx(DeviceCtx** out) {
   B200_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   return get_ctx(dev, out);
 }
+
+// Exclusive use of the (device, stream) scratch, at least `need` bytes,
+// until the lease goes out of scope. Growing first drains the stream: work
+// queued by earlier leases may still read the old buffer.
+class ScratchLease {
+ public:
+  int acquire(DeviceCtx* c, cudaStream_t st, size_t need) {
+    StreamScratch* e = nullptr;
+    {
+      std::lock_guard<std::mutex> g(g_mu);
+      auto& slot = c->scratch[st];
+      if (!slot) slot.reset(new StreamScratch);
+      e = slot.get();
+    }
+    lk_ = std::unique_lock<std::mutex>(e->mu);
+    if (e->buf.n < need) {
+      B200_CUDA(cudaStreamSynchronize(st), "sync before scratch growth");
+      B200_CUDA(e->buf.reserve(need), "alloc scratch");
+    }
+    p = e->buf.p;
+    return kOk;
+  }
+  void* p = nullptr;
+
+ private:
+  std::unique_lock<std::mutex> lk_;
+};
 
 // Pageable copies at least this large go through the pinned staging chunks.
 constexpr int64_t kStageMin = (int64_t)16 << 20;
@@ -467,8 +505,7 @@ int dense_device(DeviceCtx* c, const float* X, int64_t ldx, const float* W, int6
       rc = gemm_tf32x3_splitk(s.xhi, s.xlo, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha, splits,
                               s.partials, c->status, st, ylo, ldylo);
   }
-  if (rc != kOk) return fail(rc, std::string("dense_f32 launch failed: ") +
-                                     cudaGetErrorString(cudaGetLastError()));
+  if (rc != kOk) return fail(rc, std::string("dense_f32: ") + launch_error_text());
   return kOk;
 }
 
@@ -558,10 +595,10 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
     // A single-slab call splits W together with X (one launch) below.
     if (nslab > 1 && wmn && !w_lo_in_kernel()) {
       rc = split_lo_xw_f32(nullptr, 0, 0, K, nullptr, nullptr, dW, N, N, dWhi, c->s_comp);
-      if (rc) return fail(rc, "split W launch failed");
+      if (rc) return fail(rc, std::string("split W launch failed: ") + launch_error_text());
     } else if (!wmn && (nslab > 1 || fuse_a(static_cast<float*>(c->x[0].p), K))) {
       rc = split_w_f32(dW, N, K, N, dWhi, dWlo, c->s_comp);
-      if (rc) return fail(rc, "split W launch failed");
+      if (rc) return fail(rc, std::string("split W launch failed: ") + launch_error_text());
     }
   }
 
@@ -628,7 +665,7 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
                                   splits, part, c->status, c->s_comp);
       }
     }
-    if (rc) return fail(rc, "dense kernel launch failed");
+    if (rc) return fail(rc, std::string("dense kernel launch failed: ") + launch_error_text());
     B200_CUDA(cudaEventRecord(c->ev_comp[slot], c->s_comp), "record");
     B200_CUDA(cudaStreamWaitEvent(c->s_d2h, c->ev_comp[slot], 0), "wait");
     if (stage_y) {
@@ -737,7 +774,7 @@ int simple_host_i32_matmul(int dev, const int32_t* A, int64_t lda, const int32_t
   if (bias) B200_CUDA(cudaMemcpyAsync(db, bias, N * 4, cudaMemcpyHostToDevice, s), "H2D bias");
   rc = matmul_i32_device(c, dA, K, dB, N, db, dC, N, M, N, K, ws_bytes ? c->xhi[0].p : nullptr,
                          s);
-  if (rc) return fail(rc, "i32 matmul launch failed");
+  if (rc) return fail(rc, std::string("i32 matmul launch failed: ") + launch_error_text());
   if ((rc = d2h_rows(c, C, ldc * 4, dC, N * 4, N * 4, M, s))) return rc;
   return kOk;
 }
@@ -758,7 +795,7 @@ int elementwise_host(size_t in_bytes_x, const void* X, size_t in_bytes_b, const 
   if ((rc = h2d_flat(c, c->x[0].p, X, (int64_t)in_bytes_x, s))) return rc;
   if (b) B200_CUDA(cudaMemcpyAsync(c->bias.p, b, in_bytes_b, cudaMemcpyHostToDevice, s), "H2D b");
   rc = launch(c->x[0].p, b ? c->bias.p : nullptr, c->y[0].p, s);
-  if (rc) return fail(rc, "elementwise launch failed");
+  if (rc) return fail(rc, std::string("elementwise launch failed: ") + launch_error_text());
   return d2h_flat(c, Y, c->y[0].p, (int64_t)out_bytes, s);
 }
 
@@ -786,7 +823,7 @@ int reduce_host_impl(const T* x, const T* y, int64_t n, int op, T init, T* resul
   else
     rc = reduce_i32(static_cast<const int32_t*>(c->x[0].p),
                     y ? static_cast<const int32_t*>(c->w.p) : nullptr, n, op, init, dout, scratch, s);
-  if (rc) return fail(rc, "reduction launch failed");
+  if (rc) return fail(rc, std::string("reduction launch failed: ") + launch_error_text());
   B200_CUDA(cudaMemcpyAsync(result, dout, sizeof(T), cudaMemcpyDeviceToHost, s), "D2H result");
   B200_CUDA(cudaStreamSynchronize(s), "sync");
   return kOk;
@@ -801,26 +838,34 @@ int reduce_device_impl(const T* x, const T* y, int64_t n, int op, T init, T* out
   int rc = current_ctx(&c);
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  void* ws = nullptr;
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    DevBuf& buf = c->scratch[st];
-    if (buf.n < (size_t)reduce_scratch_bytes()) {
-      B200_CUDA(cudaStreamSynchronize(st), "sync before scratch growth");
-      B200_CUDA(buf.reserve(reduce_scratch_bytes()), "alloc scratch");
-    }
-    ws = buf.p;
-  }
+  ScratchLease lease;  // held until the reduction is queued
+  if ((rc = lease.acquire(c, st, (size_t)reduce_scratch_bytes()))) return rc;
+  void* ws = lease.p;
   if constexpr (std::is_same<T, float>::value)
     rc = reduce_f32(x, y, n, op, init, out, ws, st);
   else
     rc = reduce_i32(x, y, n, op, init, out, ws, st);
-  return rc ? fail(rc, "reduction launch failed") : kOk;
+  return rc ? fail(rc, std::string("reduction launch failed: ") + launch_error_text()) : kOk;
 }
 }  // namespace
 
 int report_error(int code, const char* msg) { return fail(code, msg); }
 int report_ok() { return succeed(); }
+
+namespace {
+thread_local std::string t_launch_err;
+}
+int launch_result(cudaError_t e) {
+  if (e == cudaSuccess) return kOk;
+  cudaGetLastError();  // clear the non-sticky error
+  t_launch_err = std::string("kernel launch: ") + cudaGetErrorString(e);
+  return kErrCuda;
+}
+int driver_failure(const char* what, int code) {
+  t_launch_err = std::string(what) + " failed (CUresult " + std::to_string(code) + ")";
+  return kErrDriver;
+}
+const char* launch_error_text() { return t_launch_err.c_str(); }
 
 }  // namespace b200
 
@@ -873,8 +918,15 @@ int b200_release(void) {
       c.sx[i].release();
       c.sy[i].release();
     }
-    for (auto& kv : c.scratch) kv.second.release();
-    c.scratch.clear();
+    std::vector<StreamScratch*> entries;
+    {
+      std::lock_guard<std::mutex> g(g_mu);
+      for (auto& kv : c.scratch) entries.push_back(kv.second.get());
+    }
+    for (StreamScratch* e : entries) {
+      std::lock_guard<std::mutex> el(e->mu);
+      e->buf.release();
+    }
   }
   if (have_prev) cudaSetDevice(prev);
   return succeed();
@@ -920,16 +972,11 @@ int b200_dense_f32(const float* X, int64_t ldx, const float* W, int64_t ldw, con
   if ((rc = current_ctx(&c))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   void* ws = nullptr;
+  ScratchLease lease;  // held until the kernels that use ws are queued
   if (M > 0 && N > 0 && K > 0) {
     const size_t need = (size_t)dense_scratch_bytes(M, N, K);
-    std::lock_guard<std::mutex> lk(g_mu);
-    DevBuf& buf = c->scratch[st];
-    if (buf.n < need) {
-      // The old buffer may still be read by queued work on this stream.
-      B200_CUDA(cudaStreamSynchronize(st), "sync before scratch growth");
-      B200_CUDA(buf.reserve(need), "alloc scratch");
-    }
-    ws = buf.p;
+    if ((rc = lease.acquire(c, st, need))) return rc;
+    ws = lease.p;
   }
   rc = dense_device(c, X, ldx, W, ldw, b, Y, ldy, M, N, K, act, alpha, ws, st);
   return rc ? rc : succeed();
@@ -948,16 +995,11 @@ int b200_dense_f32_peers(const float* X, int64_t ldx, const float* W, int64_t ld
   if ((rc = current_ctx(&c))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   void* ws = nullptr;
+  ScratchLease lease;  // held until the kernels that use ws are queued
   if (M > 0 && N > 0 && K > 0) {
     const size_t need = (size_t)dense_scratch_bytes(M, N, K);
-    std::lock_guard<std::mutex> lk(g_mu);
-    DevBuf& buf = c->scratch[st];
-    if (buf.n < need) {
-      // The old buffer may still be read by queued work on this stream.
-      B200_CUDA(cudaStreamSynchronize(st), "sync before scratch growth");
-      B200_CUDA(buf.reserve(need), "alloc scratch");
-    }
-    ws = buf.p;
+    if ((rc = lease.acquire(c, st, need))) return rc;
+    ws = lease.p;
   }
   {
     const EpiloguePeersScope peers(peer_y, npeers);
@@ -966,7 +1008,7 @@ int b200_dense_f32_peers(const float* X, int64_t ldx, const float* W, int64_t ld
   // K == 0 fills Y with act(b) by a separate kernel: fill the peers the same way
   for (int i = 0; rc == kOk && K == 0 && i < npeers; ++i)
     if (fill_bias_act_f32(b, peer_y[i], ldy, M, N, act, alpha, st) != kOk)
-      rc = fail(kErrCuda, "peer fill launch failed");
+      rc = fail(kErrCuda, std::string("peer fill launch failed: ") + launch_error_text());
   return rc ? rc : succeed();
 }
 
@@ -984,16 +1026,11 @@ int b200_dense_f32_chain(const float* X, int64_t ldx, const float* Xlo, const fl
   if ((rc = current_ctx(&c))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   void* ws = nullptr;
+  ScratchLease lease;  // held until the kernels that use ws are queued
   if (M > 0 && N > 0 && K > 0) {
     const size_t need = (size_t)dense_scratch_bytes(M, N, K);
-    std::lock_guard<std::mutex> lk(g_mu);
-    DevBuf& buf = c->scratch[st];
-    if (buf.n < need) {
-      // The old buffer may still be read by queued work on this stream.
-      B200_CUDA(cudaStreamSynchronize(st), "sync before scratch growth");
-      B200_CUDA(buf.reserve(need), "alloc scratch");
-    }
-    ws = buf.p;
+    if ((rc = lease.acquire(c, st, need))) return rc;
+    ws = lease.p;
   }
   rc = dense_device(c, X, ldx, W, ldw, b, Y, ldy, M, N, K, act, alpha, ws, st, Xlo, Ylo, ldylo);
   return rc ? rc : succeed();
@@ -1009,19 +1046,14 @@ int b200_matmul_i32(const int32_t* A, int64_t lda, const int32_t* B, int64_t ldb
   if ((rc = current_ctx(&c))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   void* ws = nullptr;
+  ScratchLease lease;  // held until the kernels that use ws are queued
   const size_t need = (size_t)gemm_i32_tc_workspace_bytes(M, N, K);
   if (need && i32_tensor_core_enabled()) {
-    std::lock_guard<std::mutex> lk(g_mu);
-    DevBuf& buf = c->scratch[st];
-    if (buf.n < need) {
-      // The old buffer may still be read by queued work on this stream.
-      B200_CUDA(cudaStreamSynchronize(st), "sync before scratch growth");
-      B200_CUDA(buf.reserve(need), "alloc scratch");
-    }
-    ws = buf.p;
+    if ((rc = lease.acquire(c, st, need))) return rc;
+    ws = lease.p;
   }
   rc = matmul_i32_device(c, A, lda, B, ldb, bias, C, ldc, M, N, K, ws, st);
-  return rc ? fail(rc, "i32 matmul launch failed") : succeed();
+  return rc ? fail(rc, std::string("i32 matmul launch failed: ") + launch_error_text()) : succeed();
 }
 
 int b200_bias_act_f32(const float* X, int64_t ldx, const float* b, float* Y, int64_t ldy,
@@ -1030,14 +1062,14 @@ int b200_bias_act_f32(const float* X, int64_t ldx, const float* b, float* Y, int
   if (M > 0 && N > 0 && (!X || !Y || ldx < N || ldy < N))
     return fail(kErrInvalidArg, "null buffer or pitch < N");
   int rc = bias_act_f32(X, ldx, b, Y, ldy, M, N, act, alpha, static_cast<cudaStream_t>(stream));
-  return rc ? fail(rc, "bias/activation launch failed") : succeed();
+  return rc ? fail(rc, std::string("bias/activation launch failed: ") + launch_error_text()) : succeed();
 }
 
 int b200_act_f32(const float* X, float* Y, int64_t count, int act, float alpha, void* stream) {
   if (count < 0 || act < 0 || act > 2) return fail(kErrInvalidArg, "bad arguments");
   if (count > 0 && (!X || !Y)) return fail(kErrInvalidArg, "null buffer");
   int rc = act_f32(X, Y, count, act, alpha, static_cast<cudaStream_t>(stream));
-  return rc ? fail(rc, "activation launch failed") : succeed();
+  return rc ? fail(rc, std::string("activation launch failed: ") + launch_error_text()) : succeed();
 }
 
 int b200_bias_add_i32(const int32_t* X, int64_t ldx, const int32_t* b, int32_t* Y, int64_t ldy,
@@ -1046,7 +1078,7 @@ int b200_bias_add_i32(const int32_t* X, int64_t ldx, const int32_t* b, int32_t* 
   if (M > 0 && N > 0 && (!X || !b || !Y || ldx < N || ldy < N))
     return fail(kErrInvalidArg, "null buffer or pitch < N");
   int rc = bias_add_i32(X, ldx, b, Y, ldy, M, N, static_cast<cudaStream_t>(stream));
-  return rc ? fail(rc, "bias add launch failed") : succeed();
+  return rc ? fail(rc, std::string("bias add launch failed: ") + launch_error_text()) : succeed();
 }
 
 int b200_stream_sync(void* stream) {
@@ -1065,7 +1097,7 @@ int b200_tf32_split_rows(const float* X, int64_t ldx, int64_t M, int64_t K, floa
     return fail(kErrInvalidArg, "bad split_rows arguments");
   if (M == 0 || K == 0) return succeed();
   int rc = split_x_f32(X, ldx, M, K, hi, lo, static_cast<cudaStream_t>(stream));
-  return rc ? fail(rc, "split_rows launch failed") : succeed();
+  return rc ? fail(rc, std::string("split_rows launch failed: ") + launch_error_text()) : succeed();
 }
 
 int b200_tf32_split_transpose(const float* W, int64_t ldw, int64_t K, int64_t N, float* hiT,
@@ -1074,7 +1106,7 @@ int b200_tf32_split_transpose(const float* W, int64_t ldw, int64_t K, int64_t N,
     return fail(kErrInvalidArg, "bad split_transpose arguments");
   if (N == 0 || K == 0) return succeed();
   int rc = split_w_f32(W, ldw, K, N, hiT, loT, static_cast<cudaStream_t>(stream));
-  return rc ? fail(rc, "split_transpose launch failed") : succeed();
+  return rc ? fail(rc, std::string("split_transpose launch failed: ") + launch_error_text()) : succeed();
 }
 
 int b200_gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
@@ -1092,7 +1124,7 @@ int b200_gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* w
   if (M == 0 || N == 0) return succeed();
   if (K == 0) rc = fill_bias_act_f32(b, Y, ldy, M, N, act, alpha, st);
   else rc = gemm_tf32x3_presplit(xhi, xlo, whiT, wloT, M, N, K, b, Y, ldy, act, alpha, c->status, st);
-  return rc ? fail(rc, "gemm launch failed") : succeed();
+  return rc ? fail(rc, std::string("gemm launch failed: ") + launch_error_text()) : succeed();
 }
 
 int b200_dense_f32_wsplit(const float* X, int64_t ldx, const float* whiT, const float* wloT,
@@ -1111,7 +1143,7 @@ int b200_dense_f32_wsplit(const float* X, int64_t ldx, const float* whiT, const 
   if (M == 0 || N == 0) return succeed();
   if (K == 0) {
     rc = fill_bias_act_f32(b, Y, ldy, M, N, act, alpha, st);
-    return rc ? fail(rc, "launch failed") : succeed();
+    return rc ? fail(rc, std::string("launch failed: ") + launch_error_text()) : succeed();
   }
   const int splits = choose_splits(M, N, K);
   const bool fused = fuse_a(X, ldx);
@@ -1119,15 +1151,11 @@ int b200_dense_f32_wsplit(const float* X, int64_t ldx, const float* whiT, const 
   const int64_t Kp = split_pitch(K);
   const int64_t xsplit = fused ? 0 : 2 * round_up(M * Kp * 4, 256);
   void* ws = nullptr;
+  ScratchLease lease;  // held until the kernels that use ws are queued
   {
-    std::lock_guard<std::mutex> lk(g_mu);
-    DevBuf& buf = c->scratch[st];
     const size_t need = (size_t)(xsplit + splitk_partials_bytes(M, N, K)) + 256;
-    if (buf.n < need) {
-      B200_CUDA(cudaStreamSynchronize(st), "sync before scratch growth");
-      B200_CUDA(buf.reserve(need), "alloc scratch");
-    }
-    ws = buf.p;
+    if ((rc = lease.acquire(c, st, need))) return rc;
+    ws = lease.p;
   }
   float* part = reinterpret_cast<float*>(static_cast<char*>(ws) + xsplit);
   if (fused) {
@@ -1147,7 +1175,7 @@ int b200_dense_f32_wsplit(const float* X, int64_t ldx, const float* whiT, const 
       rc = gemm_tf32x3_splitk(xhi, xlo, whiT, wloT, M, N, K, b, Y, ldy, act, alpha, splits, part,
                               c->status, st);
   }
-  return rc ? fail(rc, "gemm launch failed") : succeed();
+  return rc ? fail(rc, std::string("gemm launch failed: ") + launch_error_text()) : succeed();
 }
 
 // ---------------------------------------------------------------- device buffers

@@ -32,6 +32,25 @@ def max_over_ranks(value: float, dist=None, device=None) -> float:
     return float(t.item())
 
 
+def check_equal_rows(rows: int, group=None, device=None) -> None:
+    """Raises ValueError on every rank unless every rank passes the same
+    `rows`. The gathered transports place rank r's rows at r * rows of every
+    rank's buffer and key their shared buffers by `rows`; unequal shards
+    (row_shards of M % world != 0 rows) would otherwise leave ranks in
+    mismatched collectives or store at offsets that disagree across ranks."""
+    import torch
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size(group) == 1:
+        return
+    on = device if dist.get_backend(group) == "nccl" else torch.device("cpu")
+    t = torch.tensor([int(rows), -int(rows)], dtype=torch.int64, device=on)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    hi, lo = int(t[0].item()), -int(t[1].item())
+    if hi != lo:
+        raise ValueError(f"gathered dense layer needs the same rows on every rank "
+                         f"(got {lo}..{hi}); pad the shards to ceil(M / world) rows")
+
+
 def slab_bounds(rows: int, slabs: int) -> List[Tuple[int, int]]:
     """[r0, r1) of `slabs` near-equal row slabs of `rows` rows (no empty slab)."""
     slabs = max(1, min(int(slabs), rows)) if rows > 0 else 1
@@ -282,12 +301,13 @@ def dense_rows(X_local, W, b=None, act: int = 1, alpha: float = 0.0, *, gather: 
         return Y
     import torch.distributed as dist
     world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+    if transport not in ("ce", "nccl", "fused"):
+        raise ValueError(f"unknown transport {transport!r}")
+    check_equal_rows(M, group, X_local.device)
     if transport == "fused" and world > 1:
         return dense_rows_fused(X_local, W, b, act, alpha, group=group)
     if transport == "ce" and world > 1:
         return gather_rows_ce(M, N, compute, slabs=slabs, group=group, device=X_local.device)
-    if transport not in ("ce", "nccl", "fused"):
-        raise ValueError(f"unknown transport {transport!r}")
     limit = 0
     if world > 1 and reserve_sms > 0:
         sms = torch.cuda.get_device_properties(X_local.device).multi_processor_count

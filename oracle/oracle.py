@@ -166,6 +166,10 @@ def gen_config_inputs(name):
         n = 4096 if name == "matmul_4096" else 8192
         rng = np.random.default_rng(2)
         return dict(A=u(rng, -1, 1, (n, n)), B=u(rng, -1, 1, (n, n)))
+    if name == "dense_8192":  # matmul_8192's A and B, then the bias
+        rng = np.random.default_rng(2)
+        return dict(A=u(rng, -1, 1, (8192, 8192)), B=u(rng, -1, 1, (8192, 8192)),
+                    b=u(rng, -1, 1, (8192,)))
     if name == "matmul_i32_2048":
         rng = np.random.default_rng(2)
         return dict(A=rng.integers(-8, 9, (2048, 2048), dtype=np.int32),

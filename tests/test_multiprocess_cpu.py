@@ -107,6 +107,30 @@ def _failing_rank_worker(rank, world, port, errq):
         errq.put((rank, traceback.format_exc()))
 
 
+def _unequal_rows_worker(rank, world, port, errq):
+    """Gathered dense layer with 3 rows on rank 0 and 2 on rank 1: every rank
+    raises the same ValueError before any buffer exchange or native call."""
+    try:
+        _init(rank, world, port)
+        import torch
+        import torch.distributed as dist
+        from mlir_edsl.sharding import dense_rows
+        rows = 3 - rank
+        X = torch.zeros((rows, 8))
+        W = torch.zeros((8, 4))
+        for transport in ("fused", "ce", "nccl"):
+            try:
+                dense_rows(X, W, None, 1, 0.0, gather=True, transport=transport)
+                errq.put((rank, f"{transport}: unequal rows accepted"))
+            except ValueError as e:
+                if "same rows" not in str(e) or "2..3" not in str(e):
+                    errq.put((rank, f"{transport}: unexpected message {e}"))
+        dist.barrier()  # both ranks are still in step
+        dist.destroy_process_group()
+    except Exception:
+        errq.put((rank, traceback.format_exc()))
+
+
 def _spawn(fn, world=2):
     ctx = mp.get_context("spawn")
     errq = ctx.Queue()
@@ -187,3 +211,8 @@ def test_fused_output_bases():
         for r in range(world):
             assert sorted(written[r]) == [q * rows * N * 4 for q in range(world)]
 
+
+
+def test_gathered_unequal_rows_rejected_on_every_rank_gloo_world2():
+    errs = _spawn(_unequal_rows_worker)
+    assert not errs, errs

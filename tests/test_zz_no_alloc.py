@@ -73,3 +73,22 @@ def test_noalloc_rejects_oversized_problem(cuda):
     rc = L.b200_dense_f32_noalloc(_p(X), K, _p(W), N, None, _p(Y), N, M, N, K, 0, 0.0, None)
     assert rc == 7  # B200_ERR_TOO_LARGE
     assert b"scratch" in L.b200_last_error()
+
+
+def test_noalloc_limit_is_exact(cuda):
+    """M = N = 2048: K = 2048 fills the 64 MiB array exactly (four split
+    regions of 2048 x 2048 floats) and runs; K = 2049 rounds the split pitch up
+    to 2056 and is rejected before anything is launched."""
+    import torch
+    M = N = 2048
+    X, W, b, (tX, tW, tb) = _case(torch, M, N, 2048, 9)
+    Y = torch.empty((M, N), device=tX.device)
+    ref_dev = _run(torch, "b200_dense_f32", tX, tW, tb, Y, M, N, 2048, 1)
+    got = _run(torch, "b200_dense_f32_noalloc", tX, tW, tb, Y, M, N, 2048, 1)
+    assert float(np.max(np.abs(got.astype(np.float64) - ref_dev))) <= oracle.f32_bound(2048, X, W)
+    L = _native.lib()
+    X2 = torch.zeros((M, 2049), device=tX.device)
+    W2 = torch.zeros((2049, N), device=tX.device)
+    rc = L.b200_dense_f32_noalloc(_p(X2), 2049, _p(W2), N, None, _p(Y), N, M, N, 2049, 0, 0.0,
+                                  None)
+    assert rc == 7  # B200_ERR_TOO_LARGE
