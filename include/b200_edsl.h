@@ -99,6 +99,12 @@ int b200_dense_f32(const float* X, int64_t ldx, const float* W, int64_t ldw, con
  * adds them in fixed order, so results are deterministic). */
 int b200_dense_f32_splits(int64_t M, int64_t N, int64_t K);
 
+/* Kernel launches of one b200_dense_f32 call: the operand split, the GEMM,
+ * and the cut-tile reduction when the problem is split (0 for an empty
+ * output, 1 for K == 0; -1 for negative sizes). No counterpart in the reference (its GPU path always launches fill,
+ * matmul and bias+relu: cpp/src/MLIRLowering.cpp:495-718). */
+int b200_dense_f32_launches(int64_t M, int64_t N, int64_t K);
+
 /* Same as b200_dense_f32 with caller-provided scratch of at least
  * b200_dense_f32_workspace_bytes(M, N, K) bytes (256-byte aligned). */
 int64_t b200_dense_f32_workspace_bytes(int64_t M, int64_t N, int64_t K);
@@ -232,12 +238,25 @@ int b200_dense_f32_chain(const float* X, int64_t ldx, const float* Xlo, const fl
  * them with ordinary stores over NVLink as tiles finish, so a row-sharded
  * layer assembles its full result on every GPU during the GEMM itself. The
  * writes are complete when the call's work on `stream` is; the caller orders
- * them against the peers (a stream synchronisation and a cross-process
- * barrier). No counterpart in the reference, whose results never leave one
- * device. */
+ * them against the peers, on the stream with b200_peer_barrier before and
+ * after the call. No counterpart in the reference, whose results never leave
+ * one device. */
 int b200_dense_f32_peers(const float* X, int64_t ldx, const float* W, int64_t ldw,
                          const float* b, float* Y, int64_t ldy, float* const* peer_y, int npeers,
                          int64_t M, int64_t N, int64_t K, int act, float alpha, void* stream);
+
+/* Stream-ordered barrier of the `world` GPUs (<= 8) of a gathered call, as
+ * one small kernel on `stream`: rank `rank` stores `epoch` into its slot of
+ * every peer's flag array (after a system-scope fence, so its earlier stores
+ * into peer memory land first) and waits until every peer has stored `epoch`
+ * (or a later epoch, modulo 2^32) into its own flag array. flags[r] is rank
+ * r's array of `world` 32-bit slots as addressed from this device (its own,
+ * or a peer's mapped with b200_ipc_open), zero before the first barrier;
+ * every rank passes the same epoch sequence. A wait longer than timeout_ns
+ * gives up: b200_stream_sync then returns B200_ERR_DEVICE_TIMEOUT and the
+ * context stays usable. No counterpart in the reference. */
+int b200_peer_barrier(uint32_t* const* flags, int world, int rank, uint32_t epoch,
+                      int64_t timeout_ns, void* stream);
 
 /* Cross-process device buffers for the all-gather of a row-sharded result:
  * b200_ipc_alloc allocates `bytes` on the current device and writes its

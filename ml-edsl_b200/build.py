@@ -11,7 +11,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIBDIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIBDIR, "libb200edsl.so")
-SOURCES = ["gemm_tf32x3.cu", "gemm_i32.cu", "gemm_i32_tc.cu", "elementwise.cu", "runtime.cu", "noalloc.cu", "reduce.cu"]
+SOURCES = ["gemm_tf32x3.cu", "gemm_i32.cu", "gemm_i32_tc.cu", "elementwise.cu", "runtime.cu", "noalloc.cu", "reduce.cu", "peer.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

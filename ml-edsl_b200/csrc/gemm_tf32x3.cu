@@ -31,8 +31,7 @@
 // (tile, K-split) units, in a grouped raster; 320 threads):
 //   warp 0      TMA producer: 4 tiles (A_hi, A_lo, B_hi, B_lo) per k-block
 //               into a shared-memory ring: 4 stages of 48 KB (BK = 16,
-//               64-byte swizzle) by default; a 2 x 96 KB ring (BK = 32,
-//               128-byte swizzle) is kept for comparison (B200_GEMM_RING).
+//               64-byte swizzle).
 //   warp 1      allocates 512 TMEM columns (2 chunk buffers); lane 0 issues 3
 //               tcgen05.mma per 8-wide k-step and frees ring stages and chunk
 //               buffers with tcgen05.commit.
@@ -92,8 +91,7 @@ struct RingCfg {
   static_assert(BK == 32 || BK == 16, "BK must be 32 (SW128) or 16 (SW64)");
   static_assert(SmemBytes <= 232448, "shared memory over the sm_100 limit");
 };
-using CfgBK32S2 = RingCfg<32, 2>;  // 2 stages of 96 KB
-using CfgBK16S4 = RingCfg<16, 4>;  // 4 stages of 48 KB
+using Cfg = RingCfg<16, 4>;  // 4 stages of 48 KB
 
 // x -> hi (tf32: low 13 mantissa bits cleared) + lo (the rest, truncated to
 // tf32). The products hi*hi + hi*lo + lo*hi approximate x*y to f32 level.
@@ -863,201 +861,6 @@ __global__ void __launch_bounds__(kThreads + (kFuseB ? 32 * kConvWarps : 0), 1)
   }
 }
 
-// ---------------------------------------------------------------------------
-// 2-SM variant (opt-in, B200_GEMM_2SM=1): a cluster of two CTAs computes a
-// 256 x 256 tile with tcgen05.mma.cta_group::2. Each CTA loads its 128 rows
-// of A and 128 of the 256 B columns (hi and lo) into its own ring: per SM,
-// B traffic is half that of the 1-SM kernel and a stage is 32 KB, so the ring
-// holds 6 stages. The even CTA issues every MMA (both CTAs' TMEM receive
-// their 128 rows x 256 columns); its commits are multicast to the barriers of
-// both CTAs. TMA completions of both CTAs land on the leader's full barrier,
-// whose expected byte count covers both. The peer's epilogue warps release a
-// TMEM chunk with a remote arrive on the leader's tempty barrier.
-struct PairCfg {
-  static constexpr int BK = 16;
-  static constexpr int Stages = 6;
-  static constexpr int ATileBytes = 128 * BK * 4;  // this CTA's 128 rows of A
-  static constexpr int BTileBytes = 128 * BK * 4;  // this CTA's 128 columns of B
-  static constexpr int StageBytes = 2 * ATileBytes + 2 * BTileBytes;  // 32 KB
-  static constexpr int ChunkKB = kChunkK / BK;
-  static constexpr uint32_t UmmaLayout = 4u;  // SWIZZLE_64B
-  static constexpr uint32_t SBO = 8 * BK * 4;
-  static constexpr int BarOffset = Stages * StageBytes;
-  static constexpr int SmemBytes = BarOffset + 256 + 1024;
-  static_assert(SmemBytes <= 232448, "shared memory over the sm_100 limit");
-};
-constexpr int kPairBM = 256;  // rows of a pair tile
-
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap tmAhi,
-                            const __grid_constant__ CUtensorMap tmAlo,
-                            const __grid_constant__ CUtensorMap tmBhi,
-                            const __grid_constant__ CUtensorMap tmBlo, Sched sc,
-                            Epilogue ep, int* status) {
-  using Cfg = PairCfg;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::BarOffset);  // (leader) TMA -> MMA
-  uint64_t* empty = full + Cfg::Stages;                                   // MMA -> TMA
-  uint64_t* tfull = empty + Cfg::Stages;  // MMA -> epilogue
-  uint64_t* tempty = tfull + 2;           // (leader) epilogues of both CTAs -> MMA
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_ctarank();
-  const bool leader = rank == 0;
-  const int pair = blockIdx.x >> 1;
-  const int npairs = gridDim.x >> 1;
-  auto unit_of = [&](int u) { return unit_at(sc, u, kPairBM, kBN); };
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < Cfg::Stages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 2 * kEpiWarps);
-    }
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmAhi);
-    tma_prefetch_desc(&tmAlo);
-    tma_prefetch_desc(&tmBhi);
-    tma_prefetch_desc(&tmBlo);
-  }
-  if (warp == 1) tmem_alloc_pair(tmem_slot, kTmemCols);
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync();  // both CTAs' barriers initialised before any remote use
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-
-  if (warp == 0) {
-    // ------------------------------------------------ TMA producer (both CTAs)
-    if (lane == 0) {
-      int it = 0;
-      for (int u = pair; u < sc.units && !*abort_flag; u += npairs) {
-        const Unit w = unit_of(u);
-        const int a_row = w.m0 + (int)rank * 128;
-        const int b_row = w.n0 + (int)rank * 128;
-        for (int kb = 0; kb < w.nkb; ++kb, ++it) {
-          const int s = it % Cfg::Stages;
-          const int round = it / Cfg::Stages;
-          if (round > 0 &&
-              !mbar_wait(&empty[s], (round - 1) & 1, status, kDevTimeoutEmpty, abort_flag))
-            break;
-          if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::StageBytes);
-          uint8_t* st = smem + s * Cfg::StageBytes;
-          const int kx = (w.kb0 + kb) * Cfg::BK;
-          tma_load_2d_pair(st, &tmAhi, &full[s], kx, a_row);
-          tma_load_2d_pair(st + Cfg::ATileBytes, &tmAlo, &full[s], kx, a_row);
-          tma_load_2d_pair(st + 2 * Cfg::ATileBytes, &tmBhi, &full[s], kx, b_row);
-          tma_load_2d_pair(st + 2 * Cfg::ATileBytes + Cfg::BTileBytes, &tmBlo, &full[s], kx,
-                           b_row);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------ MMA issuer (leader only)
-    if (leader && lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32_f32(kPairBM, kBN);
-      using D = UmmaDesc<Cfg>;
-      int it = 0, cc = 0;
-      bool ok = true;
-      for (int u = pair; u < sc.units && ok; u += npairs) {
-        const Unit w = unit_of(u);
-        for (int kb = 0; kb < w.nkb; ++kb, ++it) {
-          const int s = it % Cfg::Stages;
-          const int round = it / Cfg::Stages;
-          const int buf = cc & 1;
-          const bool chunk_start = (kb % Cfg::ChunkKB) == 0;
-          const bool chunk_end = (kb % Cfg::ChunkKB) == Cfg::ChunkKB - 1 || kb == w.nkb - 1;
-          if (chunk_start && cc >= 2) {
-            if (!mbar_wait(&tempty[buf], ((cc >> 1) - 1) & 1, status, kDevTimeoutAccum,
-                           abort_flag)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-          }
-          if (!mbar_wait(&full[s], round & 1, status, kDevTimeoutFull, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t d_tmem = tmem_base + buf * kBN;
-          const uint32_t st = smem_u32(smem + s * Cfg::StageBytes);
-#pragma unroll
-          for (int k = 0; k < Cfg::BK / 8; ++k) {
-            umma_tf32_pair(d_tmem, D::a_lo(st, k), D::b_hi(st, k), idesc,
-                           (chunk_start && k == 0) ? 0u : 1u);
-            umma_tf32_pair(d_tmem, D::a_hi(st, k), D::b_lo(st, k), idesc, 1u);
-            umma_tf32_pair(d_tmem, D::a_hi(st, k), D::b_hi(st, k), idesc, 1u);
-          }
-          umma_commit_pair(&empty[s], 0x3);  // both CTAs may refill stage s
-          if (chunk_end) {
-            umma_commit_pair(&tfull[buf], 0x3);
-            ++cc;
-          }
-        }
-      }
-    }
-  } else {
-    // ------------------------------------------------ epilogue (8 warps, both CTAs)
-    const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    float acc[128];
-    bool ok = true;
-    int ce = 0;
-#pragma unroll 1
-    for (int u = pair; u < sc.units && ok && !*abort_flag; u += npairs) {
-      const Unit w = unit_of(u);
-      const int num_chunks = (w.nkb + Cfg::ChunkKB - 1) / Cfg::ChunkKB;
-#pragma unroll
-      for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
-#pragma unroll 1
-      for (int c = 0; c < num_chunks && ok; ++c, ++ce) {
-        const int buf = ce & 1;
-        if (!mbar_wait(&tfull[buf], (ce >> 1) & 1, status, kDevTimeoutAccum, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t taddr = tmem_base + lane_off + buf * kBN + half * 128;
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(taddr + g * 32, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) acc[g * 32 + j] += __uint_as_float(r[j]);
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[buf]), 0));
-      }
-      if (!ok || *abort_flag) break;
-      store_tile_row<kPairBM>(ep, w, sc.rest, (int)rank * 128 + quarter * 32 + lane,
-                              half * 128, acc, nullptr, lane);
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync();  // the leader's MMAs into this CTA's TMEM are complete
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc_pair(tmem_base, kTmemCols);
-  }
-}
-
 // Failure-detection self-test: one thread waits, with the GEMM's bounded
 // wait, on an mbarrier that nothing ever arrives on. After `limit_ns` the
 // wait gives up and records kDevTimeoutSelfTest in the status word, exactly
@@ -1217,17 +1020,6 @@ int split_x_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xhi, f
   return launch_result();
 }
 
-// Ring configuration used by gemm_tf32x3_presplit. B200_GEMM_RING=bk32s2
-// selects the 2 x 96 KB ring (kept for A/B measurements); default 4 x 48 KB.
-static int ring_variant() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("B200_GEMM_RING");
-    v = (e && strcmp(e, "bk32s2") == 0) ? 0 : 1;
-  }
-  return v;
-}
-
 // Programmatic dependent launch (see pdl_wait) for problems of at most 2^33
 // multiply-adds (2048^3): there the launch and prologue latency it hides is
 // 10-20% of a call (dense 1024^3: 31.0 -> 26.9 us; 256^3: 22.7 -> 18.6 us);
@@ -1339,56 +1131,10 @@ static int run_gemm(const float* xa, const float* xlo, int64_t ldx, bool fused, 
                                         stream);
 }
 
-// B200_GEMM_2SM=1 selects the 2-SM (CTA pair) kernel for the non-fused path.
-static bool pair_variant() {
-  static const bool on = [] {
-    const char* e = getenv("B200_GEMM_2SM");
-    return e && e[0] == '1';
-  }();
-  return on;
-}
-
-static int run_gemm_pair(const float* xa, const float* xlo, int64_t ldx, const float* whiT,
-                         const float* wloT, int64_t M, int64_t N, int64_t K, const Sched& sc,
-                         const Epilogue& ep, int* status, cudaStream_t stream) {
-  using Cfg = PairCfg;
-  static std::atomic<uint64_t> attr_done{0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return kErrCuda;
-  const uint64_t bit = 1ull << (dev & 63);
-  if (!(attr_done.load() & bit)) {
-    if (cudaFuncSetAttribute(gemm_tf32x3_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Cfg::SmemBytes) != cudaSuccess)
-      return launch_result();
-    attr_done.fetch_or(bit);
-  }
-  const int64_t Kp = split_pitch(K);
-  CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
-  int rc = make_tmap(&ta_hi, xa, K, M, ldx, 128, Cfg::BK);
-  if (rc == kOk) rc = make_tmap(&ta_lo, xlo, K, M, Kp, 128, Cfg::BK);
-  if (rc == kOk) rc = make_tmap(&tb_hi, whiT, K, N, Kp, 128, Cfg::BK);
-  if (rc == kOk) rc = make_tmap(&tb_lo, wloT, K, N, Kp, 128, Cfg::BK);
-  if (rc != kOk) return rc;
-  const int units = sc.units;
-  const int sms = sm_count();
-  if (sms <= 0) return kErrCuda;
-  const int pairs = std::max(1, std::min(units, sms / 2));
-  gemm_tf32x3_pair_kernel<<<2 * pairs, kThreads, Cfg::SmemBytes, stream>>>(
-      ta_hi, ta_lo, tb_hi, tb_lo, sc, ep, status);
-  count_launch();
-  return launch_result();
-}
-
-static bool use_pair(bool fused, const BOp& b) { return !fused && !b.mn && pair_variant(); }
-
 static int dispatch_gemm(const float* xa, const float* xlo, int64_t ldx, bool fused, const BOp& b,
                          int64_t M, int64_t N, int64_t K, const Sched& sc, const Epilogue& ep,
                          int* status, cudaStream_t stream) {
-  if (use_pair(fused, b))
-    return run_gemm_pair(xa, xlo, ldx, b.hi, b.lo, M, N, K, sc, ep, status, stream);
-  if (ring_variant() == 0)
-    return run_gemm<CfgBK32S2>(xa, xlo, ldx, fused, b, M, N, K, sc, ep, status, stream);
-  return run_gemm<CfgBK16S4>(xa, xlo, ldx, fused, b, M, N, K, sc, ep, status, stream);
+  return run_gemm<Cfg>(xa, xlo, ldx, fused, b, M, N, K, sc, ep, status, stream);
 }
 
 namespace {
@@ -1416,26 +1162,21 @@ int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
 }
 
 // ---------------------------------------------------------------------------
-// Schedules (see sched.cuh). One 128 x 256 tile (256 x 256 for a CTA pair)
-// over all of K takes 2 * BM * 256 * K / 1.65e12 s per SM at the measured
-// 3xTF32 rate; a piece spans at least 128 of K (half a TMEM promotion
-// chunk: a piece may end mid-chunk). Cut tiles arise
-// when the last wave is partial: the 1024^3 layer (32 tiles), the MLP's
-// layers (172 and 64 tiles), 4096^3 (512 tiles = 3.46 waves).
-static Sched sched_f32(int64_t M, int64_t N, int64_t K, bool pair, int bk, bool allow_cut) {
+// Schedules (see sched.cuh). One 128 x 256 tile over all of K takes
+// 2 * BM * 256 * K / 1.65e12 s per SM at the measured 3xTF32 rate; a piece
+// spans at least 128 of K (half a TMEM promotion chunk: a piece may end
+// mid-chunk). Cut tiles arise when the last wave is partial: the 1024^3
+// layer (32 tiles), the MLP's layers (172 and 64 tiles), 4096^3 (512 tiles =
+// 3.46 waves).
+static Sched sched_f32(int64_t M, int64_t N, int64_t K, bool allow_cut) {
   const int sms = std::max(1, sm_count());
-  const int bm = pair ? kPairBM : kBM;
-  const int procs = pair ? std::max(1, sms / 2) : sms;
-  const double t_tile = 2.0 * bm * kBN * (double)K / (pair ? 2.0 : 1.0) / 1.65e12;
-  return make_sched(M, N, K, bm, kBN, bk, procs, t_tile, 4, 0, allow_cut ? 16 : 1,
-                    128 / bk /* pieces may end mid-chunk */, kGroupM);
+  const double t_tile = 2.0 * kBM * kBN * (double)K / 1.65e12;
+  return make_sched(M, N, K, kBM, kBN, Cfg::BK, sms, t_tile, 4, 0, allow_cut ? 16 : 1,
+                    128 / Cfg::BK /* pieces may end mid-chunk */, kGroupM);
 }
 
-static int default_bk() { return ring_variant() == 0 ? CfgBK32S2::BK : CfgBK16S4::BK; }
-
 void sched_query_f32(int64_t M, int64_t N, int64_t K, int64_t* out) {
-  const bool pair = pair_variant();
-  const Sched sc = sched_f32(M, N, K, pair, pair ? PairCfg::BK : default_bk(), true);
+  const Sched sc = sched_f32(M, N, K, true);
   const int64_t v[8] = {sc.tiles_m, sc.tiles_n, sc.whole, sc.rest, sc.pieces, sc.kb, sc.kbp,
                         sc.units};
   for (int i = 0; i < 8; ++i) out[i] = v[i];
@@ -1443,9 +1184,12 @@ void sched_query_f32(int64_t M, int64_t N, int64_t K, int64_t* out) {
 
 int choose_splits(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0) return 1;
-  const bool pair = pair_variant();
-  const Sched sc = sched_f32(M, N, K, pair, pair ? PairCfg::BK : default_bk(), true);
+  const Sched sc = sched_f32(M, N, K, true);
   return sc.rest > 0 ? sc.pieces : 1;
+}
+
+int gemm_f32_launches(int64_t M, int64_t N, int64_t K) {
+  return choose_splits(M, N, K) > 1 ? 2 : 1;
 }
 
 __global__ void __launch_bounds__(256)
@@ -1491,16 +1235,11 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// Bytes of cut-tile partial sums for a call of choose_splits(M, N, K) > 1
-// (the larger of the 1-SM and CTA-pair schedules when the pair kernel is
-// selected, since the fused-A path keeps the 1-SM kernel).
+// Bytes of cut-tile partial sums for a call of choose_splits(M, N, K) > 1.
 int64_t splitk_partials_bytes(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
-  auto bytes = [&](bool pair) -> int64_t {
-    const Sched sc = sched_f32(M, N, K, pair, pair ? PairCfg::BK : default_bk(), true);
-    return sc.rest > 0 ? (int64_t)sc.pieces * sc.rest * (pair ? kPairBM : kBM) * kBN * 4 : 0;
-  };
-  const int64_t b = std::max(bytes(false), pair_variant() ? bytes(true) : int64_t(0));
+  const Sched sc = sched_f32(M, N, K, true);
+  const int64_t b = sc.rest > 0 ? (int64_t)sc.pieces * sc.rest * kBM * kBN * 4 : 0;
   return b ? (b + 255) & ~int64_t(255) : 0;
 }
 
@@ -1512,9 +1251,7 @@ static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool
                             float* Y, int64_t ldy, int act, float alpha, int splits,
                             float* partials, int* status, cudaStream_t stream, float* ylo,
                             int64_t ldylo) {
-  const bool pair = use_pair(fused, bop);
-  const Sched sc = sched_f32(M, N, K, pair, pair ? PairCfg::BK : default_bk(),
-                             splits > 1 && partials != nullptr);
+  const Sched sc = sched_f32(M, N, K, splits > 1 && partials != nullptr);
   Epilogue ep;
   ep.Y = Y;
   ep.ldy = ldy;
@@ -1536,7 +1273,7 @@ static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool
   }
   int rc = dispatch_gemm(xa, xlo, ldx, fused, bop, M, N, K, sc, ep, status, stream);
   if (rc != kOk || sc.rest == 0) return rc;
-  const int tile_m = pair ? kPairBM : kBM;
+  const int tile_m = kBM;
   const int64_t quads = (int64_t)sc.rest * tile_m * (kBN / 4);
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((quads + 255) / 256, 148 * 16));
   const cudaError_t e = launch_dependent(pdl_enabled(M, N, K), piece_reduce_kernel,
@@ -1613,7 +1350,7 @@ bool w_mn_ok(const float* W, int64_t ldw, int64_t M, int64_t N) {
     const char* e = getenv("B200_W_MN");
     return !(e && e[0] == '0');
   }();
-  return enabled && !pair_variant() && M <= 4096 && (N % 32) == 0 && ((ldw & 3) == 0) &&
+  return enabled && M <= 4096 && (N % 32) == 0 && ((ldw & 3) == 0) &&
          ((reinterpret_cast<uintptr_t>(W) & 15) == 0);
 }
 

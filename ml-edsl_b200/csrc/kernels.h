@@ -36,6 +36,18 @@ int launch_result(cudaError_t e = cudaGetLastError());
 int driver_failure(const char* what, int code);
 const char* launch_error_text();
 
+// ---- peer-GPU barrier of gathered calls (peer.cu)
+// flags[r]: rank r's flag array (world 32-bit slots) as addressed from this
+// device (its own array, or a peer's through a CUDA IPC mapping).
+constexpr int kMaxPeerRanks = 8;
+struct PeerFlags {
+  uint32_t* flags[kMaxPeerRanks];
+  int world;
+  int rank;
+};
+int peer_barrier(const PeerFlags& f, uint32_t epoch, uint64_t limit_ns, int* status,
+                 cudaStream_t stream);
+
 // ---- 3xTF32 GEMM (gemm_tf32x3.cu)
 // Row pitch (floats) of every tf32 hi/lo split buffer of K columns: K
 // rounded up to 8, so that every row starts on a 32-byte L2 sector and each
@@ -63,6 +75,8 @@ int split_w_f32(const float* W, int64_t ldw, int64_t K, int64_t N, float* whiT, 
 // Split-K (few-tile problems): splits chosen by a wave-count cost model;
 // partials scratch of splitk_partials_bytes() (0 when splits == 1).
 int choose_splits(int64_t M, int64_t N, int64_t K);
+// Kernel launches of one f32 GEMM call (1, or 2 with the cut-tile reduction).
+int gemm_f32_launches(int64_t M, int64_t N, int64_t K);
 // Cap on the SMs the f32 GEMM's persistent grid occupies (0: all); returns the
 // previous cap.
 int set_gemm_sm_limit(int n);

@@ -21,6 +21,7 @@ enum DeviceStatus : int {
   kDevTimeoutEmpty = 2,    // producer waited too long for a free stage
   kDevTimeoutAccum = 3,    // epilogue waited too long for the accumulator
   kDevTimeoutSelfTest = 4, // the self-test wait (nothing ever arrives) ran out
+  kDevTimeoutPeer = 5,     // a peer-GPU barrier waited too long for another rank
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -259,88 +260,6 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-}  // namespace b200
-
-// ---------------------------------------------------------------- CTA pairs
-// Helpers for the 2-SM (cta_group::2) GEMM: a cluster of 2 CTAs on a pair of
-// SMs; the even CTA ("leader") issues the MMAs for both.
-namespace b200 {
-
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
-               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// Address of the same shared-memory location in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-
-// Arrive on an mbarrier given by its shared::cluster address (possibly in
-// the peer CTA).
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
-}
-
-// TMA tile load into this CTA's shared memory whose completion is signalled
-// on the pair leader's mbarrier (`mbar` is this CTA's address of the barrier;
-// clearing bit 24 of the shared::cluster address selects the even CTA).
-// No multicast.
-__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* tmap, uint64_t* mbar,
-                                                 int32_t x, int32_t y) {
-  const uint32_t bar = smem_u32(mbar) & 0xFEFFFFFFu;
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(x), "r"(y)
-      : "memory");
-}
-
-// Warp-collective; issued by the same warp in both CTAs of the pair.
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                   smem_u32(dst_smem)),
-               "r"(ncols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
-               : "memory");
-}
-
-// D (both CTAs' TMEM, 128 lanes each) (+)= A (128 rows in each CTA) *
-// B (half of the N columns in each CTA); issued by one thread of the leader.
-__device__ __forceinline__ void umma_tf32_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
-                                               uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Arrive on the barrier at this offset in every CTA of `cta_mask` once all
-// prior MMAs of this thread are complete.
-__device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-      " [%0], %1;" ::"r"(smem_u32(bar)),
-      "h"(cta_mask)
-      : "memory");
 }
 
 }  // namespace b200

@@ -938,6 +938,13 @@ int64_t b200_dense_f32_workspace_bytes(int64_t M, int64_t N, int64_t K) {
   return dense_scratch_bytes(M, N, std::max<int64_t>(K, 1));
 }
 
+int b200_dense_f32_launches(int64_t M, int64_t N, int64_t K) {
+  if (M < 0 || N < 0 || K < 0) return -1;
+  if (M == 0 || N == 0) return 0;
+  if (K == 0) return 1;  // the bias / activation fill
+  return 1 + gemm_f32_launches(M, N, K);  // the split pass, the GEMM (+ reduction)
+}
+
 int b200_dense_f32_splits(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0) return 1;
   return choose_splits(M, N, K);
@@ -1405,6 +1412,27 @@ int b200_memcpy_d2d_async(void* dst, const void* src, int64_t bytes, void* strea
                               static_cast<cudaStream_t>(stream)),
               "cudaMemcpyAsync D2D");
   return succeed();
+}
+
+int b200_peer_barrier(uint32_t* const* flags, int world, int rank, uint32_t epoch,
+                      int64_t timeout_ns, void* stream) {
+  if (!flags || world < 1 || world > kMaxPeerRanks || rank < 0 || rank >= world ||
+      timeout_ns <= 0)
+    return fail(kErrInvalidArg, "peer barrier: flags, 1 <= world <= 8, 0 <= rank < world and "
+                                "a positive timeout are required");
+  PeerFlags f = {};
+  for (int r = 0; r < world; ++r) {
+    if (!flags[r]) return fail(kErrInvalidArg, "peer barrier: null flag array");
+    f.flags[r] = flags[r];
+  }
+  f.world = world;
+  f.rank = rank;
+  DeviceCtx* c = nullptr;
+  int rc = current_ctx(&c);
+  if (rc) return rc;
+  rc = peer_barrier(f, epoch, (uint64_t)timeout_ns, c->status, static_cast<cudaStream_t>(stream));
+  return rc ? fail(rc, std::string("peer barrier launch failed: ") + launch_error_text())
+            : succeed();
 }
 
 int b200_set_gemm_sm_limit(int n) {

@@ -28,13 +28,13 @@ EXPORTED_SYMBOLS = [
     "b200_version", "b200_last_error", "b200_last_status", "b200_device_count",
     "b200_launch_count", "b200_set_default_devices", "b200_get_default_devices", "b200_release",
     "b200_dense_f32", "b200_dense_f32_workspace_bytes", "b200_dense_f32_ws",
-    "b200_dense_f32_noalloc", "b200_dense_f32_splits", "b200_matmul_i32",
+    "b200_dense_f32_noalloc", "b200_dense_f32_splits", "b200_dense_f32_launches", "b200_matmul_i32",
     "b200_bias_act_f32", "b200_act_f32", "b200_bias_add_i32", "b200_stream_sync",
     "b200_tf32_split_rows", "b200_tf32_split_transpose", "b200_gemm_tf32x3_presplit",
     "b200_dense_f32_wsplit",
     "b200_malloc", "b200_free", "b200_memcpy_h2d", "b200_memcpy_d2h",
     "b200_selftest_wait_timeout", "b200_debug_fail_alloc", "b200_debug_schedule", "b200_set_gemm_sm_limit", "b200_dense_f32_chain",
-    "b200_dense_f32_peers",
+    "b200_dense_f32_peers", "b200_peer_barrier",
     "b200_ipc_alloc", "b200_ipc_free", "b200_ipc_open", "b200_ipc_close", "b200_memcpy_d2d_async",
     "b200_host_alloc", "b200_host_free",
     "b200_dense_f32_host", "b200_matmul_i32_host", "b200_bias_act_f32_host",
@@ -78,6 +78,7 @@ def _declare(lib):
         "b200_dense_f32_noalloc": ([vp, i64, vp, i64, vp, vp, i64, i64, i64, i64, i32, f32, vp],
                                    i32),
         "b200_dense_f32_splits": ([i64, i64, i64], i32),
+        "b200_dense_f32_launches": ([i64, i64, i64], i32),
         "b200_matmul_i32": ([vp, i64, vp, i64, vp, vp, i64, i64, i64, i64, vp], i32),
         "b200_bias_act_f32": ([vp, i64, vp, vp, i64, i64, i64, i32, f32, vp], i32),
         "b200_act_f32": ([vp, vp, i64, i32, f32, vp], i32),
@@ -100,6 +101,7 @@ def _declare(lib):
                                   f32, vp], i32),
         "b200_dense_f32_peers": ([vp, i64, vp, i64, vp, vp, i64, c.POINTER(vp), i32, i64, i64,
                                   i64, i32, f32, vp], i32),
+        "b200_peer_barrier": ([c.POINTER(vp), i32, i32, c.c_uint32, i64, vp], i32),
         "b200_ipc_alloc": ([c.POINTER(vp), i64, vp], i32),
         "b200_ipc_free": ([vp], i32),
         "b200_ipc_open": ([vp, c.POINTER(vp)], i32),
@@ -174,7 +176,7 @@ def dense_launches(M, N, K):
     """Kernel launches of one f32 dense layer through b200_dense_f32: one
     split pass (X and W together), the GEMM, and a split-K reduction when the
     problem is split."""
-    return 2 + (1 if lib().b200_dense_f32_splits(M, N, K) > 1 else 0)
+    return int(lib().b200_dense_f32_launches(M, N, K))
 
 
 def device_count():

@@ -5,6 +5,7 @@ contiguous shards with no exchange; W and b are replicated. The partition is
 the one the C runtime uses for its multi-device host calls (run_sharded in
 csrc/runtime.cu): M // n rows each, the first M % n shards one row more.
 """
+import os
 from typing import List, Tuple
 
 
@@ -126,11 +127,19 @@ class _DeviceArray:
                                          "strides": None, "stream": None}
 
 
+# Bounded wait of the peer barriers (ns): a rank that does not reach a
+# gathered call within this time makes its peers' calls fail with
+# B200_ERR_DEVICE_TIMEOUT instead of hanging.
+PEER_TIMEOUT_NS = int(os.environ.get("B200_PEER_TIMEOUT_MS", "60000")) * 1_000_000
+
+
 class _PeerRows:
-    """Each rank's [world * rows, N] f32 output buffer, allocated once per
-    shape and mapped into every other rank (CUDA IPC) so that a rank can copy
-    its finished rows straight into all of them. Cached per (rows, N, device,
-    group); held until the process exits."""
+    """Each rank's [world * rows, N] f32 output buffer, followed by its peer
+    barrier flags (world 32-bit slots), allocated once per shape and mapped
+    into every other rank (CUDA IPC) so that a rank can store its finished
+    rows straight into all of them. Cached per (rows, N, device, group); held
+    until the process exits. Calls order themselves against the peers with
+    b200_peer_barrier on the caller's stream (barrier())."""
 
     _cache = {}
 
@@ -148,10 +157,16 @@ class _PeerRows:
         from . import _native
         L = _native.lib()
         world, rank = dist.get_world_size(group), dist.get_rank(group)
-        nbytes = world * rows * N * 4
+        self.world, self.rank = world, rank
+        data = world * rows * N * 4
+        self.flags_off = (data + 255) // 256 * 256
+        nbytes = self.flags_off + 256
         ptr, handle = ctypes.c_void_p(), ctypes.create_string_buffer(64)
         with torch.cuda.device(device):
             _native.check(L.b200_ipc_alloc(ctypes.byref(ptr), nbytes, handle))
+            flags = torch.as_tensor(_DeviceArray(ptr.value + self.flags_off, (64,)), device=device)
+            flags.zero_()
+            torch.cuda.synchronize(device)
         handles = [None] * world
         dist.all_gather_object(handles, handle.raw, group=group)
         self.ptrs, err = [], ""
@@ -175,9 +190,20 @@ class _PeerRows:
                                + (f": {err}" if err else " on another rank"))
         self.local = ptr.value
         self.Y = torch.as_tensor(_DeviceArray(ptr.value, (world * rows, N)), device=device)
+        self.flag_ptrs = (ctypes.c_void_p * world)(*[p + self.flags_off for p in self.ptrs])
+        self.epoch = 0
         # one copy stream per peer, so that the copy engines move the pushes
         # to different peers in parallel
         self.comm = [torch.cuda.Stream(device=device) for _ in range(world)]
+
+    def barrier(self, stream):
+        """Stream-ordered barrier of all ranks on `stream` (a torch stream)."""
+        import ctypes
+        from . import _native
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+        _native.check(_native.lib().b200_peer_barrier(
+            self.flag_ptrs, self.world, self.rank, self.epoch, PEER_TIMEOUT_NS,
+            ctypes.c_void_p(stream.cuda_stream)))
 
 
 def gather_rows_ce(rows: int, N: int, compute_slab, *, slabs: int = 4, group=None, device=None):
@@ -195,9 +221,10 @@ def gather_rows_ce(rows: int, N: int, compute_slab, *, slabs: int = 4, group=Non
     L = _native.lib()
     world, rank = dist.get_world_size(group), dist.get_rank(group)
     buf = _PeerRows.get(rows, N, device, group)
-    # every rank is done with the previous result held in its buffer
-    torch.cuda.current_stream(device).synchronize()
-    dist.barrier(group=group)
+    stream = torch.cuda.current_stream(device)
+    # every rank's earlier work on its stream (which may still read its
+    # buffer) is done before any push into it
+    buf.barrier(stream)
     Yv = buf.Y.view(world, rows, N)
     for r0, r1 in slab_bounds(rows, slabs):
         compute_slab(r0, r1, Yv[rank, r0:r1])
@@ -211,10 +238,10 @@ def gather_rows_ce(rows: int, N: int, compute_slab, *, slabs: int = 4, group=Non
                 _native.check(L.b200_memcpy_d2d_async(ctypes.c_void_p(buf.ptrs[p] + off),
                                                       ctypes.c_void_p(buf.local + off), nbytes,
                                                       ctypes.c_void_p(buf.comm[p].cuda_stream)))
-    for p in range(world):  # this rank's pushes have landed in every peer
+    for p in range(world):  # this rank's pushes have landed in every peer ...
         if p != rank:
-            buf.comm[p].synchronize()
-    dist.barrier(group=group)  # ... and every peer's pushes in this buffer
+            stream.wait_stream(buf.comm[p])
+    buf.barrier(stream)  # ... and every peer's pushes in this buffer
     return buf.Y
 
 
@@ -248,19 +275,20 @@ def dense_rows_fused(X_local, W, b, act: int, alpha: float, *, group=None):
         raise ValueError("the fused transport stores into at most 7 peers")
     device = X_local.device
     buf = _PeerRows.get(rows, N, device, group)
-    # every rank is done with the previous result held in its buffer
-    torch.cuda.current_stream(device).synchronize()
-    dist.barrier(group=group)
+    stream = torch.cuda.current_stream(device)
+    # every rank's earlier work on its stream (which may still read its
+    # buffer) is done before any store into it
+    buf.barrier(stream)
     own, peers = fused_output_bases(buf.ptrs, rank, rows, N)
     arr = (ctypes.c_void_p * max(1, len(peers)))(*peers)
     p = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None
-    st = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    st = ctypes.c_void_p(stream.cuda_stream)
     _native.check(L.b200_dense_f32_peers(p(X_local), X_local.stride(0), p(W), W.stride(0), p(b),
                                          ctypes.c_void_p(own), N, arr, len(peers),
                                          rows, N, K, act, alpha, st))
-    # this rank's stores have landed in every peer ...
-    torch.cuda.current_stream(device).synchronize()
-    dist.barrier(group=group)  # ... and every peer's stores in this buffer
+    # this rank's stores have landed in every peer, and every peer's in this
+    # buffer, before later work on the stream reads it
+    buf.barrier(stream)
     return buf.Y
 
 

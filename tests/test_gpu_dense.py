@@ -221,8 +221,9 @@ def test_large_matmul_sampled_rows(cuda, name):
 
 @pytest.mark.parametrize("M,N,K", [(1024, 1024, 1024), (512, 4096, 11008), (100, 50, 1001)])
 def test_split_k_matches_unsplit(cuda, M, N, K):
-    """Split-K (chosen for few-tile problems) against the same pre-split
-    operands run without splitting; both within the f32 bound of the oracle."""
+    """Split-K (chosen for few-tile problems) through b200_dense_f32 against
+    the GEMM alone on operands split by the public split entry points; both
+    within the f32 bound of the oracle."""
     import torch
     dev = torch.device("cuda:0")
     L = _native.lib()
@@ -369,36 +370,6 @@ def test_edge_shapes(cuda, M, N, K):
     assert max_err(got[rows], ref) <= bound
     exact = np.maximum(X[rows].astype(np.float64) @ W.astype(np.float64) + b, 0)
     assert float(np.max(np.abs(got[rows] - exact))) <= bound / 10  # f32-level
-
-
-def test_two_sm_variant_option(cuda):
-    """B200_GEMM_2SM=1 (child process; read once per process): the CTA-pair
-    tcgen05.mma.cta_group::2 kernel, against the oracle, with and without
-    split-K and with ragged tails."""
-    import os
-    import subprocess
-    import sys
-    from conftest import PKG_PARENT, ROOT
-    script = r"""
-import sys, numpy as np, torch
-sys.path[:0] = sys.argv[1:4]
-import oracle
-from gpu_util import dense_device, max_err
-for (M, N, K) in [(256, 256, 16), (300, 500, 1001), (1024, 1024, 4096), (4096, 2048, 1024)]:
-    rng = np.random.default_rng(K)
-    X = rng.uniform(-1, 1, (M, K)).astype(np.float32)
-    W = rng.uniform(-1, 1, (K, N)).astype(np.float32)
-    b = rng.uniform(-1, 1, (N,)).astype(np.float32)
-    got = dense_device(torch, X, W, b, act=1)
-    rows = slice(0, min(M, 512))
-    assert max_err(got[rows], oracle.dense_f32(X[rows], W, b, act=1)) <= oracle.f32_bound(K, X, W)
-print("ok")
-"""
-    env = dict(os.environ, B200_GEMM_2SM="1")
-    tests_dir = os.path.dirname(os.path.abspath(__file__))
-    r = subprocess.run([sys.executable, "-c", script, ROOT, PKG_PARENT, tests_dir], env=env,
-                       capture_output=True, text=True, timeout=600)
-    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
 
 
 # N % 32 == 0 (the MN-major path's condition) with M and K tails, fewer than

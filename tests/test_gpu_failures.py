@@ -72,3 +72,54 @@ def test_release_keeps_the_callers_device(cuda):
     before = torch.cuda.current_device()
     _native.check(L.b200_release())
     assert torch.cuda.current_device() == before
+
+
+def _flag_arrays(torch, world):
+    """`world` zeroed flag arrays on this GPU standing in for every rank's."""
+    fl = torch.zeros((world, 8), dtype=torch.int32, device="cuda:0")
+    ptrs = (ctypes.c_void_p * world)(*[fl[r].data_ptr() for r in range(world)])
+    return fl, ptrs
+
+
+def test_peer_barrier_signals_every_peer_and_passes(cuda):
+    """One GPU plays rank 1 of 3: the peers' arrivals are already in its own
+    flag array, so the barrier passes at once; it stores its epoch into its
+    slot of each peer's array and leaves its own slot alone."""
+    import torch
+    L = _native.lib()
+    s = stream_ptr(torch)
+    fl, ptrs = _flag_arrays(torch, 3)
+    fl[1, 0] = 7
+    fl[1, 2] = 8  # a later epoch also counts as reached
+    _native.check(L.b200_peer_barrier(ptrs, 3, 1, 7, 1_000_000_000, s))
+    assert L.b200_stream_sync(s) == 0
+    got = fl.cpu().numpy()
+    assert got[0, 1] == 7 and got[2, 1] == 7 and got[1, 1] == 0
+    # a lone rank has nobody to wait for
+    _native.check(L.b200_peer_barrier(ptrs, 1, 0, 1, 1_000_000, s))
+    assert L.b200_stream_sync(s) == 0
+
+
+def test_peer_barrier_timeout_is_reported_and_context_survives(cuda):
+    """Rank 0 of 2 whose peer never arrives (a flag that nothing sets): the
+    wait gives up after 50 ms with B200_ERR_DEVICE_TIMEOUT, and the context
+    keeps working."""
+    import torch
+    L = _native.lib()
+    s = stream_ptr(torch)
+    fl, ptrs = _flag_arrays(torch, 2)
+    t0 = time.perf_counter()
+    _native.check(L.b200_peer_barrier(ptrs, 2, 0, 1, 50_000_000, s))
+    rc = L.b200_stream_sync(s)
+    elapsed = time.perf_counter() - t0
+    assert rc == 5 and b"code 5" in L.b200_last_error(), (rc, L.b200_last_error())
+    assert 0.04 < elapsed < 5.0
+    assert int(fl[1, 0].item()) == 1  # it did signal its peer
+    assert L.b200_stream_sync(s) == 0
+    rng = np.random.default_rng(2)
+    X = rng.uniform(-1, 1, (200, 64)).astype(np.float32)
+    W = rng.uniform(-1, 1, (64, 96)).astype(np.float32)
+    got = dense_device(torch, X, W, None, act=0)
+    assert max_err(got, oracle.dense_f32(X, W)) <= oracle.f32_bound(64, X, W)
+    with pytest.raises(_native.B200Error):
+        _native.check(L.b200_peer_barrier(ptrs, 9, 0, 1, 1000, s))
