@@ -353,6 +353,38 @@ def small_configs(torch, L, _native, dev, stream, peak, args):
                 "frac_of_3xtf32_peak": fl / ms / 1e9 / peak, "max_abs_err_vs_f64": err,
                 "bound": bound, "ok": err <= bound})
     del t, H, Y
+    # the same MLP end to end through @ml_function with host (NumPy) arrays:
+    # every call copies X, W1, W2 in and Y out, unless W1 and W2 are
+    # registered (b200_weights_register keeps their device copies and splits)
+    from mlir_edsl import Tensor, f32, ml_function, register_weights, release_weights, relu
+
+    @ml_function(target="b200")
+    def mlp_fn(X: Tensor[f32, 512, 4096], W1: Tensor[f32, 4096, 11008], b1: Tensor[f32, 11008],
+               W2: Tensor[f32, 11008, 4096], b2: Tensor[f32, 4096]) -> Tensor[f32, 512, 4096]:
+        return relu(relu(X @ W1 + b1) @ W2 + b2)
+
+    margs = (g["X"], g["W1"], g["b1"], g["W2"], g["b2"])
+
+    def host_ms(k=5):
+        mlp_fn(*margs)
+        t0 = time.perf_counter()
+        for _ in range(k):
+            mlp_fn(*margs)
+        return (time.perf_counter() - t0) / k * 1e3
+
+    ms_plain = host_ms()
+    register_weights(g["W1"])
+    register_weights(g["W2"])
+    try:
+        ms_reg = host_ms()
+    finally:
+        release_weights(g["W1"])
+        release_weights(g["W2"])
+    out.append({"config": "mlp_2layer_frontend_e2e", "ms_per_call": ms_plain,
+                "ms_per_call_registered_weights": ms_reg,
+                "TFLOP/s": fl / ms_plain / 1e9, "TFLOP/s_registered_weights": fl / ms_reg / 1e9,
+                "api": "@ml_function(target='b200') on NumPy arrays, host wall clock; "
+                       "registered: mlir_edsl.register_weights(W1), (W2)"})
     # i32 2048^3 (byte-sliced int8 tensor-core path), bit-exact on sampled rows
     g = workloads.config_inputs("matmul_i32_2048")
     A, B = torch.from_numpy(g["A"]).to(dev), torch.from_numpy(g["B"]).to(dev)

@@ -112,6 +112,25 @@ int b200_dense_f32_ws(const float* X, int64_t ldx, const float* W, int64_t ldw, 
                       float* Y, int64_t ldy, int64_t M, int64_t N, int64_t K, int act,
                       float alpha, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Weight cache. b200_weights_register declares the f32 weight matrix
+ * W[K,N] (row pitch ldw floats) at host address W unchanged until it is
+ * registered again with another `version` (or shape) or released. The
+ * host-buffer entry points (b200_dense_f32_host and the memref entry points)
+ * that get this W with this shape and pitch then keep its device copy and
+ * its tf32 split on each GPU they run on, made at first use, instead of
+ * copying and splitting W in every call as the reference's GPU path does
+ * (reference: cpp/src/MLIRCompiler.cpp:368-376, cuMemAlloc + cuMemcpyHtoD
+ * of every argument per call). Registering the same (W, ldw, K, N, version)
+ * again is a no-op; a new version drops the device copies after the GPUs
+ * have finished the work queued so far. b200_weights_release frees them on
+ * every GPU (same wait) and forgets W; neither may overlap a call that uses
+ * W on another thread. b200_weights_device returns the current device's copy
+ * (rows of N floats, pitch N), uploading it if needed; b200_dense_f32 and its
+ * device-pointer siblings given that address as W reuse the kept split. */
+int b200_weights_register(const float* W, int64_t ldw, int64_t K, int64_t N, uint64_t version);
+int b200_weights_release(const float* W);
+int b200_weights_device(const float* W, const float** dW);
+
 /* Y = act(X @ W + b) like b200_dense_f32, for callers that must not
  * allocate device memory while they run (for example a serving process whose
  * framework allocator already holds nearly all of HBM, or a latency-bound loop

@@ -414,6 +414,104 @@ int check_device_status(DeviceCtx* c) {
 
 int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 
+// ------------------------------------------------------------ weight cache
+// Registered weights (b200_weights_register): a host W[K, N] the caller
+// declares unchanged until it registers it again (with a new version) or
+// releases it. On each device a call runs on, the runtime keeps W's device
+// copy (rows of N floats, pitch N) and, made on first need, the tf32 split
+// the GEMM reads: the row-major lo part for the MN-major B path, or the
+// transposed hi / lo parts for the K-major one. Calls that find their W here
+// copy and split neither; device-pointer calls are recognised by the device
+// copy's address (b200_weights_device).
+struct PreSplitW {
+  const float* lo_mn = nullptr;  // row-major lo, pitch roundup(N, 4)
+  const float* hiT = nullptr;    // K-major hi / lo, pitch split_pitch(K)
+  const float* loT = nullptr;
+};
+
+struct WeightCopy {
+  DevBuf w, lo_mn, hiT, loT;
+  bool up = false, have_mn = false, have_k = false;
+};
+
+struct WeightEntry {
+  int64_t ldw = 0, K = 0, N = 0;
+  uint64_t version = 0;
+  WeightCopy dev[64];
+};
+
+std::mutex g_w_mu;
+std::map<const float*, std::unique_ptr<WeightEntry>> g_weights;  // by host address
+
+// The entry registered for host W with this shape and pitch (caller holds g_w_mu).
+WeightEntry* find_host_weights(const float* W, int64_t ldw, int64_t K, int64_t N) {
+  auto it = g_weights.find(W);
+  if (it == g_weights.end()) return nullptr;
+  WeightEntry* e = it->second.get();
+  return (e->ldw == ldw && e->K == K && e->N == N) ? e : nullptr;
+}
+
+// The entry whose copy on device `dev` starts at W (caller holds g_w_mu).
+WeightEntry* find_device_weights(int dev, const float* W) {
+  for (auto& kv : g_weights)
+    if (kv.second->dev[dev].up && kv.second->dev[dev].w.p == W) return kv.second.get();
+  return nullptr;
+}
+
+// Uploads W to device c->dev if needed and makes the split the call needs
+// (MN-major lo when `mn`, else the K-major hi / lo pair). Synchronous on the
+// device's compute stream, so the copies are complete for every stream.
+// Caller holds g_w_mu.
+int weights_ready(DeviceCtx* c, const float* Whost, WeightEntry* e, bool mn, PreSplitW* out,
+                  const float** dW) {
+  WeightCopy& d = e->dev[c->dev];
+  const int64_t K = e->K, N = e->N;
+  B200_CUDA(cudaSetDevice(c->dev), "cudaSetDevice");
+  if (!d.up) {
+    B200_CUDA(d.w.reserve((size_t)std::max<int64_t>(K * N, 1) * 4), "alloc registered W");
+    int rc = h2d_rows(c, d.w.p, N * 4, Whost, e->ldw * 4, N * 4, K, c->s_comp);
+    if (rc) return rc;
+    B200_CUDA(cudaStreamSynchronize(c->s_comp), "sync");
+    d.up = true;
+  }
+  float* w = static_cast<float*>(d.w.p);
+  if (mn && !d.have_mn) {
+    B200_CUDA(d.lo_mn.reserve((size_t)w_lo_mn_bytes(K, N)), "alloc registered W split");
+    int rc = split_lo_xw_f32(nullptr, 0, 0, K, nullptr, nullptr, w, N, N,
+                             static_cast<float*>(d.lo_mn.p), c->s_comp);
+    if (rc) return fail(rc, std::string("split of registered W: ") + launch_error_text());
+    B200_CUDA(cudaStreamSynchronize(c->s_comp), "sync");
+    d.have_mn = true;
+  }
+  if (!mn && !d.have_k) {
+    const size_t bytes = (size_t)N * split_pitch(K) * 4;
+    B200_CUDA(d.hiT.reserve(bytes), "alloc registered W split");
+    B200_CUDA(d.loT.reserve(bytes), "alloc registered W split");
+    int rc = split_w_f32(w, N, K, N, static_cast<float*>(d.hiT.p), static_cast<float*>(d.loT.p),
+                         c->s_comp);
+    if (rc) return fail(rc, std::string("split of registered W: ") + launch_error_text());
+    B200_CUDA(cudaStreamSynchronize(c->s_comp), "sync");
+    d.have_k = true;
+  }
+  if (mn) {
+    out->lo_mn = static_cast<const float*>(d.lo_mn.p);
+  } else {
+    out->hiT = static_cast<const float*>(d.hiT.p);
+    out->loT = static_cast<const float*>(d.loT.p);
+  }
+  if (dW) *dW = w;
+  return kOk;
+}
+
+void release_weight_copy(WeightCopy& d) {
+  d.w.release();
+  d.lo_mn.release();
+  d.hiT.release();
+  d.loT.release();
+  d.up = d.have_mn = d.have_k = false;
+}
+
+
 bool bad_dims(int64_t M, int64_t N, int64_t K) { return M < 0 || N < 0 || K < 0; }
 
 // Scratch layout inside one workspace block.
@@ -469,40 +567,65 @@ int dense_device(DeviceCtx* c, const float* X, int64_t ldx, const float* W, int6
   const int splits = choose_splits(M, N, K);
   const int64_t Kp = split_pitch(K);
   float* xlo = xlo_in ? const_cast<float*>(xlo_in) : s.xlo;
+  const bool xraw = fused_a_ok(X, ldx);
+  // W is a registered weight's device copy: its split is kept, only X is split
+  const bool fused = fuse_a(X, ldx) && !xlo_in;
+  const bool mn = w_mn_ok(W, ldw, M, N);
+  PreSplitW pre;
+  bool have_pre = false;
+  if (!fused && !w_lo_in_kernel()) {
+    std::lock_guard<std::mutex> g(g_w_mu);
+    WeightEntry* e = g_weights.empty() ? nullptr : find_device_weights(c->dev, W);
+    if (e && e->K == K && e->N == N && ldw == N) {
+      const int rc = weights_ready(c, nullptr, e, mn, &pre, nullptr);
+      if (rc) return rc;
+      have_pre = true;
+    }
+  }
+  auto split_x_only = [&]() -> int {
+    if (xlo_in) return kOk;
+    return xraw ? split_x_lo_f32(X, ldx, M, K, s.xlo, st)
+                : split_x_f32(X, ldx, M, K, s.xhi, s.xlo, st);
+  };
   int rc;
-  if (fuse_a(X, ldx) && !xlo_in) {
+  if (fused) {
     rc = split_w_f32(W, ldw, K, N, s.whi, s.wlo, st);
     if (rc == kOk)
       rc = gemm_tf32x3_fused(X, ldx, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha, splits,
                              s.partials, c->status, st, ylo, ldylo);
-  } else if (w_mn_ok(W, ldw, M, N) &&
-             w_lo_mn_bytes(K, N) <= reinterpret_cast<char*>(s.partials) -
-                                        reinterpret_cast<char*>(s.whi)) {
+  } else if (mn && (have_pre || w_lo_mn_bytes(K, N) <= reinterpret_cast<char*>(s.partials) -
+                                                          reinterpret_cast<char*>(s.whi))) {
     // W is read as-is (MN-major B_hi); its row-major lo part goes into the
-    // W split region. X likewise when its rows are 16-byte aligned.
-    const bool xraw = fused_a_ok(X, ldx);
-    float* wlo = w_lo_in_kernel() ? nullptr : s.whi;
-    if (xlo_in)  // X is pre-split: W alone, if anything
-      rc = wlo ? split_lo_xw_f32(nullptr, 0, 0, K, nullptr, nullptr, W, ldw, N, wlo, st) : kOk;
-    else if (wlo)
-      rc = split_lo_xw_f32(X, ldx, M, K, xraw ? nullptr : s.xhi, s.xlo, W, ldw, N, wlo, st);
+    // W split region (or is the registered weight's). X likewise when its
+    // rows are 16-byte aligned.
+    const float* wlo = have_pre ? pre.lo_mn : (w_lo_in_kernel() ? nullptr : s.whi);
+    if (have_pre || wlo == nullptr)
+      rc = split_x_only();
+    else if (xlo_in)  // X is pre-split: W alone
+      rc = split_lo_xw_f32(nullptr, 0, 0, K, nullptr, nullptr, W, ldw, N, s.whi, st);
     else
-      rc = xraw ? split_x_lo_f32(X, ldx, M, K, s.xlo, st)
-                : split_x_f32(X, ldx, M, K, s.xhi, s.xlo, st);
+      rc = split_lo_xw_f32(X, ldx, M, K, xraw ? nullptr : s.xhi, s.xlo, W, ldw, N, s.whi, st);
     if (rc == kOk)
       rc = gemm_tf32x3_wmn(xraw ? X : s.xhi, xlo, xraw ? ldx : Kp, W, ldw, wlo, M, N, K, b, Y,
                            ldy, act, alpha, splits, s.partials, c->status, st, ylo, ldylo);
-  } else if (fused_a_ok(X, ldx)) {  // X is the hi part; only lo is written
-    rc = xlo_in ? split_w_f32(W, ldw, K, N, s.whi, s.wlo, st)
-                : split_xw_f32(X, ldx, M, W, ldw, K, N, nullptr, s.xlo, s.whi, s.wlo, st);
+  } else if (xraw) {  // X is the hi part; only lo is written
+    const float* whi = have_pre ? pre.hiT : s.whi;
+    const float* wlo = have_pre ? pre.loT : s.wlo;
+    if (have_pre)
+      rc = split_x_only();
+    else
+      rc = xlo_in ? split_w_f32(W, ldw, K, N, s.whi, s.wlo, st)
+                  : split_xw_f32(X, ldx, M, W, ldw, K, N, nullptr, s.xlo, s.whi, s.wlo, st);
     if (rc == kOk)
-      rc = gemm_tf32x3_xraw(X, ldx, xlo, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha, splits,
+      rc = gemm_tf32x3_xraw(X, ldx, xlo, whi, wlo, M, N, K, b, Y, ldy, act, alpha, splits,
                             s.partials, c->status, st, ylo, ldylo);
   } else {
     if (xlo_in) return fail(kErrInvalidArg, "a pre-split X needs 16-byte aligned X rows");
-    rc = split_xw_f32(X, ldx, M, W, ldw, K, N, s.xhi, s.xlo, s.whi, s.wlo, st);
+    rc = have_pre ? split_x_only()
+                  : split_xw_f32(X, ldx, M, W, ldw, K, N, s.xhi, s.xlo, s.whi, s.wlo, st);
     if (rc == kOk)
-      rc = gemm_tf32x3_splitk(s.xhi, s.xlo, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha, splits,
+      rc = gemm_tf32x3_splitk(s.xhi, s.xlo, have_pre ? pre.hiT : s.whi,
+                              have_pre ? pre.loT : s.wlo, M, N, K, b, Y, ldy, act, alpha, splits,
                               s.partials, c->status, st, ylo, ldylo);
   }
   if (rc != kOk) return fail(rc, std::string("dense_f32: ") + launch_error_text());
@@ -560,9 +683,25 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
   const bool stage_x = K > 0 && M * K * 4 >= ((int64_t)16 << 20) && is_pageable(X);
   const bool stage_y = M * N * 4 >= ((int64_t)16 << 20) && is_pageable(Y);
 
-  // Weights (replicated): upload + split once per call on the compute stream.
+  // Weights (replicated): a registered W's device copy and split are kept
+  // (b200_weights_register); any other W is uploaded and split once per call
+  // on the compute stream.
+  const bool fa = K > 0 && fuse_a(static_cast<float*>(c->x[0].p), K);
+  PreSplitW pre;
+  const float* regW = nullptr;
+  bool have_pre = false;
+  if (K > 0 && !w_lo_in_kernel()) {
+    std::lock_guard<std::mutex> g(g_w_mu);
+    WeightEntry* e = g_weights.empty() ? nullptr : find_host_weights(W, ldw, K, N);
+    if (e) {
+      // a registered copy is cudaMalloc'd (aligned), pitch N
+      const bool mn = !fa && w_mn_ok(reinterpret_cast<const float*>(256), N, M, N);
+      if ((rc = weights_ready(c, W, e, mn, &pre, &regW))) return rc;
+      have_pre = true;
+    }
+  }
   B200_CUDA(c->bias.reserve(std::max<int64_t>(N, 1) * 4), "alloc bias");
-  if (K > 0) {
+  if (K > 0 && !have_pre) {
     B200_CUDA(c->w.reserve(K * N * 4), "alloc W");
     B200_CUDA(c->whi.reserve(std::max(N * Kp * 4, w_lo_mn_bytes(K, N))), "alloc W split");
     B200_CUDA(c->wlo.reserve(N * Kp * 4), "alloc W split");
@@ -582,25 +721,27 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
       B200_CUDA(c->xlo[i].reserve(slab * Kp * 4), "alloc X split");
     }
   }
-  float* dW = static_cast<float*>(c->w.p);
-  float* dWhi = static_cast<float*>(c->whi.p);
-  float* dWlo = static_cast<float*>(c->wlo.p);
+  float* dW = have_pre ? const_cast<float*>(regW) : static_cast<float*>(c->w.p);
+  float* dWhi = have_pre ? const_cast<float*>(pre.hiT) : static_cast<float*>(c->whi.p);
+  float* dWlo = have_pre ? const_cast<float*>(pre.loT) : static_cast<float*>(c->wlo.p);
   float* db = b ? static_cast<float*>(c->bias.p) : nullptr;
   // MN-major B (W read as-is, row-major lo part in dWhi) unless the fused A
   // split is selected.
   const bool wmn = K > 0 && !fuse_a(static_cast<float*>(c->x[0].p), K) && w_mn_ok(dW, N, M, N);
   if (b) B200_CUDA(cudaMemcpyAsync(db, b, N * 4, cudaMemcpyHostToDevice, c->s_comp), "H2D b");
-  if (K > 0) {
+  if (K > 0 && !have_pre) {
     if ((rc = h2d_rows(c, dW, N * 4, W, ldw * 4, N * 4, K, c->s_comp))) return rc;
     // A single-slab call splits W together with X (one launch) below.
     if (nslab > 1 && wmn && !w_lo_in_kernel()) {
       rc = split_lo_xw_f32(nullptr, 0, 0, K, nullptr, nullptr, dW, N, N, dWhi, c->s_comp);
-      if (rc) return fail(rc, std::string("split W launch failed: ") + launch_error_text());
+      if (rc) return fail(rc, "split W launch failed");
     } else if (!wmn && (nslab > 1 || fuse_a(static_cast<float*>(c->x[0].p), K))) {
       rc = split_w_f32(dW, N, K, N, dWhi, dWlo, c->s_comp);
-      if (rc) return fail(rc, std::string("split W launch failed: ") + launch_error_text());
+      if (rc) return fail(rc, "split W launch failed");
     }
   }
+  // W and its split are ready: slabs split X only
+  const bool w_split = have_pre || nslab > 1;
 
   for (int64_t i = 0; i < nslab; ++i) {
     const int slot = (int)(i % kRing);
@@ -638,8 +779,9 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
         float* xhi = static_cast<float*>(c->xhi[slot].p);
         float* xlo = static_cast<float*>(c->xlo[slot].p);
         const bool xraw = fused_a_ok(dX, K);
-        float* wlo = w_lo_in_kernel() ? nullptr : dWhi;
-        if (nslab == 1 && wlo)
+        float* wlo = have_pre ? const_cast<float*>(pre.lo_mn)
+                              : (w_lo_in_kernel() ? nullptr : dWhi);
+        if (!w_split && wlo)
           rc = split_lo_xw_f32(dX, K, rows, K, xraw ? nullptr : xhi, xlo, dW, N, N, wlo,
                                c->s_comp);
         else
@@ -650,16 +792,16 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
                                dY, N, act, alpha, splits, part, c->status, c->s_comp);
       } else if (fused_a_ok(dX, K)) {
         float* xlo = static_cast<float*>(c->xlo[slot].p);
-        rc = nslab == 1 ? split_xw_f32(dX, K, rows, dW, N, K, N, nullptr, xlo, dWhi, dWlo, c->s_comp)
-                        : split_x_lo_f32(dX, K, rows, K, xlo, c->s_comp);
+        rc = !w_split ? split_xw_f32(dX, K, rows, dW, N, K, N, nullptr, xlo, dWhi, dWlo, c->s_comp)
+                      : split_x_lo_f32(dX, K, rows, K, xlo, c->s_comp);
         if (rc == kOk)
           rc = gemm_tf32x3_xraw(dX, K, xlo, dWhi, dWlo, rows, N, K, db, dY, N, act, alpha, splits,
                                 part, c->status, c->s_comp);
       } else {
         float* xhi = static_cast<float*>(c->xhi[slot].p);
         float* xlo = static_cast<float*>(c->xlo[slot].p);
-        rc = nslab == 1 ? split_xw_f32(dX, K, rows, dW, N, K, N, xhi, xlo, dWhi, dWlo, c->s_comp)
-                        : split_x_f32(dX, K, rows, K, xhi, xlo, c->s_comp);
+        rc = !w_split ? split_xw_f32(dX, K, rows, dW, N, K, N, xhi, xlo, dWhi, dWlo, c->s_comp)
+                      : split_x_f32(dX, K, rows, K, xhi, xlo, c->s_comp);
         if (rc == kOk)
           rc = gemm_tf32x3_splitk(xhi, xlo, dWhi, dWlo, rows, N, K, db, dY, N, act, alpha,
                                   splits, part, c->status, c->s_comp);
@@ -918,6 +1060,10 @@ int b200_release(void) {
       c.sx[i].release();
       c.sy[i].release();
     }
+    {
+      std::lock_guard<std::mutex> g(g_w_mu);
+      for (auto& kv : g_weights) release_weight_copy(kv.second->dev[d]);
+    }
     std::vector<StreamScratch*> entries;
     {
       std::lock_guard<std::mutex> g(g_mu);
@@ -929,6 +1075,79 @@ int b200_release(void) {
     }
   }
   if (have_prev) cudaSetDevice(prev);
+  return succeed();
+}
+
+// ---------------------------------------------------------------- weight cache
+int b200_weights_register(const float* W, int64_t ldw, int64_t K, int64_t N, uint64_t version) {
+  if (!W || K <= 0 || N <= 0 || ldw < N)
+    return fail(kErrInvalidArg, "weights: non-null W, K > 0, N > 0 and ldw >= N are required");
+  if (K > (int64_t)1 << 31 || N > (int64_t)1 << 31)
+    return fail(kErrTooLarge, "dimension exceeds 2^31");
+  std::lock_guard<std::mutex> g(g_w_mu);
+  auto& slot = g_weights[W];
+  if (slot && slot->ldw == ldw && slot->K == K && slot->N == N && slot->version == version)
+    return succeed();  // unchanged: keep the device copies
+  if (slot) {
+    // new contents or shape: drop the old copies (after work that may read them)
+    int prev = 0;
+    const bool have_prev = cudaGetDevice(&prev) == cudaSuccess;
+    for (int d = 0; d < 64; ++d)
+      if (slot->dev[d].w.p || slot->dev[d].lo_mn.p || slot->dev[d].hiT.p) {
+        cudaSetDevice(d);
+        cudaDeviceSynchronize();
+        release_weight_copy(slot->dev[d]);
+      }
+    if (have_prev) cudaSetDevice(prev);
+  } else {
+    slot.reset(new WeightEntry);
+  }
+  slot->ldw = ldw;
+  slot->K = K;
+  slot->N = N;
+  slot->version = version;
+  return succeed();
+}
+
+int b200_weights_release(const float* W) {
+  int prev = 0;
+  const bool have_prev = cudaGetDevice(&prev) == cudaSuccess;
+  std::lock_guard<std::mutex> g(g_w_mu);
+  auto it = g_weights.find(W);
+  if (it == g_weights.end()) return fail(kErrInvalidArg, "weights: W is not registered");
+  for (int d = 0; d < 64; ++d) {
+    WeightCopy& wc = it->second->dev[d];
+    if (wc.w.p || wc.lo_mn.p || wc.hiT.p) {
+      cudaSetDevice(d);
+      cudaDeviceSynchronize();  // work queued on any stream may still read them
+      release_weight_copy(wc);
+    }
+  }
+  g_weights.erase(it);
+  if (have_prev) cudaSetDevice(prev);
+  return succeed();
+}
+
+int b200_weights_device(const float* W, const float** dW) {
+  if (!W || !dW) return fail(kErrInvalidArg, "weights: null argument");
+  *dW = nullptr;
+  DeviceCtx* c = nullptr;
+  int rc = current_ctx(&c);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(c->mu);  // the staging buffers of h2d_rows
+  std::lock_guard<std::mutex> g(g_w_mu);
+  auto it = g_weights.find(W);
+  if (it == g_weights.end()) return fail(kErrInvalidArg, "weights: W is not registered");
+  WeightEntry* e = it->second.get();
+  WeightCopy& d = e->dev[c->dev];
+  if (!d.up) {
+    B200_CUDA(d.w.reserve((size_t)e->K * e->N * 4), "alloc registered W");
+    if ((rc = h2d_rows(c, d.w.p, e->N * 4, W, e->ldw * 4, e->N * 4, e->K, c->s_comp)))
+      return rc;
+    B200_CUDA(cudaStreamSynchronize(c->s_comp), "sync");
+    d.up = true;
+  }
+  *dW = static_cast<const float*>(d.w.p);
   return succeed();
 }
 

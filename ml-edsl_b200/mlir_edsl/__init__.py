@@ -22,7 +22,8 @@ from .ast import CompareOp, IfOp, LinalgDot, LinalgReduce, to_value
 from .types import DYN, Tensor, TensorType, ScalarType, f32, i1, i32
 
 try:
-    from .backend import HAS_B200_BACKEND, HAS_CPP_BACKEND, get_backend
+    from .backend import (HAS_B200_BACKEND, HAS_CPP_BACKEND, get_backend, register_weights,
+                          release_weights)
 except Exception:  # pragma: no cover - import-time failure of ctypes itself
     HAS_B200_BACKEND = HAS_CPP_BACKEND = False
 
@@ -41,5 +42,6 @@ __all__ = [
     "ADD", "SUB", "MUL", "DIV",
     "Value", "Constant", "Parameter", "BinaryOp", "LinalgMatmul", "LinalgBinaryOp",
     "LinalgActivation",
-    "get_backend", "HAS_B200_BACKEND", "HAS_CPP_BACKEND",
+    "get_backend", "HAS_B200_BACKEND", "HAS_CPP_BACKEND", "register_weights",
+    "release_weights",
 ]

@@ -28,7 +28,8 @@ EXPORTED_SYMBOLS = [
     "b200_version", "b200_last_error", "b200_last_status", "b200_device_count",
     "b200_launch_count", "b200_set_default_devices", "b200_get_default_devices", "b200_release",
     "b200_dense_f32", "b200_dense_f32_workspace_bytes", "b200_dense_f32_ws",
-    "b200_dense_f32_noalloc", "b200_dense_f32_splits", "b200_dense_f32_launches", "b200_matmul_i32",
+    "b200_dense_f32_noalloc", "b200_weights_register", "b200_weights_release",
+    "b200_weights_device", "b200_dense_f32_splits", "b200_dense_f32_launches", "b200_matmul_i32",
     "b200_bias_act_f32", "b200_act_f32", "b200_bias_add_i32", "b200_stream_sync",
     "b200_tf32_split_rows", "b200_tf32_split_transpose", "b200_gemm_tf32x3_presplit",
     "b200_dense_f32_wsplit",
@@ -78,6 +79,9 @@ def _declare(lib):
         "b200_dense_f32_noalloc": ([vp, i64, vp, i64, vp, vp, i64, i64, i64, i64, i32, f32, vp],
                                    i32),
         "b200_dense_f32_splits": ([i64, i64, i64], i32),
+        "b200_weights_register": ([vp, i64, i64, i64, c.c_uint64], i32),
+        "b200_weights_release": ([vp], i32),
+        "b200_weights_device": ([vp, c.POINTER(vp)], i32),
         "b200_dense_f32_launches": ([i64, i64, i64], i32),
         "b200_matmul_i32": ([vp, i64, vp, i64, vp, vp, i64, i64, i64, i64, vp], i32),
         "b200_bias_act_f32": ([vp, i64, vp, vp, i64, i64, i64, i32, f32, vp], i32),

@@ -78,6 +78,38 @@ def _output_descriptor(shape, dtype):
 
 _DEFAULT_INIT = {0: 0.0, 2: float("-inf"), 3: float("inf")}
 
+# Registered weights: data address -> (array, version). The array is held so
+# that its memory cannot be reused by another array while registered.
+_WEIGHTS: Dict[int, Tuple[np.ndarray, int]] = {}
+
+
+def register_weights(W: np.ndarray, version: int = 0) -> None:
+    """Declares the 2-D f32 array W unchanged until it is registered again
+    with another version or released: the device copy and tf32 split of W
+    are then kept on every GPU that runs a function taking it, instead of
+    being copied and split in every call (b200_weights_register). Modifying
+    W in place without re-registering it leaves later calls on stale data."""
+    if not isinstance(W, np.ndarray) or W.dtype != np.float32 or W.ndim != 2:
+        raise TypeError("register_weights takes a 2-D float32 ndarray")
+    if not W.flags["C_CONTIGUOUS"]:
+        raise ValueError("register_weights takes a C-contiguous array")
+    _native.check(_native.lib().b200_weights_register(
+        ctypes.c_void_p(W.ctypes.data), W.shape[1], W.shape[0], W.shape[1], int(version)))
+    _WEIGHTS[W.ctypes.data] = (W, int(version))
+
+
+def release_weights(W: np.ndarray) -> None:
+    """Frees the device copies of a registered array and forgets it."""
+    if W.ctypes.data not in _WEIGHTS:
+        raise ValueError("array is not registered")
+    del _WEIGHTS[W.ctypes.data]
+    _native.check(_native.lib().b200_weights_release(ctypes.c_void_p(W.ctypes.data)))
+
+
+def _registered(a: np.ndarray) -> bool:
+    held = _WEIGHTS.get(a.ctypes.data)
+    return held is not None and held[0].shape == a.shape and a.dtype == np.float32
+
 
 def _to_python(v):
     """Scalar results are returned as Python numbers, as the reference's
@@ -239,6 +271,13 @@ class B200Backend:
                       if r.kind == "param" and s.op != "scalar_op"}
             for i in sorted(needed):
                 a = arrays[i]
+                if isinstance(a, np.ndarray) and a.ndim == 2 and _registered(a):
+                    # the registered weight's kept device copy (and split)
+                    p = ctypes.c_void_p()
+                    _native.check(L.b200_weights_device(ctypes.c_void_p(a.ctypes.data),
+                                                        ctypes.byref(p)))
+                    dparams[i] = p
+                    continue
                 p = dmalloc(a.nbytes)
                 _native.check(L.b200_memcpy_h2d(p, a.ctypes.data_as(ctypes.c_void_p), a.nbytes))
                 dparams[i] = p

@@ -197,3 +197,20 @@ def test_schedule_examples():
     s = _schedule(1, 64, 64, 20000)
     assert s["whole"] == 0 and s["pieces"] >= 3
     assert _native.lib().b200_debug_schedule(2, 1, 1, 1, (ctypes.c_int64 * 8)()) == 1
+
+
+def test_weights_register_validation_without_a_gpu():
+    """Registration is host bookkeeping: argument checks, idempotent
+    re-registration and release need no device."""
+    import ctypes
+    import numpy as np
+    lib = _native.lib()
+    W = np.zeros((8, 4), np.float32)
+    p = ctypes.c_void_p(W.ctypes.data)
+    assert lib.b200_weights_register(None, 4, 8, 4, 0) == 1
+    assert lib.b200_weights_register(p, 3, 8, 4, 0) == 1  # ldw < N
+    assert lib.b200_weights_register(p, 4, 8, 4, 0) == 0
+    assert lib.b200_weights_register(p, 4, 8, 4, 0) == 0
+    assert lib.b200_weights_register(p, 4, 8, 4, 1) == 0
+    assert lib.b200_weights_release(p) == 0
+    assert lib.b200_weights_release(p) == 1 and b"not registered" in lib.b200_last_error()
