@@ -264,6 +264,18 @@ int b200_dense_f32_peers(const float* X, int64_t ldx, const float* W, int64_t ld
                          const float* b, float* Y, int64_t ldy, float* const* peer_y, int npeers,
                          int64_t M, int64_t N, int64_t K, int act, float alpha, void* stream);
 
+/* b200_dense_f32_multicast: the gathered dense layer through NVSwitch
+ * multicast (NVLS). mc_y is the multicast address of this call's Y rows (a
+ * multicast object every rank's output buffer is bound to, at the same
+ * offsets and pitch ldy); the GEMM epilogue (and the cut-tile reduction)
+ * stores every final value once with multimem.st and the switch writes it
+ * into every GPU's copy, so each value crosses this GPU's NVLink ports once
+ * whatever the number of peers. K must be > 0. Ordering against the peers as
+ * for b200_dense_f32_peers. No counterpart in the reference. */
+int b200_dense_f32_multicast(const float* X, int64_t ldx, const float* W, int64_t ldw,
+                             const float* b, float* Y, int64_t ldy, float* mc_y, int64_t M,
+                             int64_t N, int64_t K, int act, float alpha, void* stream);
+
 /* Stream-ordered barrier of the `world` GPUs (<= 8) of a gathered call, as
  * one small kernel on `stream`: rank `rank` stores `epoch` into its slot of
  * every peer's flag array (after a system-scope fence, so its earlier stores

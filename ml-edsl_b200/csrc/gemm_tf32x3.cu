@@ -327,15 +327,27 @@ struct Epilogue {
   // CUDA IPC), with ordinary stores that travel over NVLink as tiles finish.
   int npeers;
   float* peer[kMaxEpiloguePeers];
+  // Gathered result through NVSwitch multicast: the multicast address of Y
+  // (same element offsets); every final value is written once with
+  // multimem.st and lands in Y and in every peer's copy. Replaces Y / peers.
+  float* mc;
 };
 
-// Final values: Y and every peer copy.
+// Final values: Y and every peer copy (one multicast store when ep.mc is set).
 __device__ __forceinline__ void store_final4(const Epilogue& ep, int64_t off, float4 v) {
+  if (ep.mc) {
+    multimem_st_v4(ep.mc + off, v);
+    return;
+  }
   *reinterpret_cast<float4*>(ep.Y + off) = v;
 #pragma unroll 1
   for (int p = 0; p < ep.npeers; ++p) *reinterpret_cast<float4*>(ep.peer[p] + off) = v;
 }
 __device__ __forceinline__ void store_final1(const Epilogue& ep, int64_t off, float v) {
+  if (ep.mc) {
+    multimem_st(ep.mc + off, v);
+    return;
+  }
   ep.Y[off] = v;
 #pragma unroll 1
   for (int p = 0; p < ep.npeers; ++p) ep.peer[p][off] = v;
@@ -1140,11 +1152,13 @@ static int dispatch_gemm(const float* xa, const float* xlo, int64_t ldx, bool fu
 namespace {
 thread_local int tl_npeers = 0;
 thread_local float* tl_peers[kMaxEpiloguePeers] = {};
+thread_local float* tl_mc = nullptr;
 }  // namespace
 
-void set_epilogue_peers(float* const* peers, int n) {
+void set_epilogue_peers(float* const* peers, int n, float* mc) {
   tl_npeers = (peers != nullptr && n > 0) ? std::min(n, kMaxEpiloguePeers) : 0;
   for (int i = 0; i < kMaxEpiloguePeers; ++i) tl_peers[i] = i < tl_npeers ? peers[i] : nullptr;
+  tl_mc = mc;
 }
 
 static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool fused,
@@ -1271,6 +1285,8 @@ static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool
     ep.peer[i] = tl_peers[i];
     if (i < ep.npeers && (reinterpret_cast<uintptr_t>(tl_peers[i]) & 15) != 0) ep.vec_out = 0;
   }
+  ep.mc = tl_mc;
+  if (ep.mc && (reinterpret_cast<uintptr_t>(ep.mc) & 15) != 0) ep.vec_out = 0;
   int rc = dispatch_gemm(xa, xlo, ldx, fused, bop, M, N, K, sc, ep, status, stream);
   if (rc != kOk || sc.rest == 0) return rc;
   const int tile_m = kBM;

@@ -60,10 +60,14 @@ inline int64_t split_pitch(int64_t K) { return (K + 7) & ~int64_t(7); }
 // pitch as Y) apply to the dense launches this thread makes while an
 // EpiloguePeersScope is alive.
 constexpr int kMaxEpiloguePeers = 7;
-void set_epilogue_peers(float* const* peers, int n);
+// With `mc` (the NVSwitch multicast address of Y) set instead, every final
+// value is stored once with multimem.st and reaches Y and all peers' copies.
+void set_epilogue_peers(float* const* peers, int n, float* mc = nullptr);
 struct EpiloguePeersScope {
-  EpiloguePeersScope(float* const* peers, int n) { set_epilogue_peers(peers, n); }
-  ~EpiloguePeersScope() { set_epilogue_peers(nullptr, 0); }
+  EpiloguePeersScope(float* const* peers, int n, float* mc = nullptr) {
+    set_epilogue_peers(peers, n, mc);
+  }
+  ~EpiloguePeersScope() { set_epilogue_peers(nullptr, 0, nullptr); }
   EpiloguePeersScope(const EpiloguePeersScope&) = delete;
   EpiloguePeersScope& operator=(const EpiloguePeersScope&) = delete;
 };

@@ -89,6 +89,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   return mbar_wait_for(bar, parity, status, code, abort_flag, B200_WAIT_NS);
 }
 
+// ---------------------------------------------------------------- multicast
+// Stores through an NVSwitch multicast address: one store reaches the same
+// offset in every GPU's memory bound to the multicast object (NVLS).
+__device__ __forceinline__ void multimem_st_v4(float* mc, float4 v) {
+  asm volatile("multimem.st.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void multimem_st(float* mc, float v) {
+  asm volatile("multimem.st.global.f32 [%0], %1;" ::"l"(mc), "f"(v) : "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, uint64_t* bar,
                                             int32_t x, int32_t y) {

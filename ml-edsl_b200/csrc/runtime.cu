@@ -1238,6 +1238,31 @@ int b200_dense_f32_peers(const float* X, int64_t ldx, const float* W, int64_t ld
   return rc ? rc : succeed();
 }
 
+int b200_dense_f32_multicast(const float* X, int64_t ldx, const float* W, int64_t ldw,
+                             const float* b, float* Y, int64_t ldy, float* mc_y, int64_t M,
+                             int64_t N, int64_t K, int act, float alpha, void* stream) {
+  int rc = validate_dense(X, ldx, W, ldw, Y, ldy, M, N, K, act);
+  if (rc) return rc;
+  if (!mc_y) return fail(kErrInvalidArg, "null multicast output");
+  if (M > 0 && N > 0 && K == 0)
+    return fail(kErrInvalidArg, "the multicast entry point needs K > 0");
+  DeviceCtx* c = nullptr;
+  if ((rc = current_ctx(&c))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* ws = nullptr;
+  ScratchLease lease;  // held until the kernels that use ws are queued
+  if (M > 0 && N > 0) {
+    const size_t need = (size_t)dense_scratch_bytes(M, N, K);
+    if ((rc = lease.acquire(c, st, need))) return rc;
+    ws = lease.p;
+  }
+  {
+    const EpiloguePeersScope peers(nullptr, 0, mc_y);
+    rc = dense_device(c, X, ldx, W, ldw, b, Y, ldy, M, N, K, act, alpha, ws, st);
+  }
+  return rc ? rc : succeed();
+}
+
 int b200_dense_f32_chain(const float* X, int64_t ldx, const float* Xlo, const float* W,
                          int64_t ldw, const float* b, float* Y, int64_t ldy, float* Ylo,
                          int64_t ldylo, int64_t M, int64_t N, int64_t K, int act, float alpha,

@@ -35,7 +35,7 @@ EXPORTED_SYMBOLS = [
     "b200_dense_f32_wsplit",
     "b200_malloc", "b200_free", "b200_memcpy_h2d", "b200_memcpy_d2h",
     "b200_selftest_wait_timeout", "b200_debug_fail_alloc", "b200_debug_schedule", "b200_set_gemm_sm_limit", "b200_dense_f32_chain",
-    "b200_dense_f32_peers", "b200_peer_barrier",
+    "b200_dense_f32_peers", "b200_peer_barrier", "b200_dense_f32_multicast",
     "b200_ipc_alloc", "b200_ipc_free", "b200_ipc_open", "b200_ipc_close", "b200_memcpy_d2d_async",
     "b200_host_alloc", "b200_host_free",
     "b200_dense_f32_host", "b200_matmul_i32_host", "b200_bias_act_f32_host",
@@ -105,6 +105,8 @@ def _declare(lib):
                                   f32, vp], i32),
         "b200_dense_f32_peers": ([vp, i64, vp, i64, vp, vp, i64, c.POINTER(vp), i32, i64, i64,
                                   i64, i32, f32, vp], i32),
+        "b200_dense_f32_multicast": ([vp, i64, vp, i64, vp, vp, i64, vp, i64, i64, i64, i32,
+                                      f32, vp], i32),
         "b200_peer_barrier": ([c.POINTER(vp), i32, i32, c.c_uint32, i64, vp], i32),
         "b200_ipc_alloc": ([c.POINTER(vp), i64, vp], i32),
         "b200_ipc_free": ([vp], i32),

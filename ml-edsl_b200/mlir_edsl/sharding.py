@@ -206,6 +206,89 @@ class _PeerRows:
             ctypes.c_void_p(stream.cuda_stream)))
 
 
+class _McRows:
+    """Each rank's [world * rows, N] f32 output buffer, followed by its peer
+    barrier flags, in PyTorch symmetric memory whose buffers are bound to one
+    NVSwitch multicast object (NVLS): a store to the multicast address lands
+    in every rank's buffer. Cached per (rows, N, device, group); held until
+    the process exits. Raises RuntimeError on every rank alike when the GPUs
+    offer no multicast."""
+
+    _cache = {}
+
+    @classmethod
+    def get(cls, rows, N, device, group):
+        key = (rows, N, device.index, id(group))
+        if key not in cls._cache:
+            cls._cache[key] = cls(rows, N, device, group)
+        return cls._cache[key]
+
+    def __init__(self, rows, N, device, group):
+        import ctypes
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        g = group if group is not None else dist.group.WORLD
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        self.world, self.rank = world, rank
+        data = world * rows * N
+        self.flags_off = (data * 4 + 255) // 256 * 256
+        err = ""
+        try:
+            with torch.cuda.device(device):
+                self.buf = symm_mem.empty(self.flags_off // 4 + 64, dtype=torch.float32,
+                                          device=device)
+                self.buf[self.flags_off // 4:].zero_()
+                self.hdl = symm_mem.rendezvous(self.buf, g)
+                torch.cuda.synchronize(device)
+            if not self.hdl.multicast_ptr:
+                err = "no NVSwitch multicast on this GPU"
+        except Exception as ex:  # agreed below, so every rank fails alike
+            err = f"symmetric memory: {ex}"[:300]
+        ok = torch.tensor([0 if err else 1], device=device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if not int(ok.item()):
+            raise RuntimeError("multicast output buffers unavailable"
+                               + (f": {err}" if err else " on another rank"))
+        self.ptrs = [int(p) for p in self.hdl.buffer_ptrs]
+        self.local = self.ptrs[rank]
+        self.mc = int(self.hdl.multicast_ptr)
+        self.Y = self.buf[:data].view(world * rows, N)
+        self.flag_ptrs = (ctypes.c_void_p * world)(*[p + self.flags_off for p in self.ptrs])
+        self.epoch = 0
+
+    barrier = _PeerRows.barrier
+
+
+def dense_rows_multicast(X_local, W, b, act: int, alpha: float, *, group=None):
+    """The gathered dense layer through NVSwitch multicast: this rank's rows
+    are computed once by b200_dense_f32_multicast, whose epilogue writes every
+    finished value once to the multicast address of its rows, and the switch
+    delivers it into every rank's output buffer. Ordered against the peers by
+    peer barriers on the stream. Returns the full [world * rows, N] result,
+    valid for work on this stream until the next call of this shape."""
+    import ctypes
+    import torch
+    import torch.distributed as dist
+    from . import _native
+    L = _native.lib()
+    rank = dist.get_rank(group)
+    rows, K = X_local.shape
+    N = W.shape[1]
+    device = X_local.device
+    buf = _McRows.get(rows, N, device, group)
+    stream = torch.cuda.current_stream(device)
+    buf.barrier(stream)  # every rank is done with its previous result
+    off = rank * rows * N * 4
+    p = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None
+    _native.check(L.b200_dense_f32_multicast(p(X_local), X_local.stride(0), p(W), W.stride(0),
+                                             p(b), ctypes.c_void_p(buf.local + off), N,
+                                             ctypes.c_void_p(buf.mc + off), rows, N, K, act,
+                                             alpha, ctypes.c_void_p(stream.cuda_stream)))
+    buf.barrier(stream)  # every rank's rows are in every buffer
+    return buf.Y
+
+
 def gather_rows_ce(rows: int, N: int, compute_slab, *, slabs: int = 4, group=None, device=None):
     """gather_rows_pipelined over the copy engines: each rank computes its rows
     slab by slab into its own region of a persistent IPC-shared output buffer
@@ -299,7 +382,9 @@ def dense_rows(X_local, W, b=None, act: int = 1, alpha: float = 0.0, *, gather: 
     current stream. gather=False returns this rank's rows (no communication);
     gather=True returns the full result on every rank, all-gathered with NCCL
     over NVLink slab by slab while later slabs compute (every rank must hold
-    the same number of rows). transport "ce" pushes finished slabs into the
+    the same number of rows). transport "multimem" has the GEMM's epilogue
+    write every finished value once to an NVSwitch multicast address that
+    reaches all ranks' buffers (see dense_rows_multicast); "ce" pushes finished slabs into the
     peers' IPC-mapped output buffers with the copy engines (no SMs, overlaps
     the next slab's GEMM; the result is a persistent buffer valid until the
     next call of this shape); "fused" has the GEMM's epilogue store every
@@ -329,9 +414,13 @@ def dense_rows(X_local, W, b=None, act: int = 1, alpha: float = 0.0, *, gather: 
         return Y
     import torch.distributed as dist
     world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
-    if transport not in ("ce", "nccl", "fused"):
+    if transport not in ("ce", "nccl", "fused", "multimem"):
         raise ValueError(f"unknown transport {transport!r}")
     check_equal_rows(M, group, X_local.device)
+    if transport == "multimem" and world > 1:
+        if K == 0:
+            raise ValueError("the multimem transport needs K > 0")
+        return dense_rows_multicast(X_local, W, b, act, alpha, group=group)
     if transport == "fused" and world > 1:
         return dense_rows_fused(X_local, W, b, act, alpha, group=group)
     if transport == "ce" and world > 1:

@@ -1,8 +1,9 @@
 """Row-sharded dense layer over 2 GPUs with a single-device result requested:
 dense_rows(gather=True) assembles Y on every rank slab by slab while later
 slabs compute, by peer DMA into IPC-mapped buffers (transport "ce"), by
-NCCL all-gather (transport "nccl"), or by the GEMM epilogue's own stores into
-the peers' buffers (transport "fused"). Run as 2 ranks under torchrun; skipped with fewer
+NCCL all-gather (transport "nccl"), by the GEMM epilogue's own stores into
+the peers' buffers (transport "fused"), or by its stores to an NVSwitch
+multicast address (transport "multimem"). Run as 2 ranks under torchrun; skipped with fewer
 than 2 GPUs."""
 import os
 import socket
@@ -34,13 +35,27 @@ b = rng.uniform(-1, 1, N).astype(np.float32)
 tX = torch.from_numpy(X[rank * rows:(rank + 1) * rows]).to(dev)
 tW, tb = torch.from_numpy(W).to(dev), torch.from_numpy(b).to(dev)
 ref = oracle.dense_f32(X, W, b, act=1)
-for transport in ("ce", "nccl", "fused"):
+for transport in ("ce", "nccl", "fused", "multimem"):
     for slabs in (1, 3, 3):  # the repeated call reuses the persistent IPC buffers
         Y = dense_rows(tX, tW, tb, 1, 0.0, gather=True, slabs=slabs, transport=transport)
         torch.cuda.synchronize()
         assert Y.shape == (world * rows, N)
         got = Y.cpu().numpy()
         assert max_err(got, ref) <= oracle.f32_bound(K, X, W), (transport, slabs)
+# back-to-back gathered calls with no host synchronisation in between: the
+# peer barriers on the stream order each call's stores against the peers'
+# reads of the previous result (each result is copied out on the stream)
+for transport in ("fused", "ce", "multimem"):
+    outs = []
+    for i in range(4):
+        Xi = tX * (1.0 + 0.25 * i)
+        Y = dense_rows(Xi, tW, tb, 1, 0.0, gather=True, slabs=2, transport=transport)
+        outs.append(Y.clone())
+    torch.cuda.synchronize()
+    for i, Yi in enumerate(outs):
+        Xs = (X * np.float32(1.0 + 0.25 * i)).astype(np.float32)
+        assert max_err(Yi.cpu().numpy(), oracle.dense_f32(Xs, W, b, act=1)) <= \
+            oracle.f32_bound(K, Xs, W), (transport, i)
 loc = dense_rows(tX, tW, tb, 1, 0.0, gather=False).cpu().numpy()
 assert loc.shape == (rows, N)
 assert max_err(loc, got[rank * rows:(rank + 1) * rows]) <= oracle.f32_bound(K, X, W)
