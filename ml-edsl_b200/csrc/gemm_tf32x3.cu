@@ -526,28 +526,13 @@ struct UmmaDescBMn {
   }
 };
 
-// kFusedA: the A operand arrives as raw f32 X tiles (one TMA load into the
-// A_hi slot). The tensor core reads a tf32 operand from f32 bits by ignoring
-// the low 13 mantissa bits, so the raw tile serves as A_hi unchanged; the
-// epilogue warps derive A_lo = x - hi into the A_lo slot and release it to
-// the MMA through conv[s]. The MMA issues the two products that use A_hi as
-// soon as the tile lands and the lo * B_hi product after conv[s].
-//
 // kBMn: B_hi is the raw f32 W (row-major [K, N], read as an MN-major tf32
 // operand: the tensor core drops the low 13 mantissa bits, which is the hi
 // part) and B_lo the row-major lo part, so W needs neither a transpose nor a
 // hi copy. The producer warp's lanes issue the two B tiles and two A tiles of a
 // stage from separate lanes.
-//
-// kFuseB (with kBMn): W_lo is not read from memory at all. Two more warps
-// (kConvWarps) derive it in shared memory from the raw B tile that TMA has
-// landed, w -> w - tf32(w) truncated, written at the same (swizzled) offset
-// of the B_lo slot, and release the stage to the MMA through conv[s] after a
-// proxy fence. The MMA then issues the usual three products in the usual
-// order, so results are bit-identical to the path that reads W_lo.
-constexpr int kConvWarps = 2;
-template <class Cfg, bool kFusedA, bool kBMn, bool kFuseB>
-__global__ void __launch_bounds__(kThreads + (kFuseB ? 32 * kConvWarps : 0), 1)
+template <class Cfg, bool kBMn>
+__global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAhi,
                        const __grid_constant__ CUtensorMap tmAlo,
                        const __grid_constant__ CUtensorMap tmBhi,
@@ -560,8 +545,7 @@ __global__ void __launch_bounds__(kThreads + (kFuseB ? 32 * kConvWarps : 0), 1)
   uint64_t* empty = full + Cfg::Stages;                                   // MMA -> TMA
   uint64_t* tfull = empty + Cfg::Stages;   // MMA -> epilogue: chunk accumulator ready
   uint64_t* tempty = tfull + 2;        // epilogue -> MMA: chunk accumulator drained
-  uint64_t* conv = tempty + 2;         // epilogue -> MMA: A tile split (kFusedA)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(conv + Cfg::Stages);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -578,7 +562,6 @@ __global__ void __launch_bounds__(kThreads + (kFuseB ? 32 * kConvWarps : 0), 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], kEpiWarps);
     }
-    for (int s = 0; s < Cfg::Stages; ++s) mbar_init(&conv[s], kFuseB ? kConvWarps : kEpiWarps);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -599,8 +582,6 @@ __global__ void __launch_bounds__(kThreads + (kFuseB ? 32 * kConvWarps : 0), 1)
 
   // Ring stages and TMEM chunk buffers are counted across all units of the
   // CTA, so their mbarrier phases run on from one tile to the next.
-  static_assert(!(kFusedA && kBMn), "fused A split uses K-major B");
-  static_assert(!kFuseB || kBMn, "the in-kernel B_lo uses the MN-major layout");
   if (warp == 0 && kBMn) {
     // ------------------------------------------------ TMA producer (MN-major B)
     // Lane 0 waits for the stage and posts the byte count; the decision is
@@ -620,8 +601,7 @@ __global__ void __launch_bounds__(kThreads + (kFuseB ? 32 * kConvWarps : 0), 1)
               !mbar_wait(&empty[s], (round - 1) & 1, status, kDevTimeoutEmpty, abort_flag))
             go = 0;
           else
-            mbar_arrive_expect_tx(&full[s], kFuseB ? Cfg::StageBytes - Cfg::BTileBytes
-                                                   : Cfg::StageBytes);
+            mbar_arrive_expect_tx(&full[s], Cfg::StageBytes);
         }
         if (!__shfl_sync(0xffffffffu, go, 0)) {
           ok = false;
@@ -629,7 +609,7 @@ __global__ void __launch_bounds__(kThreads + (kFuseB ? 32 * kConvWarps : 0), 1)
         }
         uint8_t* st = smem + s * Cfg::StageBytes;
         const int kx = (w.kb0 + kb) * Cfg::BK;
-        if (lane < (kFuseB ? 1 : 2)) {  // whole 256-column B tile: {0, kx, n0 / 32}
+        if (lane < 2) {  // whole 256-column B tile: {0, kx, n0 / 32}
           tma_load_3d(st + 2 * Cfg::ATileBytes + lane * Cfg::BTileBytes,
                       lane == 0 ? &tmBhi : &tmBlo, &full[s], 0, kx, w.n0 / 32);
         } else if (lane == 2) {
@@ -654,14 +634,9 @@ __global__ void __launch_bounds__(kThreads + (kFuseB ? 32 * kConvWarps : 0), 1)
             break;
           uint8_t* st = smem + s * Cfg::StageBytes;
           const int kx = (w.kb0 + kb) * Cfg::BK;
-          if constexpr (kFusedA) {
-            mbar_arrive_expect_tx(&full[s], Cfg::ATileBytes + 2 * Cfg::BTileBytes);
-            tma_load_2d(st, &tmAhi, &full[s], kx, w.m0);  // raw f32 X tile
-          } else {
-            mbar_arrive_expect_tx(&full[s], Cfg::StageBytes);
-            tma_load_2d(st, &tmAhi, &full[s], kx, w.m0);
-            tma_load_2d(st + Cfg::ATileBytes, &tmAlo, &full[s], kx, w.m0);
-          }
+          mbar_arrive_expect_tx(&full[s], Cfg::StageBytes);
+          tma_load_2d(st, &tmAhi, &full[s], kx, w.m0);
+          tma_load_2d(st + Cfg::ATileBytes, &tmAlo, &full[s], kx, w.m0);
           tma_load_2d(st + 2 * Cfg::ATileBytes, &tmBhi, &full[s], kx, w.n0);
           tma_load_2d(st + 2 * Cfg::ATileBytes + Cfg::BTileBytes, &tmBlo, &full[s], kx, w.n0);
         }
@@ -698,36 +673,12 @@ __global__ void __launch_bounds__(kThreads + (kFuseB ? 32 * kConvWarps : 0), 1)
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + buf * kBN;
           const uint32_t st = smem_u32(smem + s * Cfg::StageBytes);
-          if constexpr (kFusedA) {
 #pragma unroll
-            for (int k = 0; k < Cfg::BK / 8; ++k) {
-              umma_tf32(d_tmem, D::a_hi(st, k), D::b_lo(st, k), idesc,
-                        (chunk_start && k == 0) ? 0u : 1u);
-              umma_tf32(d_tmem, D::a_hi(st, k), D::b_hi(st, k), idesc, 1u);
-            }
-            if (!mbar_wait(&conv[s], round & 1, status, kDevTimeoutFull, abort_flag)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-#pragma unroll
-            for (int k = 0; k < Cfg::BK / 8; ++k)
-              umma_tf32(d_tmem, D::a_lo(st, k), D::b_hi(st, k), idesc, 1u);
-          } else {
-            if constexpr (kFuseB) {  // B_lo of this stage derived in shared memory
-              if (!mbar_wait(&conv[s], round & 1, status, kDevTimeoutFull, abort_flag)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-            }
-#pragma unroll
-            for (int k = 0; k < Cfg::BK / 8; ++k) {  // tf32 UMMA consumes K = 8
-              umma_tf32(d_tmem, D::a_lo(st, k), DB::b_hi(st, k), idesc,
-                        (chunk_start && k == 0) ? 0u : 1u);
-              umma_tf32(d_tmem, D::a_hi(st, k), DB::b_lo(st, k), idesc, 1u);
-              umma_tf32(d_tmem, D::a_hi(st, k), DB::b_hi(st, k), idesc, 1u);
-            }
+          for (int k = 0; k < Cfg::BK / 8; ++k) {  // tf32 UMMA consumes K = 8
+            umma_tf32(d_tmem, D::a_lo(st, k), DB::b_hi(st, k), idesc,
+                      (chunk_start && k == 0) ? 0u : 1u);
+            umma_tf32(d_tmem, D::a_hi(st, k), DB::b_lo(st, k), idesc, 1u);
+            umma_tf32(d_tmem, D::a_hi(st, k), DB::b_hi(st, k), idesc, 1u);
           }
           umma_commit(&empty[s]);  // stage s may be refilled once these MMAs finish
           if (chunk_end) {
@@ -735,40 +686,6 @@ __global__ void __launch_bounds__(kThreads + (kFuseB ? 32 * kConvWarps : 0), 1)
             ++cc;
           }
         }
-      }
-    }
-  } else if (kFuseB && warp >= 2 + kEpiWarps) {
-    // ------------------------------------------------ B_lo converters (kFuseB)
-    const int ct = threadIdx.x - 32 * (2 + kEpiWarps);  // 0 .. 32 * kConvWarps - 1
-    int it = 0;
-    bool ok = true;
-#pragma unroll 1
-    for (int u = blockIdx.x; u < sc.units && ok; u += gridDim.x) {
-      const Unit w = unit_of(u);
-#pragma unroll 1
-      for (int kb = 0; kb < w.nkb; ++kb, ++it) {
-        const int s = it % Cfg::Stages;
-        if (!mbar_wait(&full[s], (it / Cfg::Stages) & 1, status, kDevTimeoutFull, abort_flag)) {
-          ok = false;
-          break;
-        }
-        const float4* hi =
-            reinterpret_cast<const float4*>(smem + s * Cfg::StageBytes + 2 * Cfg::ATileBytes);
-        float4* lo = reinterpret_cast<float4*>(smem + s * Cfg::StageBytes + 2 * Cfg::ATileBytes +
-                                               Cfg::BTileBytes);
-#pragma unroll 4
-        for (int i = ct; i < Cfg::BTileBytes / 16; i += 32 * kConvWarps) {
-          const float4 v = hi[i];
-          float4 h, l;  // h is what the tensor core reads from v
-          tf32_split(v.x, h.x, l.x);
-          tf32_split(v.y, h.y, l.y);
-          tf32_split(v.z, h.z, l.z);
-          tf32_split(v.w, h.w, l.w);
-          lo[i] = l;
-        }
-        fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&conv[s]);
       }
     }
   } else {
@@ -780,7 +697,6 @@ __global__ void __launch_bounds__(kThreads + (kFuseB ? 32 * kConvWarps : 0), 1)
     float acc[128];
     bool ok = true;
     int ce = 0;  // TMEM chunks drained by this CTA
-    int it = 0;  // k-blocks converted (kFusedA)
     // Adds the next chunk's partial sums (TMEM buffer ce % 2) into acc, frees it.
     auto drain = [&]() -> bool {
       const int buf = ce & 1;
@@ -808,50 +724,8 @@ __global__ void __launch_bounds__(kThreads + (kFuseB ? 32 * kConvWarps : 0), 1)
       const int num_chunks = (w.nkb + Cfg::ChunkKB - 1) / Cfg::ChunkKB;
 #pragma unroll
       for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
-      if constexpr (kFusedA) {
-        // Derive every A tile's lo part as it lands; drain chunk c once the
-        // conversion has run kDrainLag k-blocks past its last one, so the MMA
-        // always has converted tiles queued while the drain runs.
-        constexpr int kDrainLag = 2;
-        const int et = threadIdx.x - 64;  // 0..255
-        int next = 0;
 #pragma unroll 1
-        for (int kb = 0; kb < w.nkb && ok; ++kb, ++it) {
-          const int s = it % Cfg::Stages;
-          if (!mbar_wait(&full[s], (it / Cfg::Stages) & 1, status, kDevTimeoutFull,
-                         abort_flag)) {
-            ok = false;
-            break;
-          }
-          const float4* a = reinterpret_cast<const float4*>(smem + s * Cfg::StageBytes);
-          float4* lo = reinterpret_cast<float4*>(smem + s * Cfg::StageBytes + Cfg::ATileBytes);
-#pragma unroll
-          for (int i = et; i < Cfg::ATileBytes / 16; i += 32 * kEpiWarps) {
-            const float4 v = a[i];
-            float4 h, l;  // h is what the tensor core reads from v
-            tf32_split(v.x, h.x, l.x);
-            tf32_split(v.y, h.y, l.y);
-            tf32_split(v.z, h.z, l.z);
-            tf32_split(v.w, h.w, l.w);
-            lo[i] = l;
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&conv[s]);
-          while (ok && next < num_chunks &&
-                 min((next + 1) * Cfg::ChunkKB, w.nkb) - 1 + kDrainLag <= kb) {
-            ok = drain();
-            ++next;
-          }
-        }
-        while (ok && next < num_chunks) {
-          ok = drain();
-          ++next;
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < num_chunks && ok; ++c) ok = drain();
-      }
+      for (int c = 0; c < num_chunks && ok; ++c) ok = drain();
       if (!ok || *abort_flag) break;
       // The MMAs of the next unit proceed into the two TMEM buffers while
       // this tile is stored.
@@ -1073,7 +947,7 @@ static cudaError_t launch_dependent(bool pdl, void (*kernel)(KArgs...), unsigned
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-template <class Cfg, bool kFusedA, bool kBMn, bool kFuseB = false>
+template <class Cfg, bool kBMn>
 static int launch_gemm(const CUtensorMap& ta_hi, const CUtensorMap& ta_lo,
                        const CUtensorMap& tb_hi, const CUtensorMap& tb_lo, int64_t M, int64_t N,
                        int64_t K, const Sched& sc, const Epilogue& ep, int* status,
@@ -1081,72 +955,47 @@ static int launch_gemm(const CUtensorMap& ta_hi, const CUtensorMap& ta_lo,
   // The dynamic shared-memory opt-in is made once per device (thread-safe).
   static std::atomic<uint64_t> attr_done{0};
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return kErrCuda;
+  if (cudaGetDevice(&dev) != cudaSuccess) return launch_result();
   const uint64_t bit = 1ull << (dev & 63);
   if (!(attr_done.load() & bit)) {
-    if (cudaFuncSetAttribute(gemm_tf32x3_kernel<Cfg, kFusedA, kBMn, kFuseB>,
+    if (cudaFuncSetAttribute(gemm_tf32x3_kernel<Cfg, kBMn>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Cfg::SmemBytes) != cudaSuccess)
       return launch_result();
     attr_done.fetch_or(bit);
   }
-  const int units = sc.units;
   // Persistent: one CTA per SM (the shared-memory ring admits one) walks the
   // work units with stride gridDim.x.
   const int sms = sm_count();
   if (sms <= 0) return kErrCuda;
-  // B200_PERSIST=0: one CTA per unit (the non-persistent schedule), for A/B.
-  static const bool persist = [] {
-    const char* e = getenv("B200_PERSIST");
-    return !(e && e[0] == '0');
-  }();
-  const int grid = persist ? std::min(units, sms) : units;
+  const int grid = std::min(sc.units, sms);
   const cudaError_t e =
-      launch_dependent(pdl_enabled(M, N, K), gemm_tf32x3_kernel<Cfg, kFusedA, kBMn, kFuseB>,
-                       (unsigned)grid, kThreads + (kFuseB ? 32 * kConvWarps : 0),
-                       Cfg::SmemBytes, stream, ta_hi, ta_lo, tb_hi,
-                       tb_lo, sc, ep, status);
+      launch_dependent(pdl_enabled(M, N, K), gemm_tf32x3_kernel<Cfg, kBMn>, (unsigned)grid,
+                       kThreads, Cfg::SmemBytes, stream, ta_hi, ta_lo, tb_hi, tb_lo, sc, ep,
+                       status);
   count_launch();
   return launch_result(e);
 }
 
 // A operand: hi from `xa` with row pitch ldx (the pre-split xhi with pitch
-// Kp, or raw X), lo from xlo (pitch Kp); fused: lo derived in the kernel.
-template <class Cfg>
-static int run_gemm(const float* xa, const float* xlo, int64_t ldx, bool fused, const BOp& b,
-                    int64_t M, int64_t N, int64_t K, const Sched& sc, const Epilogue& ep,
-                    int* status, cudaStream_t stream) {
+// Kp, or raw X), lo from xlo (pitch Kp).
+static int dispatch_gemm(const float* xa, const float* xlo, int64_t ldx, const BOp& b, int64_t M,
+                         int64_t N, int64_t K, const Sched& sc, const Epilogue& ep, int* status,
+                         cudaStream_t stream) {
   const int64_t Kp = split_pitch(K);
   CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
   int rc = make_tmap(&ta_hi, xa, K, M, ldx, kBM, Cfg::BK);
-  if (rc == kOk) rc = make_tmap(&ta_lo, fused ? xa : xlo, K, M, fused ? ldx : Kp, kBM, Cfg::BK);
+  if (rc == kOk) rc = make_tmap(&ta_lo, xlo, K, M, Kp, kBM, Cfg::BK);
   if (b.mn) {
-    if (fused) return kErrInvalidArg;
     if (rc == kOk) rc = make_tmap_mn(&tb_hi, b.hi, N, K, b.ld_hi, Cfg::BK);
-    if (b.lo == nullptr) {  // B_lo derived in shared memory
-      if (rc != kOk) return rc;
-      return launch_gemm<Cfg, false, true, true>(ta_hi, ta_lo, tb_hi, tb_hi, M, N, K, sc, ep,
-                                                 status, stream);
-    }
     if (rc == kOk) rc = make_tmap_mn(&tb_lo, b.lo, N, K, b.ld_lo, Cfg::BK);
     if (rc != kOk) return rc;
-    return launch_gemm<Cfg, false, true>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, sc, ep, status,
-                                         stream);
+    return launch_gemm<Cfg, true>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, sc, ep, status, stream);
   }
   if (rc == kOk) rc = make_tmap(&tb_hi, b.hi, K, N, b.ld_hi, kBN, Cfg::BK);
   if (rc == kOk) rc = make_tmap(&tb_lo, b.lo, K, N, b.ld_lo, kBN, Cfg::BK);
   if (rc != kOk) return rc;
-  if (fused)
-    return launch_gemm<Cfg, true, false>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, sc, ep, status,
-                                         stream);
-  return launch_gemm<Cfg, false, false>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, sc, ep, status,
-                                        stream);
-}
-
-static int dispatch_gemm(const float* xa, const float* xlo, int64_t ldx, bool fused, const BOp& b,
-                         int64_t M, int64_t N, int64_t K, const Sched& sc, const Epilogue& ep,
-                         int* status, cudaStream_t stream) {
-  return run_gemm<Cfg>(xa, xlo, ldx, fused, b, M, N, K, sc, ep, status, stream);
+  return launch_gemm<Cfg, false>(ta_hi, ta_lo, tb_hi, tb_lo, M, N, K, sc, ep, status, stream);
 }
 
 namespace {
@@ -1161,7 +1010,7 @@ void set_epilogue_peers(float* const* peers, int n, float* mc) {
   tl_mc = mc;
 }
 
-static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool fused,
+static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx,
                             const BOp& bop, int64_t M, int64_t N, int64_t K, const float* bias,
                             float* Y, int64_t ldy, int act, float alpha, int splits,
                             float* partials, int* status, cudaStream_t stream,
@@ -1171,7 +1020,7 @@ int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
                          const float* wloT, int64_t M, int64_t N, int64_t K, const float* bias,
                          float* Y, int64_t ldy, int act, float alpha, int* status,
                          cudaStream_t stream) {
-  return gemm_with_splits(xhi, xlo, split_pitch(K), false, bop_k(whiT, wloT, K), M, N, K,
+  return gemm_with_splits(xhi, xlo, split_pitch(K), bop_k(whiT, wloT, K), M, N, K,
                           bias, Y, ldy, act, alpha, 1, nullptr, status, stream);
 }
 
@@ -1260,7 +1109,7 @@ int64_t splitk_partials_bytes(int64_t M, int64_t N, int64_t K) {
 // One GEMM call: `splits` > 1 (with `partials` sized by splitk_partials_bytes)
 // lets the schedule cut the tiles of a partial last wave into K pieces;
 // otherwise every tile runs over all of K.
-static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool fused,
+static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx,
                             const BOp& bop, int64_t M, int64_t N, int64_t K, const float* bias,
                             float* Y, int64_t ldy, int act, float alpha, int splits,
                             float* partials, int* status, cudaStream_t stream, float* ylo,
@@ -1287,7 +1136,7 @@ static int gemm_with_splits(const float* xa, const float* xlo, int64_t ldx, bool
   }
   ep.mc = tl_mc;
   if (ep.mc && (reinterpret_cast<uintptr_t>(ep.mc) & 15) != 0) ep.vec_out = 0;
-  int rc = dispatch_gemm(xa, xlo, ldx, fused, bop, M, N, K, sc, ep, status, stream);
+  int rc = dispatch_gemm(xa, xlo, ldx, bop, M, N, K, sc, ep, status, stream);
   if (rc != kOk || sc.rest == 0) return rc;
   const int tile_m = kBM;
   const int64_t quads = (int64_t)sc.rest * tile_m * (kBN / 4);
@@ -1304,7 +1153,7 @@ int gemm_tf32x3_splitk(const float* xhi, const float* xlo, const float* whiT, co
                        int64_t M, int64_t N, int64_t K, const float* bias, float* Y, int64_t ldy,
                        int act, float alpha, int splits, float* partials, int* status,
                        cudaStream_t stream, float* ylo, int64_t ldylo) {
-  return gemm_with_splits(xhi, xlo, split_pitch(K), false, bop_k(whiT, wloT, K), M, N, K,
+  return gemm_with_splits(xhi, xlo, split_pitch(K), bop_k(whiT, wloT, K), M, N, K,
                           bias, Y, ldy, act, alpha, splits, partials, status, stream, ylo, ldylo);
 }
 
@@ -1337,22 +1186,13 @@ int gemm_tf32x3_xraw(const float* X, int64_t ldx, const float* xlo, const float*
                      const float* wloT, int64_t M, int64_t N, int64_t K, const float* bias,
                      float* Y, int64_t ldy, int act, float alpha, int splits, float* partials,
                      int* status, cudaStream_t stream, float* ylo, int64_t ldylo) {
-  if (!fused_a_ok(X, ldx)) return kErrInvalidArg;
-  return gemm_with_splits(X, xlo, ldx, false, bop_k(whiT, wloT, K), M, N, K, bias, Y, ldy, act,
+  if (!x_raw_ok(X, ldx)) return kErrInvalidArg;
+  return gemm_with_splits(X, xlo, ldx, bop_k(whiT, wloT, K), M, N, K, bias, Y, ldy, act,
                           alpha, splits, partials, status, stream, ylo, ldylo);
 }
 
-bool fused_a_ok(const float* X, int64_t ldx) {
+bool x_raw_ok(const float* X, int64_t ldx) {
   return ((ldx & 3) == 0) && ((reinterpret_cast<uintptr_t>(X) & 15) == 0);
-}
-
-int gemm_tf32x3_fused(const float* X, int64_t ldx, const float* whiT, const float* wloT,
-                      int64_t M, int64_t N, int64_t K, const float* bias, float* Y, int64_t ldy,
-                      int act, float alpha, int splits, float* partials, int* status,
-                      cudaStream_t stream, float* ylo, int64_t ldylo) {
-  if (!fused_a_ok(X, ldx)) return kErrInvalidArg;
-  return gemm_with_splits(X, nullptr, ldx, true, bop_k(whiT, wloT, K), M, N, K, bias, Y, ldy, act,
-                          alpha, splits, partials, status, stream, ylo, ldylo);
 }
 
 // ---------------------------------------------------------------------------
@@ -1371,14 +1211,6 @@ bool w_mn_ok(const float* W, int64_t ldw, int64_t M, int64_t N) {
 }
 
 int64_t w_lo_mn_bytes(int64_t K, int64_t N) { return K * ((N + 3) & ~int64_t(3)) * 4; }
-
-bool w_lo_in_kernel() {
-  static const bool on = [] {
-    const char* e = getenv("B200_FUSE_B");
-    return e && e[0] == '1';
-  }();
-  return on;
-}
 
 int split_lo_xw_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xhi, float* xlo,
                     const float* W, int64_t ldw, int64_t N, float* wlo, cudaStream_t stream) {
@@ -1401,9 +1233,9 @@ int gemm_tf32x3_wmn(const float* xa, const float* xlo, int64_t ldx, const float*
                     const float* wlo, int64_t M, int64_t N, int64_t K, const float* bias,
                     float* Y, int64_t ldy, int act, float alpha, int splits, float* partials,
                     int* status, cudaStream_t stream, float* ylo, int64_t ldylo) {
-  if (!fused_a_ok(xa, ldx) || !w_mn_ok(W, ldw, M, N)) return kErrInvalidArg;
-  const BOp b{W, wlo, ldw, (N + 3) & ~int64_t(3), true};  // wlo == nullptr: derived in-kernel
-  return gemm_with_splits(xa, xlo, ldx, false, b, M, N, K, bias, Y, ldy, act, alpha, splits,
+  if (!x_raw_ok(xa, ldx) || !w_mn_ok(W, ldw, M, N)) return kErrInvalidArg;
+  const BOp b{W, wlo, ldw, (N + 3) & ~int64_t(3), true};
+  return gemm_with_splits(xa, xlo, ldx, b, M, N, K, bias, Y, ldy, act, alpha, splits,
                           partials, status, stream, ylo, ldylo);
 }
 

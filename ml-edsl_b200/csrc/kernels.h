@@ -99,7 +99,7 @@ int split_xw_f32(const float* X, int64_t ldx, int64_t M, const float* W, int64_t
                  int64_t K, int64_t N, float* xhi, float* xlo, float* whiT, float* wloT,
                  cudaStream_t stream);
 
-// Raw-X A operand (X rows 16-byte aligned: fused_a_ok): the split pass
+// Raw-X A operand (X rows 16-byte aligned: x_raw_ok): the split pass
 // writes only the lo part [M, Kp]; the GEMM reads X itself as the hi part.
 int split_x_lo_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xlo,
                    cudaStream_t stream);
@@ -113,16 +113,12 @@ int gemm_tf32x3_xraw(const float* X, int64_t ldx, const float* xlo, const float*
 
 // MN-major B operand: the GEMM reads the row-major W itself as B_hi and a
 // row-major lo part W_lo [K, Np] (Np = roundup(N, 4)) as B_lo. w_mn_ok:
-// W rows 16-byte aligned, N % 32 == 0, M <= 4096, the 2-SM kernel not
-// selected and B200_W_MN not 0. split_lo_xw_f32 writes X's lo (and hi when
+// W rows 16-byte aligned, N % 32 == 0, M <= 4096 and B200_W_MN not 0. split_lo_xw_f32 writes X's lo (and hi when
 // xhi != nullptr; X may be null for W alone) and W_lo in one launch.
 bool w_mn_ok(const float* W, int64_t ldw, int64_t M, int64_t N);
 int64_t w_lo_mn_bytes(int64_t K, int64_t N);
 int split_lo_xw_f32(const float* X, int64_t ldx, int64_t M, int64_t K, float* xhi, float* xlo,
                     const float* W, int64_t ldw, int64_t N, float* wlo, cudaStream_t stream);
-// w_lo_in_kernel (B200_FUSE_B=1): pass wlo == nullptr and the GEMM derives
-// W_lo in shared memory from the raw W tiles (no W pass at all).
-bool w_lo_in_kernel();
 // xa: raw X (pitch ldx) or its pre-split hi part (pitch Kp); xlo pitch Kp.
 int gemm_tf32x3_wmn(const float* xa, const float* xlo, int64_t ldx, const float* W, int64_t ldw,
                     const float* wlo, int64_t M, int64_t N, int64_t K, const float* bias,
@@ -130,13 +126,9 @@ int gemm_tf32x3_wmn(const float* xa, const float* xlo, int64_t ldx, const float*
                     int* status, cudaStream_t stream, float* ylo = nullptr,
                     int64_t ldylo = 0);
 
-// Fused A split: raw X (pitch ldx, 16-byte aligned rows: fused_a_ok) is
-// split to tf32 hi/lo inside the GEMM; W pre-split as whiT/wloT.
-bool fused_a_ok(const float* X, int64_t ldx);
-int gemm_tf32x3_fused(const float* X, int64_t ldx, const float* whiT, const float* wloT,
-                      int64_t M, int64_t N, int64_t K, const float* bias, float* Y, int64_t ldy,
-                      int act, float alpha, int splits, float* partials, int* status,
-                      cudaStream_t stream, float* ylo = nullptr, int64_t ldylo = 0);
+// True when X (pitch ldx) can be read as the raw tf32 hi operand: 16-byte
+// aligned rows (TMA strides).
+bool x_raw_ok(const float* X, int64_t ldx);
 int gemm_tf32x3_presplit(const float* xhi, const float* xlo, const float* whiT,
                          const float* wloT, int64_t M, int64_t N, int64_t K, const float* bias,
                          float* Y, int64_t ldy, int act, float alpha, int* status,

@@ -541,18 +541,6 @@ SplitBufs carve(void* ws, int64_t M, int64_t N, int64_t K) {
   return s;
 }
 
-// B200_FUSE_A=1 moves the A-operand split into the GEMM (X rows must be
-// 16-byte aligned). Off by default: on B200 it measured slower (201 vs 231
-// TFLOP/s on the 65536 x 4096 x 4096 dense layer) than the separate
-// HBM-bound split pass, which costs ~4% of the step.
-bool fuse_a(const float* X, int64_t ldx) {
-  static const bool enabled = [] {
-    const char* e = getenv("B200_FUSE_A");
-    return e && e[0] == '1';
-  }();
-  return enabled && fused_a_ok(X, ldx);
-}
-
 // xlo_in (optional): X's tf32 lo part, pitch split_pitch(K), from the previous
 // layer's epilogue (X rows must then be 16-byte aligned: X itself is A_hi),
 // so X is not split again. ylo (optional, pitch ldylo): the epilogue also
@@ -567,13 +555,12 @@ int dense_device(DeviceCtx* c, const float* X, int64_t ldx, const float* W, int6
   const int splits = choose_splits(M, N, K);
   const int64_t Kp = split_pitch(K);
   float* xlo = xlo_in ? const_cast<float*>(xlo_in) : s.xlo;
-  const bool xraw = fused_a_ok(X, ldx);
+  const bool xraw = x_raw_ok(X, ldx);
   // W is a registered weight's device copy: its split is kept, only X is split
-  const bool fused = fuse_a(X, ldx) && !xlo_in;
   const bool mn = w_mn_ok(W, ldw, M, N);
   PreSplitW pre;
   bool have_pre = false;
-  if (!fused && !w_lo_in_kernel()) {
+  {
     std::lock_guard<std::mutex> g(g_w_mu);
     WeightEntry* e = g_weights.empty() ? nullptr : find_device_weights(c->dev, W);
     if (e && e->K == K && e->N == N && ldw == N) {
@@ -588,18 +575,13 @@ int dense_device(DeviceCtx* c, const float* X, int64_t ldx, const float* W, int6
                 : split_x_f32(X, ldx, M, K, s.xhi, s.xlo, st);
   };
   int rc;
-  if (fused) {
-    rc = split_w_f32(W, ldw, K, N, s.whi, s.wlo, st);
-    if (rc == kOk)
-      rc = gemm_tf32x3_fused(X, ldx, s.whi, s.wlo, M, N, K, b, Y, ldy, act, alpha, splits,
-                             s.partials, c->status, st, ylo, ldylo);
-  } else if (mn && (have_pre || w_lo_mn_bytes(K, N) <= reinterpret_cast<char*>(s.partials) -
+  if (mn && (have_pre || w_lo_mn_bytes(K, N) <= reinterpret_cast<char*>(s.partials) -
                                                           reinterpret_cast<char*>(s.whi))) {
     // W is read as-is (MN-major B_hi); its row-major lo part goes into the
     // W split region (or is the registered weight's). X likewise when its
     // rows are 16-byte aligned.
-    const float* wlo = have_pre ? pre.lo_mn : (w_lo_in_kernel() ? nullptr : s.whi);
-    if (have_pre || wlo == nullptr)
+    const float* wlo = have_pre ? pre.lo_mn : s.whi;
+    if (have_pre)
       rc = split_x_only();
     else if (xlo_in)  // X is pre-split: W alone
       rc = split_lo_xw_f32(nullptr, 0, 0, K, nullptr, nullptr, W, ldw, N, s.whi, st);
@@ -686,16 +668,15 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
   // Weights (replicated): a registered W's device copy and split are kept
   // (b200_weights_register); any other W is uploaded and split once per call
   // on the compute stream.
-  const bool fa = K > 0 && fuse_a(static_cast<float*>(c->x[0].p), K);
   PreSplitW pre;
   const float* regW = nullptr;
   bool have_pre = false;
-  if (K > 0 && !w_lo_in_kernel()) {
+  if (K > 0) {
     std::lock_guard<std::mutex> g(g_w_mu);
     WeightEntry* e = g_weights.empty() ? nullptr : find_host_weights(W, ldw, K, N);
     if (e) {
       // a registered copy is cudaMalloc'd (aligned), pitch N
-      const bool mn = !fa && w_mn_ok(reinterpret_cast<const float*>(256), N, M, N);
+      const bool mn = w_mn_ok(reinterpret_cast<const float*>(256), N, M, N);
       if ((rc = weights_ready(c, W, e, mn, &pre, &regW))) return rc;
       have_pre = true;
     }
@@ -725,17 +706,16 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
   float* dWhi = have_pre ? const_cast<float*>(pre.hiT) : static_cast<float*>(c->whi.p);
   float* dWlo = have_pre ? const_cast<float*>(pre.loT) : static_cast<float*>(c->wlo.p);
   float* db = b ? static_cast<float*>(c->bias.p) : nullptr;
-  // MN-major B (W read as-is, row-major lo part in dWhi) unless the fused A
-  // split is selected.
-  const bool wmn = K > 0 && !fuse_a(static_cast<float*>(c->x[0].p), K) && w_mn_ok(dW, N, M, N);
+  // MN-major B (W read as-is, row-major lo part in dWhi) when W qualifies.
+  const bool wmn = K > 0 && w_mn_ok(dW, N, M, N);
   if (b) B200_CUDA(cudaMemcpyAsync(db, b, N * 4, cudaMemcpyHostToDevice, c->s_comp), "H2D b");
   if (K > 0 && !have_pre) {
     if ((rc = h2d_rows(c, dW, N * 4, W, ldw * 4, N * 4, K, c->s_comp))) return rc;
     // A single-slab call splits W together with X (one launch) below.
-    if (nslab > 1 && wmn && !w_lo_in_kernel()) {
+    if (nslab > 1 && wmn) {
       rc = split_lo_xw_f32(nullptr, 0, 0, K, nullptr, nullptr, dW, N, N, dWhi, c->s_comp);
       if (rc) return fail(rc, "split W launch failed");
-    } else if (!wmn && (nslab > 1 || fuse_a(static_cast<float*>(c->x[0].p), K))) {
+    } else if (!wmn && nslab > 1) {
       rc = split_w_f32(dW, N, K, N, dWhi, dWlo, c->s_comp);
       if (rc) return fail(rc, "split W launch failed");
     }
@@ -772,16 +752,12 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
     } else {
       float* part = static_cast<float*>(c->part[slot].p);
       const int splits = choose_splits(rows, N, K);
-      if (fuse_a(dX, K)) {
-        rc = gemm_tf32x3_fused(dX, K, dWhi, dWlo, rows, N, K, db, dY, N, act, alpha, splits,
-                               part, c->status, c->s_comp);
-      } else if (wmn) {
+      if (wmn) {
         float* xhi = static_cast<float*>(c->xhi[slot].p);
         float* xlo = static_cast<float*>(c->xlo[slot].p);
-        const bool xraw = fused_a_ok(dX, K);
-        float* wlo = have_pre ? const_cast<float*>(pre.lo_mn)
-                              : (w_lo_in_kernel() ? nullptr : dWhi);
-        if (!w_split && wlo)
+        const bool xraw = x_raw_ok(dX, K);
+        float* wlo = have_pre ? const_cast<float*>(pre.lo_mn) : dWhi;
+        if (!w_split)
           rc = split_lo_xw_f32(dX, K, rows, K, xraw ? nullptr : xhi, xlo, dW, N, N, wlo,
                                c->s_comp);
         else
@@ -790,7 +766,7 @@ int dense_host_on_device(int dev, const float* X, int64_t ldx, const float* W, i
         if (rc == kOk)
           rc = gemm_tf32x3_wmn(xraw ? dX : xhi, xlo, xraw ? K : Kp, dW, N, wlo, rows, N, K, db,
                                dY, N, act, alpha, splits, part, c->status, c->s_comp);
-      } else if (fused_a_ok(dX, K)) {
+      } else if (x_raw_ok(dX, K)) {
         float* xlo = static_cast<float*>(c->xlo[slot].p);
         rc = !w_split ? split_xw_f32(dX, K, rows, dW, N, K, N, nullptr, xlo, dWhi, dWlo, c->s_comp)
                       : split_x_lo_f32(dX, K, rows, K, xlo, c->s_comp);
@@ -1269,7 +1245,7 @@ int b200_dense_f32_chain(const float* X, int64_t ldx, const float* Xlo, const fl
                          void* stream) {
   int rc = validate_dense(X, ldx, W, ldw, Y, ldy, M, N, K, act);
   if (rc) return rc;
-  if (Xlo && (!fused_a_ok(X, ldx) || (reinterpret_cast<uintptr_t>(Xlo) & 15) != 0))
+  if (Xlo && (!x_raw_ok(X, ldx) || (reinterpret_cast<uintptr_t>(Xlo) & 15) != 0))
     return fail(kErrInvalidArg, "a pre-split X needs 16-byte aligned X and Xlo rows");
   if (Ylo && ldylo < N) return fail(kErrInvalidArg, "Ylo pitch < N");
   if (Ylo && K == 0) return fail(kErrInvalidArg, "Ylo needs K > 0");
@@ -1397,10 +1373,9 @@ int b200_dense_f32_wsplit(const float* X, int64_t ldx, const float* whiT, const 
     return rc ? fail(rc, std::string("launch failed: ") + launch_error_text()) : succeed();
   }
   const int splits = choose_splits(M, N, K);
-  const bool fused = fuse_a(X, ldx);
   // Scratch: [X hi | X lo] (separate split pass) then the split-K partials.
   const int64_t Kp = split_pitch(K);
-  const int64_t xsplit = fused ? 0 : 2 * round_up(M * Kp * 4, 256);
+  const int64_t xsplit = 2 * round_up(M * Kp * 4, 256);
   void* ws = nullptr;
   ScratchLease lease;  // held until the kernels that use ws are queued
   {
@@ -1409,10 +1384,7 @@ int b200_dense_f32_wsplit(const float* X, int64_t ldx, const float* whiT, const 
     ws = lease.p;
   }
   float* part = reinterpret_cast<float*>(static_cast<char*>(ws) + xsplit);
-  if (fused) {
-    rc = gemm_tf32x3_fused(X, ldx, whiT, wloT, M, N, K, b, Y, ldy, act, alpha, splits, part,
-                           c->status, st);
-  } else if (fused_a_ok(X, ldx)) {
+  if (x_raw_ok(X, ldx)) {
     float* xlo = reinterpret_cast<float*>(static_cast<char*>(ws) + xsplit / 2);
     rc = split_x_lo_f32(X, ldx, M, K, xlo, st);
     if (rc == kOk)
