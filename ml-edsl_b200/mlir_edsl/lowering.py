@@ -6,7 +6,7 @@ bias_add + relu (cpp/src/MLIRLowering.cpp:355-434). The b200 target
 recognises the same op chains directly on the AST and binds each chain to
 one fused kernel step:
 
-  matmul(A, B)                         -> gemm (f32: 3xTF32 tcgen05; i32: CUDA cores)
+  matmul(A, B)                         -> gemm (f32: 3xTF32 tcgen05; i32: byte-sliced int8 tcgen05)
   matmul(A, B) + b        (either side)  -> gemm with fused bias
   relu / leaky_relu(gemm)                -> gemm with fused activation
   X + b, relu(X + b), relu(X), leaky(X)  -> bias_act (HBM-bound elementwise)
