@@ -216,12 +216,13 @@ def time_oracle_rows(X, W, b, threads, act=1):
     return dt, 2.0 * X.shape[0] * N_DIM * K_DIM, Y
 
 
-def calibrate_rows(target_s, threads, X, W, b):
-    """Row count whose oracle run takes about target_s seconds (multiple of 64)."""
+def calibrate_rows(target_s, threads, X, W, b, cap=None):
+    """Row count (at most `cap`, default X's rows; a multiple of 64) whose
+    oracle run takes about target_s seconds, timed on X's first 64 rows."""
     probe = 64
     dt, _, _ = time_oracle_rows(X[:probe], W, b, threads)
     rows = int(probe * target_s / max(dt, 1e-3))
-    return max(64, min(X.shape[0], rows // 64 * 64))
+    return max(64, min(cap or X.shape[0], rows // 64 * 64))
 
 
 def run_reference(args):
@@ -234,7 +235,7 @@ def run_reference(args):
     per_step = max(1.0, min(8.0, 150.0 / max(1, args.steps + args.warmup)))
     W, b = workload_weights()
     X = workload_rows(0, 64)
-    rows = calibrate_rows(per_step, cores, X, W, b)
+    rows = calibrate_rows(per_step, cores, X, W, b, cap=M_TOTAL)
     X = workload_rows(0, rows)
     for _ in range(args.warmup):
         time_oracle_rows(X, W, b, cores)
